@@ -1,0 +1,405 @@
+#!/usr/bin/env python3
+"""Benchmark of the B200 forward pass (one JSON line on rank 0).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config C5] [--impl b200|reference]
+
+Workload: BASELINE configuration C5 by default (batch 512, seq 1024,
+d_model 256, 8 heads, ffn 1024, 4 layers, causal), the configuration the
+metric's 1/2/4/8-GPU clause is quoted on; the batch is sharded across the N
+ranks (one process per GPU, launched by torchrun for N > 1) with no
+collective in the data path.  A step is one forward of this rank's shard.
+
+  value  device-resident inputs; per step: L2 flush (256 MiB write, untimed),
+         CUDA events around the forward; max over ranks of the summed step
+         times; sequences/s of the whole job.
+  e2e    same metric through the public model call with host buffers: every
+         step copies the input shard from pinned host memory and the FP32
+         output back to pinned host memory inside the timed region.
+  roofline  the dominant kernel's algorithmic FLOPs (or bytes) per launch over
+         its mean event-timed duration inside the timed region, against the
+         measured peak in MEASURED_PEAKS.json.
+  cpu_baseline  (rank 0, N = 1) the FP32 oracle on the host cores, on a
+         bounded sample of sequences of the same workload.
+
+--impl reference times the reference's FP32 CPU path (the oracle
+restatement; the reference itself is Python that cannot be installed on the
+GPU box) on rank 0 only, a bounded sample of sequences per step.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import shutil
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+import torch
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+if ROOT not in sys.path:
+    sys.path.insert(0, ROOT)
+
+# Workload table: (batch, seq, d_model, heads, ffn, layers, causal, padding_ratio)
+WORKLOADS = {
+    "C1": (64, 128, 128, 4, 128, 4, True, 0.0),
+    "C2": (64, 1024, 128, 4, 128, 4, True, 0.0),
+    "C3": (256, 256, 32, 2, 128, 4, True, 0.0),
+    "C4": (16, 2048, 512, 8, 2048, 6, True, 0.5),
+    "C5": (512, 1024, 256, 8, 1024, 4, True, 0.0),
+}
+METRIC = "sequences/sec (forward, FP32 in/out)"
+UNIT = "seq/s"
+SEED = 1234 + 100000  # the reference's timing-input seed (torch_transformer_benchmark.py:747)
+KERNEL_KIND_LABEL = {"attn": "attn_fwd_kernel", "qkv": "gemm_kernel<EPI_QKV>", "out_ln": "gemm_kernel<EPI_RESID_LN>",
+                     "ffn_in": "gemm_kernel<EPI_GELU>", "ffn_out_ln": "gemm_kernel<EPI_RESID_LN>",
+                     "ln0": "layernorm_rows_kernel", "mask": "mask_kv_end_kernel", "ffn_fused": "ffn_fused_kernel"}
+
+
+def parse_args():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--config", default="C5", choices=sorted(WORKLOADS))
+    ap.add_argument("--impl", default="b200", choices=("b200", "reference"))
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-sample-seconds", type=float, default=12.0)
+    return ap.parse_args()
+
+
+def make_inputs(cfg, padding_ratio, seed):
+    """x ~ N(0,1) FP32 [B, S, D] and the prefix key-padding mask, generated on CPU
+    the way the reference's generate_random_case does (torch_transformer_benchmark.py:448-486)."""
+    B, S, D = cfg["batch"], cfg["seq"], cfg["d_model"]
+    g = torch.Generator(device="cpu")
+    g.manual_seed(seed)
+    x = torch.randn(B, S, D, generator=g, dtype=torch.float32)
+    if padding_ratio <= 0:
+        return x, None
+    min_valid = max(1, int(round(S * (1.0 - padding_ratio))))
+    lengths = torch.randint(min_valid, S + 1, (B,), generator=g)
+    mask = torch.arange(S)[None, :] < lengths[:, None]
+    return x.masked_fill(~mask[..., None], 0), mask
+
+
+def algorithmic(cfg, batch):
+    """Per-layer algorithmic FLOPs and HBM bytes of each kernel kind for `batch` sequences.
+
+    attention: FLOPs 2*B*S^2*D causal (4*B*S^2*D full), bytes 8ND (Q, K, V read, ctx written, FP16)
+    qkv:       FLOPs 6ND^2, bytes 8ND + 6D^2
+    out_ln:    FLOPs 2ND^2, bytes 12ND + 2D^2 (ctx FP16 in, residual FP32 in/out, normalized FP16 out)
+    ffn (split): ffn_in FLOPs 2NDF, bytes 2ND + 2NF + 2DF; ffn_out_ln FLOPs 2NDF, bytes 2NF + 10ND + 2DF
+    """
+    S, D, F = cfg["seq"], cfg["d_model"], cfg["ffn"]
+    N = batch * S
+    attn_flops = (2.0 if cfg["causal"] else 4.0) * batch * S * S * D
+    return {
+        "attn": (attn_flops, 8.0 * N * D),
+        "qkv": (6.0 * N * D * D, 8.0 * N * D + 6.0 * D * D),
+        "out_ln": (2.0 * N * D * D, 12.0 * N * D + 2.0 * D * D),
+        "ffn_in": (2.0 * N * D * F, 2.0 * N * D + 2.0 * N * F + 2.0 * D * F),
+        "ffn_out_ln": (2.0 * N * D * F, 2.0 * N * F + 10.0 * N * D + 2.0 * D * F),
+        "ln0": (0.0, 6.0 * N * D),
+    }
+
+
+def load_peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), float(p["bf16_tflops"]), "measured"
+    except Exception:
+        return 6650.0, 1590.0, "fallback"
+
+
+def load_traffic(workload, per_gpu_batch, kind):
+    """DRAM bytes per launch of (workload, kernel kind) from the committed ncu summary, or None.
+
+    The summary records bytes for a capture at `captured_batch` sequences per
+    launch; traffic grows in proportion to the sequences a launch processes.
+    """
+    path = os.path.join(ROOT, "profiles", "traffic.json")
+    try:
+        with open(path) as f:
+            ent = json.load(f).get(f"{workload}/{kind}")
+        if ent is None:
+            return None
+        return float(ent["bytes_per_launch"]) * per_gpu_batch / float(ent["captured_batch"])
+    except Exception:
+        return None
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled every 200 ms while running."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self):
+        self.proc = None
+        self.path = None
+
+    def start(self):
+        exe = shutil.which("nvidia-smi")
+        if exe is None:
+            return
+        fd, self.path = tempfile.mkstemp(suffix=".csv")
+        os.close(fd)
+        self.out = open(self.path, "w")
+        self.proc = subprocess.Popen([exe, f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                                      "-lms", "200"], stdout=self.out, stderr=subprocess.DEVNULL)
+
+    def stop(self, gpu_indices):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self.out.close()
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        with open(self.path) as f:
+            for line in f:
+                parts = [p.strip() for p in line.split(",")]
+                if len(parts) < 9 or not parts[0].isdigit() or int(parts[0]) not in gpu_indices:
+                    continue
+                try:
+                    sm.append(float(parts[1]))
+                    mx = float(parts[2])
+                except ValueError:
+                    continue
+                for n, v in zip(names, parts[5:9]):
+                    if v.lower() == "active":
+                        reasons.add(n)
+        os.unlink(self.path)
+        if not sm:
+            return None
+        loaded = [v for v in sm if v > 0.5 * (mx or max(sm))] or sm
+        return {"sm_mhz": statistics.median(loaded), "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def cpu_baseline(cfg, padding_ratio, budget_s):
+    """FP32 oracle on the host cores over a bounded sample of sequences: (seq/s, cores, sample)."""
+    import oracle  # the CPU baseline leg is the one place bench.py uses the oracle
+
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    ocfg = oracle.Config(1, cfg["seq"], cfg["d_model"], cfg["heads"], cfg["ffn"], cfg["layers"], cfg["causal"])
+    sd = oracle.seeded_state_dict(ocfg, 1234)
+    big = oracle.Config(cfg["batch"], cfg["seq"], cfg["d_model"], cfg["heads"], cfg["ffn"], cfg["layers"],
+                        cfg["causal"])
+    x, mask = make_inputs(cfg, padding_ratio, SEED)
+    with torch.inference_mode():
+        t0 = time.perf_counter()
+        oracle.forward(sd, big, x[:1], None if mask is None else mask[:1])  # warm-up + size probe
+        one = time.perf_counter() - t0
+        n = int(max(1, min(cfg["batch"], budget_s / max(one, 1e-3))))
+        t0 = time.perf_counter()
+        done = 0
+        while done < n:
+            k = min(4, n - done)
+            oracle.forward(sd, big, x[done:done + k], None if mask is None else mask[done:done + k])
+            done += k
+        dt = time.perf_counter() - t0
+    return done / dt, threads, f"{done} of {cfg['batch']} sequences of the workload, batches of <=4, FP32 oracle"
+
+
+def run_reference(args, cfg, padding_ratio, workload_name):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    import oracle
+
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    big = oracle.Config(cfg["batch"], cfg["seq"], cfg["d_model"], cfg["heads"], cfg["ffn"], cfg["layers"],
+                        cfg["causal"])
+    sd = oracle.seeded_state_dict(big, 1234)
+    x, mask = make_inputs(cfg, padding_ratio, SEED)
+    per_step = min(4, cfg["batch"])
+    times = []
+    with torch.inference_mode():
+        for i in range(args.warmup + args.steps):
+            s = (i * per_step) % max(1, cfg["batch"] - per_step + 1)
+            t0 = time.perf_counter()
+            oracle.forward(sd, big, x[s:s + per_step], None if mask is None else mask[s:s + per_step])
+            dt = time.perf_counter() - t0
+            if i >= args.warmup:
+                times.append(dt)
+    total = sum(times)
+    value = per_step * len(times) / total
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000.0 * total / len(times),
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": workload_name, "sample_per_step": per_step, **cfg},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port",
+                         "sample": f"{per_step} sequences per step of the {workload_name} workload, FP32 oracle "
+                                   "restatement of BaselineTransformer on CPU"},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def main() -> int:
+    args = parse_args()
+    B, S, D, H, F, L, causal, pad = WORKLOADS[args.config]
+    cfg = {"batch": B, "seq": S, "d_model": D, "heads": H, "ffn": F, "layers": L, "causal": causal}
+    workload_name = args.config
+    if args.impl == "reference":
+        return run_reference(args, cfg, pad, workload_name)
+
+    import torch.distributed as dist
+
+    from tiktoktechjam2026_b200 import B200Transformer, TransformerConfig, _lib
+    from tiktoktechjam2026_b200.sharding import shard_bounds
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    if world > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=300),
+                                device_id=dev)
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local_rank])
+        torch.cuda.synchronize(dev)
+
+    def max_over_ranks(v):
+        if world == 1:
+            return v
+        t = torch.tensor([v], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    s0, s1 = shard_bounds(B, world, rank)
+    nb = s1 - s0
+    torch.manual_seed(1234)
+    model = B200Transformer(TransformerConfig(nb, S, D, H, F, L, causal)).to(dev).eval()
+    model.convert_projections_to_fp16()
+    model.assume_all_tokens_valid = pad <= 0
+    x_full, mask_full = make_inputs(cfg, pad, SEED)
+    x_host = x_full[s0:s1].contiguous().pin_memory()
+    mask_host = None if mask_full is None else mask_full[s0:s1].contiguous().pin_memory()
+    del x_full, mask_full
+    out_host = torch.empty_like(x_host).pin_memory()
+    x_dev = x_host.to(dev)
+    mask_dev = None if mask_host is None else mask_host.to(dev)
+    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)
+    stream = torch.cuda.current_stream(dev)
+
+    with torch.inference_mode():
+        for _ in range(max(3, args.warmup)):
+            model(x_dev, mask_dev)
+        barrier()
+
+        # ---------------- value: device-resident inputs ----------------
+        model.set_profiling(True, dev)
+        model.profile_collect(dev)
+        starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+        ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+        sampler = ClockSampler() if rank == 0 else None
+        if sampler:
+            sampler.start()
+        launches0 = _lib.lib().tt_launch_count()
+        barrier()
+        for i in range(args.steps):
+            flush.zero_()
+            starts[i].record(stream)
+            model(x_dev, mask_dev)
+            ends[i].record(stream)
+        barrier()
+        launches = _lib.lib().tt_launch_count() - launches0
+        step_ms = [a.elapsed_time(b) for a, b in zip(starts, ends)]
+        prof = model.profile_collect(dev)
+        model.set_profiling(False, dev)
+        total_ms = max_over_ranks(sum(step_ms))
+
+        # ---------------- e2e: host buffers through the public call ----------------
+        model(x_host.to(dev, non_blocking=True), None if mask_host is None else mask_host.to(dev, non_blocking=True))
+        barrier()
+        e_start = torch.cuda.Event(enable_timing=True)
+        e_end = torch.cuda.Event(enable_timing=True)
+        barrier()
+        e_start.record(stream)
+        for _ in range(args.steps):
+            xd = x_host.to(dev, non_blocking=True)
+            md = None if mask_host is None else mask_host.to(dev, non_blocking=True)
+            y = model(xd, md)
+            out_host.copy_(y, non_blocking=True)
+        e_end.record(stream)
+        barrier()
+        clocks = sampler.stop(list(range(world))) if sampler else None
+        e2e_ms = max_over_ranks(e_start.elapsed_time(e_end))
+
+    # ---------------- roofline of the dominant kernel ----------------
+    hbm_peak, tc_peak, peak_src = load_peaks()
+    dominant = max(((k, v) for k, v in prof.items() if v[1] > 0), key=lambda kv: kv[1][0])
+    kind, (kms, kcount) = dominant
+    per_launch_s = kms / kcount / 1e3
+    flops, nbytes = algorithmic(cfg, nb)[kind]
+    t_tc = flops / (tc_peak * 1e12)
+    t_hbm = nbytes / (hbm_peak * 1e9)
+    if t_tc >= t_hbm:
+        roof = {"bound": "tensor", "achieved": flops / per_launch_s / 1e12, "peak": tc_peak, "unit": "TFLOP/s"}
+    else:
+        roof = {"bound": "hbm", "achieved": nbytes / per_launch_s / 1e9, "peak": hbm_peak, "unit": "GB/s"}
+    roof["frac"] = roof["achieved"] / roof["peak"]
+    roof["traffic"] = load_traffic(workload_name, nb, kind)
+    roof["kernel"] = KERNEL_KIND_LABEL.get(kind, kind)
+    roof["mean_launch_us"] = per_launch_s * 1e6
+    roof["algorithmic_per_launch"] = {"flops": flops, "bytes": nbytes}
+    roof["peak_source"] = f"{peak_src} ({'bf16_tflops burst' if roof['bound'] == 'tensor' else 'hbm_gbs'})"
+    roof["share_of_step"] = kms / max(sum(step_ms), 1e-9)
+
+    if rank == 0:
+        ms_per_step = total_ms / args.steps
+        value = B * 1000.0 / ms_per_step
+        e2e_value = B * 1000.0 / (e2e_ms / args.steps)
+        line = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "f16 tensor-core operands, f32 accumulate/softmax/LayerNorm/residual",
+            "data": "synthetic (x ~ N(0,1) FP32 from the reference's timing seed; seeded default-init weights)",
+            "config": {"workload": f"{workload_name}: batch {B}, seq {S}, d_model {D}, heads {H}, ffn {F}, "
+                                   f"layers {L}, causal{', key padding' if pad > 0 else ''}",
+                       "global_batch": B, "per_gpu_batch": nb, "seq_len": S, "d_model": D, "heads": H, "ffn": F,
+                       "layers": L, "parallelism": f"batch-sharded x{world}, no collective in the data path",
+                       "l2": "flushed between timed steps (256 MiB write, untimed)"},
+            "e2e": {"value": e2e_value, "unit": UNIT,
+                    "h2d_bytes_per_step": x_host.numel() * 4 + (0 if mask_host is None else mask_host.numel()),
+                    "d2h_bytes_per_step": out_host.numel() * 4},
+            "gpu_launches": int(launches),
+            "roofline": roof,
+            "kernel_ms_per_step": {k: v[0] / args.steps for k, v in prof.items() if v[1] > 0},
+            "clocks": clocks,
+        }
+        if world == 1 and not args.no_cpu_baseline:
+            v, cores, sample = cpu_baseline(cfg, pad, args.cpu_sample_seconds)
+            line["cpu_baseline"] = {"value": v, "unit": UNIT, "cores": cores, "kind": "port", "sample": sample}
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    raise SystemExit(main())

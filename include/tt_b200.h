@@ -1,0 +1,192 @@
+/*
+ * tt_b200.h -- C ABI of libtt_b200.so, the B200 (sm_100a) forward pass of the
+ * TikTokTechJam2026 causal Transformer encoder.
+ *
+ * Conventions
+ *   - Every pointer argument is a DEVICE pointer owned by the caller, except
+ *     where a comment says "host".  FP16 tensors are passed as void*.
+ *   - Every compute entry point takes the CUDA stream to launch on (as void*,
+ *     a cudaStream_t; NULL = legacy default stream), launches asynchronously
+ *     and returns a status code.  No entry point allocates device memory, and
+ *     none traps or exits: failures are status codes, plus a device error word
+ *     that bounded in-kernel waits set on timeout (see tt_device_error).
+ *   - Kernels run on the calling thread's current CUDA device.
+ *
+ * Each entry point cites the reference interface it replaces
+ * (neil0618/TikTokTechJam2026, path:line).
+ */
+#ifndef TT_B200_H_
+#define TT_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes ------------------------------------------------------- */
+#define TT_OK 0
+#define TT_ERR_SHAPE 1       /* unsupported or inconsistent sizes                */
+#define TT_ERR_ALIGN 2       /* pointer or stride alignment violates TMA rules   */
+#define TT_ERR_UNSUPPORTED 3 /* shape outside the dispatch table's coverage      */
+#define TT_ERR_LAUNCH 4      /* CUDA launch / runtime error                      */
+#define TT_ERR_TIMEOUT 5     /* a bounded in-kernel wait gave up                 */
+#define TT_ERR_ARG 6         /* null or invalid argument                         */
+#define TT_ERR_WORKSPACE 7   /* workspace too small                              */
+
+/* Version of this ABI (bumped on any signature change). */
+int tt_abi_version(void);
+
+/* Last error message of the calling thread (host string, never NULL). */
+const char* tt_last_error(void);
+
+/* Synchronizes the current device, then reads its device error word into
+ * *word (host) and clears it when `clear` is nonzero.  Returns TT_ERR_TIMEOUT
+ * when the word records a timed-out wait, TT_OK when it is zero. */
+int tt_device_error(unsigned int* word, int clear);
+
+/* Per-wait limit, in nanoseconds, of every bounded in-kernel wait launched
+ * after this call (default 2 s). */
+void tt_set_wait_timeout_ns(unsigned long long ns);
+
+/* Number of kernels this library has launched in this process. */
+unsigned long long tt_launch_count(void);
+
+/* Launches a kernel whose only wait can never be satisfied and must time out
+ * after `timeout_ns`; returns TT_ERR_TIMEOUT when the watchdog fired as
+ * designed (synchronizes the stream; clears the error word afterwards). */
+int tt_watchdog_selftest(unsigned long long timeout_ns, void* stream);
+
+/* ---- single ops ----------------------------------------------------------- */
+
+/* out[r, :] = LayerNorm(x[r, :]) * gamma + beta over d features, FP32 math,
+ * out FP16 (out_is_f16 = 1) or FP32.  Requires d % 32 == 0, d <= 1024.
+ * Replaces `layers[0].norm1(x)` + cast (mixed_precision/transformer.py:489-491)
+ * and the row LayerNorm of fused_add_layer_norm
+ * (torch_transformer_benchmark.py:37-103). */
+int tt_layernorm_rows(const float* x, const float* gamma, const float* beta, void* out,
+                      int64_t n_rows, int d, float eps, int out_is_f16, void* stream);
+
+/* kv_end[b] = 1 + index of the last nonzero byte of mask[b, :] (0 if none).
+ * Host-side helper of the key-padding path; the reference builds the
+ * equivalent [B,1,1,S] attention mask (mixed_precision/transformer.py:144-148). */
+int tt_mask_kv_end(const uint8_t* mask, int batch, int seq, int* kv_end, void* stream);
+
+/* Packed QKV projection: qkv = normalized[N, D] (FP16) . w_qkv[3D, D]^T (FP16)
+ * + b_qkv (FP32), FP32 accumulation, stored FP16 head-major:
+ *   q, k : [batch, heads, seq, head_dim]
+ *   vt   : [batch, heads, head_dim, seq_pad]   (V transposed; seq_pad >= seq,
+ *          seq_pad % 8 == 0; columns >= seq are left untouched)
+ * Replaces mixed_linear on qkv_proj (mixed_precision/triton_linear.py:221-269,
+ * called at mixed_precision/transformer.py:93-143). */
+int tt_qkv_projection(const void* normalized, const void* w_qkv, const float* b_qkv, void* q,
+                      void* k, void* vt, int batch, int seq, int d_model, int heads, int seq_pad,
+                      void* stream);
+
+/* ctx[b, s, h*hd:(h+1)*hd] = softmax(q k^T * scale + causal + key mask) v,
+ * FP16 operands, FP32 softmax statistics and accumulation, FP16 output.
+ * key_mask: [batch, seq] bytes (nonzero = valid) or NULL; kv_end must then hold
+ * tt_mask_kv_end's output.  head_dim in {16, 32, 64}.
+ * Replaces fp16_causal_attention / causal_attention
+ * (custom_kernel/triton_attention.py:126-232, 264-390) and the SDPA route
+ * (mixed_precision/transformer.py:157-198). */
+int tt_causal_attention(const void* q, const void* k, const void* vt, const uint8_t* key_mask,
+                        const int* kv_end, void* ctx, int batch, int seq, int heads, int head_dim,
+                        int seq_pad, float scale, int causal, void* stream);
+
+/* resid_out = a[N, k_in] (FP16) . w[d_model, k_in]^T + bias + resid_in (FP32);
+ * norm_out = LayerNorm(resid_out) * gamma + beta (FP16 or FP32); rows whose
+ * row_mask byte is 0 get norm_out = 0 (row_mask may be NULL).  d_model <= 256
+ * or 512; in-place (resid_out == resid_in) is allowed.
+ * Replaces mixed_linear_add_layer_norm (mixed_precision/triton_linear.py:72-125,
+ * 272-324) and, with k_in = ffn, the FFN-out + fused_add_layer_norm tail of
+ * the generic route (mixed_precision/transformer.py:675-695). */
+int tt_linear_residual_layernorm(const void* a, const void* w, const float* bias,
+                                 const float* resid_in, const float* gamma, const float* beta,
+                                 float* resid_out, void* norm_out, int64_t n_rows, int k_in,
+                                 int d_model, float eps, int norm_out_is_f16,
+                                 const uint8_t* row_mask, void* stream);
+
+/* out[N, n_out] = GELU_erf(a[N, k_in] . w[n_out, k_in]^T + bias), FP16 out.
+ * Replaces mixed_linear(..., fuse_gelu=True) (mixed_precision/triton_linear.py:
+ * 16-69) and ffn_in + F.gelu of the generic route (transformer.py:669-674). */
+int tt_linear_gelu(const void* a, const void* w, const float* bias, void* out, int64_t n_rows,
+                   int k_in, int n_out, void* stream);
+
+/* Writes a one-line description of the route and tile configuration the
+ * shape-dispatch table selects for (d_model, heads, seq, ffn) into buf
+ * (host).  Returns TT_OK, or TT_ERR_UNSUPPORTED for shapes outside it. */
+int tt_route_describe(int d_model, int heads, int seq, int ffn, char* buf, int buflen);
+
+/* ---- whole model ----------------------------------------------------------- */
+
+/* Per-layer parameters (device pointers).  Linear weights are FP16 [out, in]
+ * (nn.Linear layout), biases and LayerNorm parameters FP32. */
+typedef struct tt_layer_weights {
+  const void* w_qkv;        /* [3D, D]  cat(Wq, Wk, Wv)                 */
+  const float* b_qkv;       /* [3D]                                      */
+  const void* w_out;        /* [D, D]                                    */
+  const float* b_out;       /* [D]                                       */
+  const float* ln_attn_w;   /* norm2 of this layer                       */
+  const float* ln_attn_b;
+  const void* w_ffn_in;     /* [F, D]                                    */
+  const float* b_ffn_in;    /* [F]                                       */
+  const void* w_ffn_out;    /* [D, F]                                    */
+  const float* b_ffn_out;   /* [D]                                       */
+  const float* ln_next_w;   /* norm1 of the next layer, or final_norm    */
+  const float* ln_next_b;
+} tt_layer_weights;
+
+typedef struct tt_model_desc {
+  int d_model, heads, ffn_dim, num_layers, causal;
+  float eps;
+  const float* ln0_w; /* norm1 of layer 0 */
+  const float* ln0_b;
+  const tt_layer_weights* layers; /* host array of num_layers entries */
+} tt_model_desc;
+
+typedef struct tt_model tt_model;
+
+/* Creates a model handle bound to the current device; weights are referenced,
+ * not copied, and must outlive the handle.  The handle is not thread-safe.
+ * Replaces MixedPrecisionTransformer.__init__ + convert_projections_to_fp16
+ * (mixed_precision/transformer.py:330-478). */
+int tt_model_create(const tt_model_desc* desc, tt_model** out);
+void tt_model_destroy(tt_model* model);
+
+/* Workspace bytes tt_model_forward needs for (batch, seq). */
+int tt_model_workspace_bytes(const tt_model* model, int batch, int seq, size_t* bytes);
+
+/* out[B, S, D] (FP32) = the model applied to x[B, S, D] (FP32).  mask: [B, S]
+ * bytes (nonzero = valid token) or NULL; with a mask, padded output rows are
+ * exactly zero.  x and out must not overlap the workspace.
+ * Replaces MixedPrecisionTransformer.forward (mixed_precision/transformer.py:480-699). */
+int tt_model_forward(tt_model* model, const float* x, const uint8_t* mask, float* out, int batch,
+                     int seq, void* workspace, size_t workspace_bytes, void* stream);
+
+/* Kernel kinds reported by tt_model_profile_collect. */
+#define TT_KERNEL_LN0 0
+#define TT_KERNEL_MASK 1
+#define TT_KERNEL_QKV 2
+#define TT_KERNEL_ATTN 3
+#define TT_KERNEL_OUT_LN 4
+#define TT_KERNEL_FFN_IN 5
+#define TT_KERNEL_FFN_OUT_LN 6
+#define TT_KERNEL_FFN_FUSED 7
+#define TT_KERNEL_KINDS 8
+
+/* When enabled, every launch of tt_model_forward is bracketed by CUDA events
+ * on the launch stream. */
+int tt_model_set_profiling(tt_model* model, int enable);
+
+/* Synchronizes the recorded events and writes, per kernel kind, the summed
+ * device milliseconds (ms) and launch counts (counts) since the last collect
+ * (host arrays of n entries). */
+int tt_model_profile_collect(tt_model* model, float* ms, int* counts, int n);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* TT_B200_H_ */

@@ -1,0 +1,166 @@
+"""Per-kernel parity of libtt_b200 against plain PyTorch FP32 math of the same op.
+
+Operands are rounded to FP16 exactly as the kernels consume them, so the only
+differences left are accumulation order, FP32 transcendental rounding and the
+FP16 rounding of FP16 outputs.  Tolerances are stated per test.
+"""
+
+import math
+
+import pytest
+import torch
+import torch.nn.functional as F
+
+from tiktoktechjam2026_b200 import ops
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda:0"
+
+
+def _gen(seed):
+    g = torch.Generator(device="cpu")
+    g.manual_seed(seed)
+    return g
+
+
+@pytest.mark.parametrize("d", [32, 64, 96, 128, 256, 512])
+@pytest.mark.parametrize("n", [1, 7, 1000])
+@pytest.mark.parametrize("out_dtype", [torch.float16, torch.float32])
+def test_layernorm_rows(tt_lib, d, n, out_dtype):
+    g = _gen(d * 31 + n)
+    x = (torch.randn(n, d, generator=g) * 3 + 0.5).to(DEV)
+    w = torch.randn(d, generator=g).to(DEV)
+    b = torch.randn(d, generator=g).to(DEV)
+    out = ops.layernorm_rows(x, w, b, 1e-5, out_dtype)
+    ref = F.layer_norm(x, (d,), w, b, 1e-5)
+    tol = 4e-3 if out_dtype == torch.float16 else 2e-5  # FP16 output rounding (|y| < 8)
+    torch.testing.assert_close(out.float(), ref, rtol=tol, atol=tol)
+
+
+QKV_SHAPES = [(2, 16, 32, 2), (3, 130, 128, 4), (1, 256, 256, 8), (2, 64, 512, 8), (64, 128, 128, 4)]
+
+
+@pytest.mark.parametrize("B,S,D,H", QKV_SHAPES)
+def test_qkv_projection(tt_lib, B, S, D, H):
+    g = _gen(B * S + D)
+    n = torch.randn(B, S, D, generator=g).half().to(DEV)
+    w = (torch.randn(3 * D, D, generator=g) / math.sqrt(D)).half().to(DEV)
+    b = (torch.randn(3 * D, generator=g) * 0.1).to(DEV)
+    q, k, vt = ops.qkv_projection(n, w, b, H)
+    ref = (n.float() @ w.float().t() + b).view(B, S, 3, H, D // H).permute(2, 0, 3, 1, 4)
+    # FP16 output rounding of |x| < 8 values: 4e-3
+    torch.testing.assert_close(q.float(), ref[0], rtol=2e-3, atol=4e-3)
+    torch.testing.assert_close(k.float(), ref[1], rtol=2e-3, atol=4e-3)
+    torch.testing.assert_close(vt[..., :S].float(), ref[2].transpose(-1, -2), rtol=2e-3, atol=4e-3)
+
+
+def _attn_ref(q, k, vt, scale, causal, mask):
+    B, H, S, hd = q.shape
+    v = vt[..., :S].transpose(-1, -2).float()
+    s = (q.float() @ k.float().transpose(-1, -2)) * scale
+    if causal:
+        s = s.masked_fill(torch.ones(S, S, dtype=torch.bool, device=q.device).triu(1), float("-inf"))
+    if mask is not None:
+        s = s.masked_fill(~mask[:, None, None, :], float("-inf"))
+    p = torch.softmax(s, dim=-1)
+    p = torch.nan_to_num(p, nan=0.0)  # rows with no valid key are defined as 0
+    return (p @ v).transpose(1, 2).reshape(B, S, H * hd)
+
+
+ATTN_SHAPES = [
+    (2, 2, 16, 16), (1, 4, 130, 32), (2, 2, 256, 64), (1, 8, 1024, 32), (3, 1, 200, 16), (1, 2, 384, 64),
+]
+
+
+@pytest.mark.parametrize("B,H,S,hd", ATTN_SHAPES)
+@pytest.mark.parametrize("causal", [True, False])
+@pytest.mark.parametrize("mask_kind", [None, "prefix", "random"])
+def test_attention(tt_lib, B, H, S, hd, causal, mask_kind):
+    g = _gen(B * 1000 + S + hd)
+    q = torch.randn(B, H, S, hd, generator=g).half().to(DEV)
+    k = torch.randn(B, H, S, hd, generator=g).half().to(DEV)
+    sp = ops.seq_pad_of(S)
+    vt = torch.zeros(B, H, hd, sp, dtype=torch.float16)
+    vt[..., :S] = torch.randn(B, H, hd, S, generator=g).half()
+    vt = vt.to(DEV)
+    mask = None
+    if mask_kind == "prefix":
+        lengths = torch.randint(max(1, S // 2), S + 1, (B,), generator=g)
+        mask = (torch.arange(S)[None, :] < lengths[:, None]).to(DEV)
+    elif mask_kind == "random":
+        mask = (torch.rand(B, S, generator=g) > 0.3).to(DEV)
+        mask[:, 0] = True
+    scale = hd**-0.5
+    out = ops.attention(q, k, vt, scale, causal, mask)
+    ref = _attn_ref(q, k, vt, scale, causal, mask)
+    if mask is not None:
+        # Query rows whose causal window holds no valid key are defined as zero.
+        cm = torch.ones(S, S, dtype=torch.bool, device=DEV).tril() if causal else torch.ones(S, S, dtype=torch.bool, device=DEV)
+        seen = (cm[None] & mask[:, None, :]).any(-1)  # [B, S]
+        ref = ref.masked_fill(~seen[..., None], 0)
+    # P is rounded to FP16 before P.V (as in the reference kernel); |ctx| <= max|v| < 5
+    torch.testing.assert_close(out.float(), ref, rtol=5e-3, atol=5e-3)
+
+
+def test_attention_fully_padded_tile_is_zero(tt_lib):
+    B, H, S, hd = 2, 2, 512, 32
+    g = _gen(9)
+    q = torch.randn(B, H, S, hd, generator=g).half().to(DEV)
+    k = torch.randn(B, H, S, hd, generator=g).half().to(DEV)
+    vt = torch.randn(B, H, hd, S, generator=g).half().to(DEV)
+    mask = torch.zeros(B, S, dtype=torch.bool, device=DEV)
+    mask[0, :100] = True
+    mask[1, :300] = True
+    out = ops.attention(q, k, vt, hd**-0.5, True, mask)
+    assert torch.all(out[0, 128:] == 0) and torch.all(out[1, 384:] == 0)
+    ref = _attn_ref(q, k, vt, hd**-0.5, True, mask)
+    torch.testing.assert_close(out[0, :100].float(), ref[0, :100], rtol=5e-3, atol=5e-3)
+    torch.testing.assert_close(out[1, :300].float(), ref[1, :300], rtol=5e-3, atol=5e-3)
+
+
+LIN_LN_SHAPES = [(1000, 128, 128), (300, 32, 32), (513, 256, 256), (257, 512, 512), (200, 2048, 512),
+                 (129, 1024, 256), (4096, 128, 128)]
+
+
+@pytest.mark.parametrize("N,K,D", LIN_LN_SHAPES)
+@pytest.mark.parametrize("norm_dtype", [torch.float16, torch.float32])
+def test_linear_residual_layernorm(tt_lib, N, K, D, norm_dtype):
+    g = _gen(N + K + D)
+    a = torch.randn(N, K, generator=g).half().to(DEV)
+    w = (torch.randn(D, K, generator=g) / math.sqrt(K)).half().to(DEV)
+    b = (torch.randn(D, generator=g) * 0.1).to(DEV)
+    r = torch.randn(N, D, generator=g).to(DEV)
+    gw = (1 + 0.1 * torch.randn(D, generator=g)).to(DEV)
+    gb = (0.1 * torch.randn(D, generator=g)).to(DEV)
+    mask = (torch.rand(N, generator=g) > 0.2).to(DEV)
+    resid, norm = ops.linear_residual_layernorm(a, w, b, r, gw, gb, 1e-5, norm_dtype, mask)
+    ref_r = r + a.float() @ w.float().t() + b
+    ref_n = F.layer_norm(ref_r, (D,), gw, gb, 1e-5).masked_fill(~mask[:, None], 0)
+    torch.testing.assert_close(resid, ref_r, rtol=1e-5, atol=2e-5)
+    tol = 4e-3 if norm_dtype == torch.float16 else 5e-5
+    torch.testing.assert_close(norm.float(), ref_n, rtol=tol, atol=tol)
+
+
+@pytest.mark.parametrize("N,K,Fo", [(1000, 128, 128), (300, 32, 128), (257, 512, 2048), (129, 256, 1024)])
+def test_linear_gelu(tt_lib, N, K, Fo):
+    g = _gen(N * 3 + K + Fo)
+    a = torch.randn(N, K, generator=g).half().to(DEV)
+    w = (torch.randn(Fo, K, generator=g) / math.sqrt(K)).half().to(DEV)
+    b = (torch.randn(Fo, generator=g) * 0.1).to(DEV)
+    out = ops.linear_gelu(a, w, b)
+    ref = F.gelu(a.float() @ w.float().t() + b, approximate="none")
+    torch.testing.assert_close(out.float(), ref, rtol=2e-3, atol=4e-3)
+
+
+def test_watchdog_times_out_cleanly_and_context_survives(tt_lib):
+    from tiktoktechjam2026_b200 import _lib
+
+    stream = torch.cuda.current_stream(DEV).cuda_stream
+    rc = tt_lib.tt_watchdog_selftest(20_000_000, stream)  # 20 ms limit
+    assert rc == _lib.TT_ERR_TIMEOUT, _lib.last_error()
+    # error word was cleared; the context still runs kernels correctly
+    word = __import__("ctypes").c_uint(0)
+    assert tt_lib.tt_device_error(__import__("ctypes").byref(word), 1) == _lib.TT_OK
+    x = torch.randn(64, 128, device=DEV)
+    out = ops.layernorm_rows(x, torch.ones(128, device=DEV), torch.zeros(128, device=DEV), 1e-5, torch.float32)
+    torch.testing.assert_close(out, F.layer_norm(x, (128,)), rtol=2e-5, atol=2e-5)

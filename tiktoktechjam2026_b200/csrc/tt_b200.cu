@@ -1,0 +1,922 @@
+// libtt_b200.so: host side of the C ABI declared in include/tt_b200.h.
+//
+// Holds the tensor-map encoding (driver entry point fetched at run time, so
+// the library does not link libcuda), the shape-dispatch table, the
+// whole-model forward launcher and its optional per-launch event profiling.
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <cudaTypedefs.h>
+
+#include <atomic>
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <vector>
+
+#include "tt_attention.cuh"
+#include "tt_gemm.cuh"
+#include "tt_misc.cuh"
+#include "../../include/tt_b200.h"
+
+namespace tt {
+
+__device__ unsigned int g_err_word;
+
+namespace {
+
+constexpr int kAbiVersion = 1;
+constexpr int kMaxDevices = 64;
+constexpr int kSmemBudget = 200 * 1024;
+
+thread_local char g_last_error[512] = "";
+std::atomic<unsigned long long> g_launches{0};
+std::atomic<unsigned long long> g_timeout_ns{2000000000ull};
+
+int fail(int code, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_last_error, sizeof(g_last_error), fmt, ap);
+  va_end(ap);
+  return code;
+}
+
+int check_cuda(cudaError_t e, const char* what) {
+  if (e == cudaSuccess) return TT_OK;
+  return fail(TT_ERR_LAUNCH, "%s: %s", what, cudaGetErrorString(e));
+}
+
+// ---------------------------------------------------------------- per device
+struct DeviceState {
+  std::once_flag once;
+  int status = TT_OK;
+  unsigned int* err = nullptr;  // device address of g_err_word
+  int sm_count = 0;
+};
+DeviceState g_dev[kMaxDevices];
+
+PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+std::once_flag g_encode_once;
+
+int current_device_state(DeviceState** out) {
+  int dev = 0;
+  if (int rc = check_cuda(cudaGetDevice(&dev), "cudaGetDevice")) return rc;
+  if (dev < 0 || dev >= kMaxDevices) return fail(TT_ERR_ARG, "device ordinal %d out of range", dev);
+  DeviceState& st = g_dev[dev];
+  std::call_once(st.once, [&] {
+    void* p = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&p, g_err_word);
+    if (e != cudaSuccess) {
+      st.status = fail(TT_ERR_LAUNCH, "cudaGetSymbolAddress(error word): %s", cudaGetErrorString(e));
+      return;
+    }
+    st.err = static_cast<unsigned int*>(p);
+    e = cudaDeviceGetAttribute(&st.sm_count, cudaDevAttrMultiProcessorCount, dev);
+    if (e != cudaSuccess) {
+      st.status = fail(TT_ERR_LAUNCH, "cudaDeviceGetAttribute: %s", cudaGetErrorString(e));
+      return;
+    }
+    int major = 0, minor = 0;
+    cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
+    cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev);
+    if (major != 10 || minor != 0) {
+      st.status = fail(TT_ERR_UNSUPPORTED,
+                       "libtt_b200 is built for sm_100a (B200); device %d is sm_%d%d", dev, major,
+                       minor);
+      return;
+    }
+    st.status = TT_OK;
+  });
+  if (st.status != TT_OK) return st.status;
+  *out = &st;
+  return TT_OK;
+}
+
+int get_encoder() {
+  std::call_once(g_encode_once, [] {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+  });
+  if (!g_encode) return fail(TT_ERR_LAUNCH, "cuTensorMapEncodeTiled entry point not available");
+  return TT_OK;
+}
+
+CUtensorMapSwizzle swizzle_for_bytes(int inner_bytes) {
+  return inner_bytes == 128   ? CU_TENSOR_MAP_SWIZZLE_128B
+         : inner_bytes == 64  ? CU_TENSOR_MAP_SWIZZLE_64B
+         : inner_bytes == 32  ? CU_TENSOR_MAP_SWIZZLE_32B
+                              : CU_TENSOR_MAP_SWIZZLE_NONE;
+}
+
+// FP16 tensor map of rank 2 or 3 (dims innermost first, byte strides of dims 1..).
+int encode_f16(CUtensorMap* tm, const void* base, int rank, const uint64_t* dims,
+               const uint64_t* strides_bytes, const uint32_t* box) {
+  if (int rc = get_encoder()) return rc;
+  if (reinterpret_cast<uintptr_t>(base) % 16 != 0)
+    return fail(TT_ERR_ALIGN, "tensor base %p is not 16-byte aligned", base);
+  for (int i = 0; i < rank - 1; ++i)
+    if (strides_bytes[i] % 16 != 0)
+      return fail(TT_ERR_ALIGN, "tensor stride %llu is not a multiple of 16 bytes",
+                  static_cast<unsigned long long>(strides_bytes[i]));
+  cuuint32_t elem_strides[3] = {1, 1, 1};
+  const CUresult r = g_encode(
+      tm, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, static_cast<cuuint32_t>(rank), const_cast<void*>(base),
+      reinterpret_cast<const cuuint64_t*>(dims), reinterpret_cast<const cuuint64_t*>(strides_bytes),
+      reinterpret_cast<const cuuint32_t*>(box), elem_strides, CU_TENSOR_MAP_INTERLEAVE_NONE,
+      swizzle_for_bytes(static_cast<int>(box[0]) * 2), CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+      CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(TT_ERR_LAUNCH, "cuTensorMapEncodeTiled failed (%d)", int(r));
+  return TT_OK;
+}
+
+// Row-major [rows, cols] FP16 matrix, box {box_cols, box_rows}.
+int encode_matrix(CUtensorMap* tm, const void* base, uint64_t rows, uint64_t cols, int box_cols,
+                  int box_rows) {
+  const uint64_t dims[2] = {cols, rows};
+  const uint64_t strides[1] = {cols * 2};
+  const uint32_t box[2] = {static_cast<uint32_t>(box_cols), static_cast<uint32_t>(box_rows)};
+  return encode_f16(tm, base, 2, dims, strides, box);
+}
+
+template <typename K>
+int prepare_kernel(K kernel, int smem_bytes) {
+  return check_cuda(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         smem_bytes),
+                    "cudaFuncSetAttribute");
+}
+
+int after_launch(const char* what) {
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return fail(TT_ERR_LAUNCH, "%s launch: %s", what, cudaGetErrorString(e));
+  g_launches.fetch_add(1, std::memory_order_relaxed);
+  return TT_OK;
+}
+
+// ---------------------------------------------------------------- dispatch
+// Shape-dispatch table keyed on (d_model, heads, seq, ffn): tile widths and
+// pipeline depths for every kernel of one layer.  Shapes not listed use the
+// generic rule in choose_route().
+struct Route {
+  const char* name;
+  int qkv_bn, qkv_nst;
+  int out_nst;
+  int ffn_in_bn, ffn_in_nst;
+  int ffn_out_nst;
+};
+
+struct RouteEntry {
+  int d_model, heads, seq, ffn;
+  Route route;
+};
+
+const RouteEntry kRouteTable[] = {
+    // C1  B64 S128  D128 H4 F128
+    {128, 4, 128, 128, {"d128-h4-s128", 128, 2, 2, 128, 2, 2}},
+    // C2  B64 S1024 D128 H4 F128
+    {128, 4, 1024, 128, {"d128-h4-s1024", 128, 2, 2, 128, 2, 2}},
+    // C3  B256 S256 D32 H2 F128
+    {32, 2, 256, 128, {"d32-h2-s256", 96, 1, 1, 128, 1, 4}},
+    // C4  B16 S2048 D512 H8 F2048 (+ key padding)
+    {512, 8, 2048, 2048, {"d512-h8-s2048", 256, 4, 2, 256, 4, 2}},
+    // C5  B512 S1024 D256 H8 F1024
+    {256, 8, 1024, 1024, {"d256-h8-s1024", 256, 2, 2, 256, 2, 3}},
+};
+
+int largest_bn_dividing(int n, int cap) {
+  for (int bn = cap; bn >= 32; bn -= 32)
+    if (n % bn == 0) return bn;
+  return 0;
+}
+
+int clamp_nst(int ksw, int bn, int k, int want) {
+  const int nk = k / ksw;
+  int nst = want < nk ? want : nk;
+  while (nst > 1 && gemm_smem_bytes(ksw, bn, nst) > kSmemBudget) --nst;
+  return nst < 1 ? 1 : nst;
+}
+
+int check_model_shape(int d_model, int heads, int ffn) {
+  if (d_model <= 0 || heads <= 0 || ffn <= 0 || d_model % heads != 0)
+    return fail(TT_ERR_SHAPE, "invalid (d_model=%d, heads=%d, ffn=%d)", d_model, heads, ffn);
+  const int hd = d_model / heads;
+  if (hd != 16 && hd != 32 && hd != 64)
+    return fail(TT_ERR_UNSUPPORTED, "head_dim %d not in {16, 32, 64}", hd);
+  if (d_model % 32 != 0 || d_model > 512 || (d_model > 256 && d_model != 512))
+    return fail(TT_ERR_UNSUPPORTED, "d_model %d must be a multiple of 32, <= 256, or 512", d_model);
+  if (ffn % 32 != 0) return fail(TT_ERR_UNSUPPORTED, "ffn %d must be a multiple of 32", ffn);
+  return TT_OK;
+}
+
+int choose_route(int d_model, int heads, int seq, int ffn, Route* out) {
+  if (int rc = check_model_shape(d_model, heads, ffn)) return rc;
+  for (const RouteEntry& e : kRouteTable) {
+    if (e.d_model == d_model && e.heads == heads && e.seq == seq && e.ffn == ffn) {
+      *out = e.route;
+      return TT_OK;
+    }
+  }
+  Route r;
+  r.name = "generic";
+  r.qkv_bn = largest_bn_dividing(3 * d_model, 256);
+  r.qkv_nst = 4;
+  r.out_nst = 4;
+  r.ffn_in_bn = largest_bn_dividing(ffn, 256);
+  r.ffn_in_nst = 4;
+  r.ffn_out_nst = 4;
+  if (r.qkv_bn == 0 || r.ffn_in_bn == 0)
+    return fail(TT_ERR_UNSUPPORTED, "no column split for d_model=%d ffn=%d", d_model, ffn);
+  *out = r;
+  return TT_OK;
+}
+
+int ksw_for(int k) { return (k % 64 == 0) ? 64 : 32; }
+
+// ---------------------------------------------------------------- launchers
+template <int KSW, int EPI>
+int launch_gemm_t(const CUtensorMap& tmA, const CUtensorMap& tmW, const GemmParams& p,
+                  cudaStream_t stream) {
+  const int smem = gemm_smem_bytes(KSW, p.bn, p.nst);
+  auto kern = gemm_kernel<KSW, EPI>;
+  if (int rc = prepare_kernel(kern, smem)) return rc;
+  const long long m_tiles = (static_cast<long long>(p.M) + 127) / 128;
+  const long long grid = m_tiles * p.n_splits;
+  if (grid > 0x7fffffffLL) return fail(TT_ERR_SHAPE, "grid too large");
+  kern<<<static_cast<unsigned>(grid), 192, smem, stream>>>(tmA, tmW, p);
+  return after_launch("gemm");
+}
+
+int launch_gemm(int ksw, int epi, const CUtensorMap& tmA, const CUtensorMap& tmW,
+                const GemmParams& p, cudaStream_t stream) {
+  if (ksw == 64) {
+    if (epi == EPI_QKV) return launch_gemm_t<64, EPI_QKV>(tmA, tmW, p, stream);
+    if (epi == EPI_RESID_LN) return launch_gemm_t<64, EPI_RESID_LN>(tmA, tmW, p, stream);
+    return launch_gemm_t<64, EPI_GELU>(tmA, tmW, p, stream);
+  }
+  if (epi == EPI_QKV) return launch_gemm_t<32, EPI_QKV>(tmA, tmW, p, stream);
+  if (epi == EPI_RESID_LN) return launch_gemm_t<32, EPI_RESID_LN>(tmA, tmW, p, stream);
+  return launch_gemm_t<32, EPI_GELU>(tmA, tmW, p, stream);
+}
+
+GemmParams base_params(DeviceState* ds) {
+  GemmParams p;
+  memset(&p, 0, sizeof(p));
+  p.err = ds->err;
+  p.timeout_ns = g_timeout_ns.load();
+  return p;
+}
+
+int run_layernorm(const float* x, const float* gamma, const float* beta, void* out,
+                  long long n_rows, int d, float eps, int out_f16, cudaStream_t stream) {
+  if (n_rows <= 0) return TT_OK;
+  const unsigned grid = static_cast<unsigned>((n_rows + 7) / 8);
+  switch (d / 32) {
+#define TT_LN_CASE(V)                                                                  \
+  case V:                                                                              \
+    layernorm_rows_kernel<V><<<grid, 256, 0, stream>>>(x, gamma, beta, out, n_rows, eps, \
+                                                       out_f16);                       \
+    break;
+    TT_LN_CASE(1)
+    TT_LN_CASE(2)
+    TT_LN_CASE(3)
+    TT_LN_CASE(4)
+    TT_LN_CASE(8)
+    TT_LN_CASE(12)
+    TT_LN_CASE(16)
+    TT_LN_CASE(32)
+#undef TT_LN_CASE
+    default:
+      return fail(TT_ERR_UNSUPPORTED, "layernorm width %d not supported", d);
+  }
+  return after_launch("layernorm");
+}
+
+int check_ln_width(int d) {
+  const int v = d / 32;
+  if (d % 32 != 0 || !(v == 1 || v == 2 || v == 3 || v == 4 || v == 8 || v == 12 || v == 16 ||
+                       v == 32))
+    return fail(TT_ERR_UNSUPPORTED, "layernorm width %d not supported", d);
+  return TT_OK;
+}
+
+// Q/K/V^T tensor maps for attention over a [B*H, S, hd] / [B*H, hd, S_pad] layout.
+int encode_attention_maps(CUtensorMap* tq, CUtensorMap* tk, CUtensorMap* tv, const void* q,
+                          const void* k, const void* vt, int bh, int seq, int hd, int seq_pad) {
+  {
+    const uint64_t dims[3] = {static_cast<uint64_t>(hd), static_cast<uint64_t>(seq),
+                              static_cast<uint64_t>(bh)};
+    const uint64_t strides[2] = {static_cast<uint64_t>(hd) * 2,
+                                 static_cast<uint64_t>(hd) * seq * 2};
+    const uint32_t box[3] = {static_cast<uint32_t>(hd), 128, 1};
+    if (int rc = encode_f16(tq, q, 3, dims, strides, box)) return rc;
+    if (int rc = encode_f16(tk, k, 3, dims, strides, box)) return rc;
+  }
+  {
+    const uint64_t dims[3] = {static_cast<uint64_t>(seq_pad), static_cast<uint64_t>(hd),
+                              static_cast<uint64_t>(bh)};
+    const uint64_t strides[2] = {static_cast<uint64_t>(seq_pad) * 2,
+                                 static_cast<uint64_t>(seq_pad) * hd * 2};
+    const uint32_t box[3] = {64, static_cast<uint32_t>(hd), 1};
+    if (int rc = encode_f16(tv, vt, 3, dims, strides, box)) return rc;
+  }
+  return TT_OK;
+}
+
+int launch_attention(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
+                     const AttnParams& ap, int hd, cudaStream_t stream) {
+  const int n_qt = (ap.seq + 127) / 128;
+  if (n_qt > 65535) return fail(TT_ERR_SHAPE, "seq %d too long", ap.seq);
+  const long long bh = static_cast<long long>(ap.batch) * ap.heads;
+  if (bh > 0x7fffffffLL) return fail(TT_ERR_SHAPE, "batch*heads too large");
+  dim3 grid(static_cast<unsigned>(bh), static_cast<unsigned>(n_qt));
+  switch (hd) {
+#define TT_ATTN_CASE(HD)                                                          \
+  case HD: {                                                                      \
+    auto kern = attn_fwd_kernel<HD>;                                              \
+    if (int rc = prepare_kernel(kern, AttnLayout<HD>::SMEM_ALLOC)) return rc;     \
+    kern<<<grid, 192, AttnLayout<HD>::SMEM_ALLOC, stream>>>(tq, tk, tv, ap);      \
+    break;                                                                        \
+  }
+    TT_ATTN_CASE(16)
+    TT_ATTN_CASE(32)
+    TT_ATTN_CASE(64)
+#undef TT_ATTN_CASE
+    default:
+      return fail(TT_ERR_UNSUPPORTED, "head_dim %d not in {16, 32, 64}", hd);
+  }
+  return after_launch("attention");
+}
+
+}  // namespace
+}  // namespace tt
+
+using namespace tt;
+
+// =========================================================================
+// Whole model
+// =========================================================================
+struct tt_model {
+  int device = -1;
+  int D = 0, H = 0, F = 0, L = 0, causal = 1;
+  float eps = 1e-5f;
+  const float* ln0_w = nullptr;
+  const float* ln0_b = nullptr;
+  std::vector<tt_layer_weights> layers;
+  // Per-layer weight tensor maps.
+  std::vector<CUtensorMap> tm_wqkv, tm_wout, tm_win, tm_wout2;
+  // Route + bound workspace (re-encoded when shape or workspace change).
+  Route route{};
+  int route_seq = -1;
+  int bound_batch = -1, bound_seq = -1;
+  void* bound_ws = nullptr;
+  CUtensorMap tm_norm{}, tm_ctx{}, tm_hidden{}, tm_q{}, tm_k{}, tm_vt{};
+  // Profiling.
+  bool profiling = false;
+  struct Rec {
+    int kind;
+    cudaEvent_t a, b;
+  };
+  std::vector<Rec> recs;
+  std::vector<cudaEvent_t> pool;
+};
+
+namespace {
+
+struct WsLayout {
+  size_t resid, norm, q, k, vt, ctx, hidden, kv_end, total;
+  int seq_pad;
+};
+
+size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+WsLayout ws_layout(const tt_model* m, int batch, int seq) {
+  WsLayout w;
+  const size_t N = static_cast<size_t>(batch) * seq;
+  const int hd = m->D / m->H;
+  w.seq_pad = (seq + 7) / 8 * 8;
+  size_t off = 0;
+  auto take = [&](size_t bytes) {
+    const size_t o = off;
+    off = align_up(off + bytes, 1024);
+    return o;
+  };
+  w.resid = take(N * m->D * 4);
+  w.norm = take(N * m->D * 2);
+  w.q = take(N * m->D * 2);
+  w.k = take(N * m->D * 2);
+  w.vt = take(static_cast<size_t>(batch) * m->H * hd * w.seq_pad * 2);
+  w.ctx = take(N * m->D * 2);
+  w.hidden = take(N * m->F * 2);
+  w.kv_end = take(static_cast<size_t>(batch) * 4);
+  w.total = off;
+  return w;
+}
+
+int record_begin(tt_model* m, cudaStream_t s, cudaEvent_t* ev) {
+  if (!m->profiling) return TT_OK;
+  if (m->pool.empty()) {
+    cudaEvent_t e;
+    if (int rc = check_cuda(cudaEventCreate(&e), "cudaEventCreate")) return rc;
+    m->pool.push_back(e);
+  }
+  *ev = m->pool.back();
+  m->pool.pop_back();
+  return check_cuda(cudaEventRecord(*ev, s), "cudaEventRecord");
+}
+
+int record_end(tt_model* m, cudaStream_t s, int kind, cudaEvent_t start) {
+  if (!m->profiling) return TT_OK;
+  if (m->pool.empty()) {
+    cudaEvent_t e;
+    if (int rc = check_cuda(cudaEventCreate(&e), "cudaEventCreate")) return rc;
+    m->pool.push_back(e);
+  }
+  cudaEvent_t end = m->pool.back();
+  m->pool.pop_back();
+  m->recs.push_back({kind, start, end});
+  return check_cuda(cudaEventRecord(end, s), "cudaEventRecord");
+}
+
+int bind_workspace(tt_model* m, int batch, int seq, void* ws, cudaStream_t stream) {
+  if (m->route_seq != seq) {
+    if (int rc = choose_route(m->D, m->H, seq, m->F, &m->route)) return rc;
+    m->route_seq = seq;
+    // Weight maps depend on the route's column tiles.
+    const int ksw_d = ksw_for(m->D), ksw_f = ksw_for(m->F);
+    m->tm_wqkv.resize(m->L);
+    m->tm_wout.resize(m->L);
+    m->tm_win.resize(m->L);
+    m->tm_wout2.resize(m->L);
+    const int out_box = m->D > 256 ? 256 : m->D;
+    for (int l = 0; l < m->L; ++l) {
+      const tt_layer_weights& w = m->layers[l];
+      if (int rc = encode_matrix(&m->tm_wqkv[l], w.w_qkv, 3 * m->D, m->D, ksw_d, m->route.qkv_bn))
+        return rc;
+      if (int rc = encode_matrix(&m->tm_wout[l], w.w_out, m->D, m->D, ksw_d, out_box)) return rc;
+      if (int rc = encode_matrix(&m->tm_win[l], w.w_ffn_in, m->F, m->D, ksw_d, m->route.ffn_in_bn))
+        return rc;
+      if (int rc = encode_matrix(&m->tm_wout2[l], w.w_ffn_out, m->D, m->F, ksw_f, out_box))
+        return rc;
+    }
+    m->bound_ws = nullptr;
+  }
+  if (m->bound_ws == ws && m->bound_batch == batch && m->bound_seq == seq) return TT_OK;
+  const WsLayout w = ws_layout(m, batch, seq);
+  uint8_t* base = static_cast<uint8_t*>(ws);
+  const uint64_t N = static_cast<uint64_t>(batch) * seq;
+  const int hd = m->D / m->H;
+  const int ksw_d = ksw_for(m->D), ksw_f = ksw_for(m->F);
+  if (int rc = encode_matrix(&m->tm_norm, base + w.norm, N, m->D, ksw_d, 128)) return rc;
+  if (int rc = encode_matrix(&m->tm_ctx, base + w.ctx, N, m->D, ksw_d, 128)) return rc;
+  if (int rc = encode_matrix(&m->tm_hidden, base + w.hidden, N, m->F, ksw_f, 128)) return rc;
+  if (int rc = encode_attention_maps(&m->tm_q, &m->tm_k, &m->tm_vt, base + w.q, base + w.k,
+                                     base + w.vt, batch * m->H, seq, hd, w.seq_pad))
+    return rc;
+  // V^T columns in [seq, seq_pad) are never written by the projection; they
+  // must hold finite values because masked probabilities (0) multiply them.
+  if (w.seq_pad != seq)
+    if (int rc = check_cuda(cudaMemsetAsync(base + w.vt, 0,
+                                            static_cast<size_t>(batch) * m->H * hd * w.seq_pad * 2,
+                                            stream),
+                            "cudaMemsetAsync"))
+      return rc;
+  m->bound_ws = ws;
+  m->bound_batch = batch;
+  m->bound_seq = seq;
+  return TT_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int tt_abi_version(void) { return kAbiVersion; }
+
+const char* tt_last_error(void) { return g_last_error; }
+
+void tt_set_wait_timeout_ns(unsigned long long ns) { g_timeout_ns.store(ns ? ns : 1); }
+
+unsigned long long tt_launch_count(void) { return g_launches.load(); }
+
+int tt_device_error(unsigned int* word, int clear) {
+  DeviceState* ds;
+  if (int rc = current_device_state(&ds)) return rc;
+  if (int rc = check_cuda(cudaDeviceSynchronize(), "cudaDeviceSynchronize")) return rc;
+  unsigned int w = 0;
+  if (int rc = check_cuda(cudaMemcpy(&w, ds->err, sizeof(w), cudaMemcpyDeviceToHost), "read error word"))
+    return rc;
+  if (word) *word = w;
+  if (clear && w != 0)
+    if (int rc = check_cuda(cudaMemset(ds->err, 0, sizeof(unsigned int)), "clear error word"))
+      return rc;
+  if (w & kDevErrTimeout)
+    return fail(TT_ERR_TIMEOUT, "a bounded in-kernel wait timed out (site 0x%x)", w & 0xffffu);
+  return TT_OK;
+}
+
+int tt_watchdog_selftest(unsigned long long timeout_ns, void* stream) {
+  DeviceState* ds;
+  if (int rc = current_device_state(&ds)) return rc;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (int rc = check_cuda(cudaStreamSynchronize(s), "cudaStreamSynchronize")) return rc;
+  if (int rc = check_cuda(cudaMemset(ds->err, 0, sizeof(unsigned int)), "clear error word"))
+    return rc;
+  watchdog_selftest_kernel<<<1, 32, 0, s>>>(ds->err, timeout_ns);
+  if (int rc = after_launch("watchdog self-test")) return rc;
+  if (int rc = check_cuda(cudaStreamSynchronize(s), "cudaStreamSynchronize")) return rc;
+  unsigned int w = 0;
+  if (int rc = check_cuda(cudaMemcpy(&w, ds->err, sizeof(w), cudaMemcpyDeviceToHost), "read error word"))
+    return rc;
+  if (int rc = check_cuda(cudaMemset(ds->err, 0, sizeof(unsigned int)), "clear error word"))
+    return rc;
+  if ((w & kDevErrTimeout) && (w & 0xffffu) == 0x7e57u)
+    return fail(TT_ERR_TIMEOUT, "watchdog fired as designed (word 0x%x)", w);
+  return fail(TT_ERR_LAUNCH, "watchdog did not fire (word 0x%x)", w);
+}
+
+int tt_layernorm_rows(const float* x, const float* gamma, const float* beta, void* out,
+                      int64_t n_rows, int d, float eps, int out_is_f16, void* stream) {
+  DeviceState* ds;
+  if (int rc = current_device_state(&ds)) return rc;
+  if (!x || !gamma || !beta || !out || n_rows < 0) return fail(TT_ERR_ARG, "null argument");
+  if (int rc = check_ln_width(d)) return rc;
+  return run_layernorm(x, gamma, beta, out, n_rows, d, eps, out_is_f16,
+                       static_cast<cudaStream_t>(stream));
+}
+
+int tt_mask_kv_end(const uint8_t* mask, int batch, int seq, int* kv_end, void* stream) {
+  DeviceState* ds;
+  if (int rc = current_device_state(&ds)) return rc;
+  if (!mask || !kv_end || batch < 0 || seq <= 0) return fail(TT_ERR_ARG, "invalid argument");
+  if (batch == 0) return TT_OK;
+  mask_kv_end_kernel<<<batch, 256, 0, static_cast<cudaStream_t>(stream)>>>(mask, seq, kv_end);
+  return after_launch("mask_kv_end");
+}
+
+int tt_qkv_projection(const void* normalized, const void* w_qkv, const float* b_qkv, void* q,
+                      void* k, void* vt, int batch, int seq, int d_model, int heads, int seq_pad,
+                      void* stream) {
+  DeviceState* ds;
+  if (int rc = current_device_state(&ds)) return rc;
+  if (!normalized || !w_qkv || !b_qkv || !q || !k || !vt) return fail(TT_ERR_ARG, "null argument");
+  if (batch <= 0 || seq <= 0 || seq_pad < seq || seq_pad % 8 != 0)
+    return fail(TT_ERR_SHAPE, "invalid batch/seq/seq_pad (%d, %d, %d)", batch, seq, seq_pad);
+  if (int rc = check_model_shape(d_model, heads, 32)) return rc;
+  Route r;
+  r.qkv_bn = largest_bn_dividing(3 * d_model, d_model <= 128 ? 128 : 256);
+  r.qkv_nst = 4;
+  const int ksw = ksw_for(d_model);
+  CUtensorMap tmA, tmW;
+  const uint64_t N = static_cast<uint64_t>(batch) * seq;
+  if (int rc = encode_matrix(&tmA, normalized, N, d_model, ksw, 128)) return rc;
+  if (int rc = encode_matrix(&tmW, w_qkv, 3 * d_model, d_model, ksw, r.qkv_bn)) return rc;
+  GemmParams p = base_params(ds);
+  p.M = static_cast<int>(N);
+  p.N_total = 3 * d_model;
+  p.K = d_model;
+  p.bn = r.qkv_bn;
+  p.n_splits = p.N_total / p.bn;
+  p.nst = clamp_nst(ksw, p.bn, p.K, r.qkv_nst);
+  p.bias = b_qkv;
+  p.q = static_cast<__half*>(q);
+  p.k = static_cast<__half*>(k);
+  p.vt = static_cast<__half*>(vt);
+  p.seq = seq;
+  p.heads = heads;
+  p.head_dim = d_model / heads;
+  p.seq_pad = seq_pad;
+  p.d_model = d_model;
+  if (N > 0x7fffffffULL) return fail(TT_ERR_SHAPE, "too many rows");
+  return launch_gemm(ksw, EPI_QKV, tmA, tmW, p, static_cast<cudaStream_t>(stream));
+}
+
+int tt_causal_attention(const void* q, const void* k, const void* vt, const uint8_t* key_mask,
+                        const int* kv_end, void* ctx, int batch, int seq, int heads, int head_dim,
+                        int seq_pad, float scale, int causal, void* stream) {
+  DeviceState* ds;
+  if (int rc = current_device_state(&ds)) return rc;
+  if (!q || !k || !vt || !ctx || (key_mask && !kv_end)) return fail(TT_ERR_ARG, "null argument");
+  if (batch <= 0 || seq <= 0 || heads <= 0 || seq_pad < seq || seq_pad % 8 != 0)
+    return fail(TT_ERR_SHAPE, "invalid sizes");
+  CUtensorMap tq, tk, tv;
+  if (int rc = encode_attention_maps(&tq, &tk, &tv, q, k, vt, batch * heads, seq, head_dim, seq_pad))
+    return rc;
+  AttnParams ap;
+  ap.batch = batch;
+  ap.seq = seq;
+  ap.heads = heads;
+  ap.seq_pad = seq_pad;
+  ap.causal = causal ? 1 : 0;
+  ap.scale_log2 = scale * 1.4426950408889634f;
+  ap.key_mask = key_mask;
+  ap.kv_end = kv_end;
+  ap.ctx = static_cast<__half*>(ctx);
+  ap.err = ds->err;
+  ap.timeout_ns = g_timeout_ns.load();
+  return launch_attention(tq, tk, tv, ap, head_dim, static_cast<cudaStream_t>(stream));
+}
+
+int tt_linear_residual_layernorm(const void* a, const void* w, const float* bias,
+                                 const float* resid_in, const float* gamma, const float* beta,
+                                 float* resid_out, void* norm_out, int64_t n_rows, int k_in,
+                                 int d_model, float eps, int norm_out_is_f16,
+                                 const uint8_t* row_mask, void* stream) {
+  DeviceState* ds;
+  if (int rc = current_device_state(&ds)) return rc;
+  if (!a || !w || !bias || !resid_in || !gamma || !beta || !resid_out || !norm_out)
+    return fail(TT_ERR_ARG, "null argument");
+  if (n_rows <= 0 || n_rows > 0x7fffffffLL || k_in <= 0 || k_in % 32 != 0)
+    return fail(TT_ERR_SHAPE, "invalid n_rows/k_in (%lld, %d)", (long long)n_rows, k_in);
+  if (d_model % 32 != 0 || d_model <= 0 || (d_model > 256 && d_model != 512))
+    return fail(TT_ERR_UNSUPPORTED, "d_model %d must be a multiple of 32, <= 256, or 512", d_model);
+  const int ksw = ksw_for(k_in);
+  CUtensorMap tmA, tmW;
+  if (int rc = encode_matrix(&tmA, a, n_rows, k_in, ksw, 128)) return rc;
+  if (int rc = encode_matrix(&tmW, w, d_model, k_in, ksw, d_model > 256 ? 256 : d_model)) return rc;
+  GemmParams p = base_params(ds);
+  p.M = static_cast<int>(n_rows);
+  p.N_total = d_model;
+  p.K = k_in;
+  p.bn = d_model;
+  p.n_splits = 1;
+  p.nst = clamp_nst(ksw, p.bn, p.K, 4);
+  p.bias = bias;
+  p.resid_in = resid_in;
+  p.resid_out = resid_out;
+  p.gamma = gamma;
+  p.beta = beta;
+  p.norm_out = norm_out;
+  p.norm_f16 = norm_out_is_f16 ? 1 : 0;
+  p.eps = eps;
+  p.row_mask = row_mask;
+  return launch_gemm(ksw, EPI_RESID_LN, tmA, tmW, p, static_cast<cudaStream_t>(stream));
+}
+
+int tt_linear_gelu(const void* a, const void* w, const float* bias, void* out, int64_t n_rows,
+                   int k_in, int n_out, void* stream) {
+  DeviceState* ds;
+  if (int rc = current_device_state(&ds)) return rc;
+  if (!a || !w || !bias || !out) return fail(TT_ERR_ARG, "null argument");
+  if (n_rows <= 0 || n_rows > 0x7fffffffLL || k_in <= 0 || k_in % 32 != 0 || n_out % 32 != 0)
+    return fail(TT_ERR_SHAPE, "invalid sizes");
+  const int bn = largest_bn_dividing(n_out, 256);
+  if (bn == 0) return fail(TT_ERR_UNSUPPORTED, "n_out %d", n_out);
+  const int ksw = ksw_for(k_in);
+  CUtensorMap tmA, tmW;
+  if (int rc = encode_matrix(&tmA, a, n_rows, k_in, ksw, 128)) return rc;
+  if (int rc = encode_matrix(&tmW, w, n_out, k_in, ksw, bn)) return rc;
+  GemmParams p = base_params(ds);
+  p.M = static_cast<int>(n_rows);
+  p.N_total = n_out;
+  p.K = k_in;
+  p.bn = bn;
+  p.n_splits = n_out / bn;
+  p.nst = clamp_nst(ksw, bn, k_in, 4);
+  p.bias = bias;
+  p.act_out = static_cast<__half*>(out);
+  return launch_gemm(ksw, EPI_GELU, tmA, tmW, p, static_cast<cudaStream_t>(stream));
+}
+
+int tt_route_describe(int d_model, int heads, int seq, int ffn, char* buf, int buflen) {
+  Route r;
+  if (int rc = choose_route(d_model, heads, seq, ffn, &r)) return rc;
+  if (buf && buflen > 0)
+    snprintf(buf, buflen,
+             "route=%s qkv_bn=%d qkv_nst=%d out_nst=%d ffn=split ffn_in_bn=%d ffn_in_nst=%d "
+             "ffn_out_nst=%d attn_tile=128x128",
+             r.name, r.qkv_bn, r.qkv_nst, r.out_nst, r.ffn_in_bn, r.ffn_in_nst, r.ffn_out_nst);
+  return TT_OK;
+}
+
+int tt_model_create(const tt_model_desc* desc, tt_model** out) {
+  if (!desc || !out || !desc->layers || !desc->ln0_w || !desc->ln0_b)
+    return fail(TT_ERR_ARG, "null argument");
+  *out = nullptr;
+  DeviceState* ds;
+  if (int rc = current_device_state(&ds)) return rc;
+  if (int rc = check_model_shape(desc->d_model, desc->heads, desc->ffn_dim)) return rc;
+  if (int rc = check_ln_width(desc->d_model)) return rc;
+  if (desc->num_layers <= 0) return fail(TT_ERR_SHAPE, "num_layers must be positive");
+  for (int l = 0; l < desc->num_layers; ++l) {
+    const tt_layer_weights& w = desc->layers[l];
+    if (!w.w_qkv || !w.b_qkv || !w.w_out || !w.b_out || !w.ln_attn_w || !w.ln_attn_b ||
+        !w.w_ffn_in || !w.b_ffn_in || !w.w_ffn_out || !w.b_ffn_out || !w.ln_next_w || !w.ln_next_b)
+      return fail(TT_ERR_ARG, "layer %d has a null parameter", l);
+  }
+  tt_model* m = new tt_model();
+  cudaGetDevice(&m->device);
+  m->D = desc->d_model;
+  m->H = desc->heads;
+  m->F = desc->ffn_dim;
+  m->L = desc->num_layers;
+  m->causal = desc->causal ? 1 : 0;
+  m->eps = desc->eps;
+  m->ln0_w = desc->ln0_w;
+  m->ln0_b = desc->ln0_b;
+  m->layers.assign(desc->layers, desc->layers + desc->num_layers);
+  *out = m;
+  return TT_OK;
+}
+
+void tt_model_destroy(tt_model* m) {
+  if (!m) return;
+  for (auto& r : m->recs) {
+    cudaEventDestroy(r.a);
+    cudaEventDestroy(r.b);
+  }
+  for (auto e : m->pool) cudaEventDestroy(e);
+  delete m;
+}
+
+int tt_model_workspace_bytes(const tt_model* m, int batch, int seq, size_t* bytes) {
+  if (!m || !bytes) return fail(TT_ERR_ARG, "null argument");
+  if (batch <= 0 || seq <= 0) return fail(TT_ERR_SHAPE, "invalid batch/seq");
+  *bytes = ws_layout(m, batch, seq).total;
+  return TT_OK;
+}
+
+int tt_model_forward(tt_model* m, const float* x, const uint8_t* mask, float* out, int batch,
+                     int seq, void* workspace, size_t workspace_bytes, void* stream) {
+  if (!m || !x || !out || !workspace) return fail(TT_ERR_ARG, "null argument");
+  DeviceState* ds;
+  if (int rc = current_device_state(&ds)) return rc;
+  int dev = -1;
+  cudaGetDevice(&dev);
+  if (dev != m->device)
+    return fail(TT_ERR_ARG, "model was created on device %d but device %d is current", m->device, dev);
+  if (batch <= 0 || seq <= 0) return fail(TT_ERR_SHAPE, "invalid batch/seq (%d, %d)", batch, seq);
+  const long long Nll = static_cast<long long>(batch) * seq;
+  if (Nll > 0x7fffffffLL) return fail(TT_ERR_SHAPE, "batch*seq too large");
+  const WsLayout w = ws_layout(m, batch, seq);
+  if (workspace_bytes < w.total)
+    return fail(TT_ERR_WORKSPACE, "workspace %zu < required %zu bytes", workspace_bytes, w.total);
+  if (reinterpret_cast<uintptr_t>(workspace) % 1024 != 0)
+    return fail(TT_ERR_ALIGN, "workspace must be 1024-byte aligned");
+  if (reinterpret_cast<uintptr_t>(x) % 16 != 0 || reinterpret_cast<uintptr_t>(out) % 16 != 0)
+    return fail(TT_ERR_ALIGN, "x and out must be 16-byte aligned");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (int rc = bind_workspace(m, batch, seq, workspace, s)) return rc;
+  const Route& r = m->route;
+  uint8_t* base = static_cast<uint8_t*>(workspace);
+  float* resid = reinterpret_cast<float*>(base + w.resid);
+  __half* norm = reinterpret_cast<__half*>(base + w.norm);
+  __half* qb = reinterpret_cast<__half*>(base + w.q);
+  __half* kb = reinterpret_cast<__half*>(base + w.k);
+  __half* vtb = reinterpret_cast<__half*>(base + w.vt);
+  __half* ctx = reinterpret_cast<__half*>(base + w.ctx);
+  __half* hidden = reinterpret_cast<__half*>(base + w.hidden);
+  int* kv_end = reinterpret_cast<int*>(base + w.kv_end);
+  const int N = static_cast<int>(Nll);
+  const int D = m->D, F = m->F, H = m->H, hd = D / H;
+  const int ksw_d = ksw_for(D), ksw_f = ksw_for(F);
+  cudaEvent_t ev = nullptr;
+
+  if (mask) {
+    if (int rc = record_begin(m, s, &ev)) return rc;
+    mask_kv_end_kernel<<<batch, 256, 0, s>>>(mask, seq, kv_end);
+    if (int rc = after_launch("mask_kv_end")) return rc;
+    if (int rc = record_end(m, s, TT_KERNEL_MASK, ev)) return rc;
+  }
+  if (int rc = record_begin(m, s, &ev)) return rc;
+  if (int rc = run_layernorm(x, m->ln0_w, m->ln0_b, norm, N, D, m->eps, 1, s)) return rc;
+  if (int rc = record_end(m, s, TT_KERNEL_LN0, ev)) return rc;
+
+  AttnParams ap;
+  ap.batch = batch;
+  ap.seq = seq;
+  ap.heads = H;
+  ap.seq_pad = w.seq_pad;
+  ap.causal = m->causal;
+  ap.scale_log2 = static_cast<float>(1.0 / std::sqrt(static_cast<double>(hd)) * 1.4426950408889634);
+  ap.key_mask = mask;
+  ap.kv_end = mask ? kv_end : nullptr;
+  ap.ctx = ctx;
+  ap.err = ds->err;
+  ap.timeout_ns = g_timeout_ns.load();
+
+  for (int l = 0; l < m->L; ++l) {
+    const tt_layer_weights& lw = m->layers[l];
+    const bool last = (l == m->L - 1);
+    // QKV projection
+    {
+      GemmParams p = base_params(ds);
+      p.M = N;
+      p.N_total = 3 * D;
+      p.K = D;
+      p.bn = r.qkv_bn;
+      p.n_splits = p.N_total / p.bn;
+      p.nst = clamp_nst(ksw_d, p.bn, D, r.qkv_nst);
+      p.bias = lw.b_qkv;
+      p.q = qb;
+      p.k = kb;
+      p.vt = vtb;
+      p.seq = seq;
+      p.heads = H;
+      p.head_dim = hd;
+      p.seq_pad = w.seq_pad;
+      p.d_model = D;
+      if (int rc = record_begin(m, s, &ev)) return rc;
+      if (int rc = launch_gemm(ksw_d, EPI_QKV, m->tm_norm, m->tm_wqkv[l], p, s)) return rc;
+      if (int rc = record_end(m, s, TT_KERNEL_QKV, ev)) return rc;
+    }
+    // Attention
+    if (int rc = record_begin(m, s, &ev)) return rc;
+    if (int rc = launch_attention(m->tm_q, m->tm_k, m->tm_vt, ap, hd, s)) return rc;
+    if (int rc = record_end(m, s, TT_KERNEL_ATTN, ev)) return rc;
+    // Output projection + residual + norm2
+    {
+      GemmParams p = base_params(ds);
+      p.M = N;
+      p.N_total = D;
+      p.K = D;
+      p.bn = D;
+      p.n_splits = 1;
+      p.nst = clamp_nst(ksw_d, D, D, r.out_nst);
+      p.bias = lw.b_out;
+      p.resid_in = (l == 0) ? x : resid;
+      p.resid_out = resid;
+      p.gamma = lw.ln_attn_w;
+      p.beta = lw.ln_attn_b;
+      p.norm_out = norm;
+      p.norm_f16 = 1;
+      p.eps = m->eps;
+      p.row_mask = nullptr;
+      if (int rc = record_begin(m, s, &ev)) return rc;
+      if (int rc = launch_gemm(ksw_d, EPI_RESID_LN, m->tm_ctx, m->tm_wout[l], p, s)) return rc;
+      if (int rc = record_end(m, s, TT_KERNEL_OUT_LN, ev)) return rc;
+    }
+    // FFN in + GELU
+    {
+      GemmParams p = base_params(ds);
+      p.M = N;
+      p.N_total = F;
+      p.K = D;
+      p.bn = r.ffn_in_bn;
+      p.n_splits = F / p.bn;
+      p.nst = clamp_nst(ksw_d, p.bn, D, r.ffn_in_nst);
+      p.bias = lw.b_ffn_in;
+      p.act_out = hidden;
+      if (int rc = record_begin(m, s, &ev)) return rc;
+      if (int rc = launch_gemm(ksw_d, EPI_GELU, m->tm_norm, m->tm_win[l], p, s)) return rc;
+      if (int rc = record_end(m, s, TT_KERNEL_FFN_IN, ev)) return rc;
+    }
+    // FFN out + residual + next norm (final_norm -> FP32 model output on the last layer)
+    {
+      GemmParams p = base_params(ds);
+      p.M = N;
+      p.N_total = D;
+      p.K = F;
+      p.bn = D;
+      p.n_splits = 1;
+      p.nst = clamp_nst(ksw_f, D, F, r.ffn_out_nst);
+      p.bias = lw.b_ffn_out;
+      p.resid_in = resid;
+      p.resid_out = resid;
+      p.gamma = lw.ln_next_w;
+      p.beta = lw.ln_next_b;
+      p.norm_out = last ? static_cast<void*>(out) : static_cast<void*>(norm);
+      p.norm_f16 = last ? 0 : 1;
+      p.eps = m->eps;
+      p.row_mask = last ? mask : nullptr;
+      if (int rc = record_begin(m, s, &ev)) return rc;
+      if (int rc = launch_gemm(ksw_f, EPI_RESID_LN, m->tm_hidden, m->tm_wout2[l], p, s)) return rc;
+      if (int rc = record_end(m, s, TT_KERNEL_FFN_OUT_LN, ev)) return rc;
+    }
+  }
+  return TT_OK;
+}
+
+int tt_model_set_profiling(tt_model* m, int enable) {
+  if (!m) return fail(TT_ERR_ARG, "null model");
+  m->profiling = enable != 0;
+  return TT_OK;
+}
+
+int tt_model_profile_collect(tt_model* m, float* ms, int* counts, int n) {
+  if (!m || !ms || !counts || n <= 0) return fail(TT_ERR_ARG, "invalid argument");
+  for (int i = 0; i < n; ++i) {
+    ms[i] = 0.f;
+    counts[i] = 0;
+  }
+  int rc_all = TT_OK;
+  for (auto& r : m->recs) {
+    if (rc_all == TT_OK) {
+      if (int rc = check_cuda(cudaEventSynchronize(r.b), "cudaEventSynchronize")) rc_all = rc;
+    }
+    float t = 0.f;
+    if (rc_all == TT_OK && cudaEventElapsedTime(&t, r.a, r.b) == cudaSuccess && r.kind < n) {
+      ms[r.kind] += t;
+      counts[r.kind] += 1;
+    }
+    m->pool.push_back(r.a);
+    m->pool.push_back(r.b);
+  }
+  m->recs.clear();
+  return rc_all;
+}
+
+}  // extern "C"

@@ -1,0 +1,336 @@
+"""B200 drop-in for the reference's ``MixedPrecisionTransformer``.
+
+Same constructor arguments, module tree, parameter names and shapes as
+mixed_precision/transformer.py:327-699, so ``copy_mixed_model_weights`` loads
+into it with ``strict=True`` and ``mixed_precision_benchmark.py`` can use it
+unchanged apart from the import.  ``forward`` makes one call into
+libtt_b200.so (``tt_model_forward``), which launches the hand-written sm_100a
+kernels for every op of every layer; there is no PyTorch, Triton or CPU
+compute path behind it.
+"""
+
+from __future__ import annotations
+
+import copy
+import ctypes
+from dataclasses import dataclass
+from typing import Dict, Optional
+
+import torch
+import torch.nn as nn
+
+from . import _lib
+
+
+@dataclass(frozen=True)
+class TransformerConfig:
+    """Field-for-field the reference's TransformerConfig (torch_transformer_benchmark.py:106-133)."""
+
+    batch_size: int
+    seq_len: int
+    d_model: int
+    num_heads: int
+    ffn_dim: int
+    num_layers: int
+    causal: bool
+
+    def validate(self) -> None:
+        for name in ("batch_size", "seq_len", "d_model", "num_heads", "ffn_dim", "num_layers"):
+            if getattr(self, name) <= 0:
+                raise ValueError(f"{name} must be positive")
+        if self.d_model % self.num_heads != 0:
+            raise ValueError(
+                f"d_model ({self.d_model}) must be divisible by num_heads ({self.num_heads})"
+            )
+
+
+class MixedPrecisionSelfAttention(nn.Module):
+    """Parameter holder matching mixed_precision/transformer.py:35-66 (qkv_proj, out_proj)."""
+
+    def __init__(self, d_model: int, num_heads: int) -> None:
+        super().__init__()
+        self.d_model = d_model
+        self.num_heads = num_heads
+        self.head_dim = d_model // num_heads
+        self.scale = self.head_dim**-0.5
+        self.qkv_proj = nn.Linear(d_model, 3 * d_model, bias=True)
+        self.out_proj = nn.Linear(d_model, d_model, bias=True)
+
+    def convert_projections_to_fp16(self) -> None:
+        self.qkv_proj.half()
+        self.out_proj.half()
+
+
+class MixedPrecisionTransformerBlock(nn.Module):
+    """Parameter holder matching mixed_precision/transformer.py:281-324."""
+
+    def __init__(self, d_model: int, num_heads: int, ffn_dim: int) -> None:
+        super().__init__()
+        self.norm1 = nn.LayerNorm(d_model)
+        self.attention = MixedPrecisionSelfAttention(d_model, num_heads)
+        self.norm2 = nn.LayerNorm(d_model)
+        self.ffn_in = nn.Linear(d_model, ffn_dim)
+        self.ffn_out = nn.Linear(ffn_dim, d_model)
+
+    def convert_projections_to_fp16(self) -> None:
+        self.attention.convert_projections_to_fp16()
+        self.ffn_in.half()
+        self.ffn_out.half()
+
+
+class _DevicePlan:
+    """libtt_b200 model handle + workspace for one device and one set of weights."""
+
+    def __init__(self, model: "B200Transformer", device: torch.device) -> None:
+        cfg = model.config
+        self.device = device
+        self.key = model._weights_key()
+        self._keep = []  # tensors whose pointers the C handle holds
+        layers = (_lib.LayerWeights * cfg.num_layers)()
+        for i, layer in enumerate(model.layers):
+            att = layer.attention
+            nxt = model.layers[i + 1].norm1 if i + 1 < cfg.num_layers else model.final_norm
+            lw = layers[i]
+            lw.w_qkv = self._w16(att.qkv_proj.weight)
+            lw.b_qkv = self._b32(model, f"layers.{i}.attention.qkv_proj", att.qkv_proj.bias)
+            lw.w_out = self._w16(att.out_proj.weight)
+            lw.b_out = self._b32(model, f"layers.{i}.attention.out_proj", att.out_proj.bias)
+            lw.ln_attn_w = self._f32(layer.norm2.weight)
+            lw.ln_attn_b = self._f32(layer.norm2.bias)
+            lw.w_ffn_in = self._w16(layer.ffn_in.weight)
+            lw.b_ffn_in = self._b32(model, f"layers.{i}.ffn_in", layer.ffn_in.bias)
+            lw.w_ffn_out = self._w16(layer.ffn_out.weight)
+            lw.b_ffn_out = self._b32(model, f"layers.{i}.ffn_out", layer.ffn_out.bias)
+            lw.ln_next_w = self._f32(nxt.weight)
+            lw.ln_next_b = self._f32(nxt.bias)
+        desc = _lib.ModelDesc()
+        desc.d_model = cfg.d_model
+        desc.heads = cfg.num_heads
+        desc.ffn_dim = cfg.ffn_dim
+        desc.num_layers = cfg.num_layers
+        desc.causal = int(bool(cfg.causal))
+        desc.eps = float(model.layers[0].norm1.eps)
+        desc.ln0_w = self._f32(model.layers[0].norm1.weight)
+        desc.ln0_b = self._f32(model.layers[0].norm1.bias)
+        desc.layers = layers
+        handle = ctypes.c_void_p()
+        with torch.cuda.device(device):
+            _lib.check(_lib.lib().tt_model_create(ctypes.byref(desc), ctypes.byref(handle)))
+        self.handle = handle
+        self._ws: Optional[torch.Tensor] = None
+        self._ws_ptr = 0
+        self._ws_bytes = 0
+
+    def _hold(self, t: torch.Tensor) -> int:
+        if t.device != self.device:
+            raise ValueError(f"parameter on {t.device}, model running on {self.device}")
+        self._keep.append(t)
+        return t.data_ptr()
+
+    def _w16(self, w: torch.Tensor) -> int:
+        if w.dtype != torch.float16:
+            raise RuntimeError(
+                "projection weights must be FP16: call convert_projections_to_fp16() after moving "
+                "the model to the GPU (mixed_precision_benchmark.py does this)"
+            )
+        return self._hold(w.detach().contiguous())
+
+    def _f32(self, t: torch.Tensor) -> int:
+        if t.dtype != torch.float32:
+            raise RuntimeError("LayerNorm parameters must stay FP32")
+        return self._hold(t.detach().contiguous())
+
+    def _b32(self, model: "B200Transformer", name: str, b: torch.Tensor) -> int:
+        src = model._bias_fp32.get(name)
+        if src is None or src.shape != b.shape:
+            src = b.detach()
+        return self._hold(src.to(device=self.device, dtype=torch.float32).contiguous())
+
+    def workspace(self, batch: int, seq: int):
+        nbytes = ctypes.c_size_t()
+        _lib.check(_lib.lib().tt_model_workspace_bytes(self.handle, batch, seq, ctypes.byref(nbytes)))
+        need = int(nbytes.value)
+        if self._ws is None or self._ws_bytes < need:
+            self._ws = None
+            raw = torch.empty(need + 1024, dtype=torch.uint8, device=self.device)
+            base = raw.data_ptr()
+            self._ws = raw
+            self._ws_ptr = (base + 1023) // 1024 * 1024
+            self._ws_bytes = need + 1024 - (self._ws_ptr - base)
+        return self._ws_ptr, self._ws_bytes
+
+    def close(self) -> None:
+        if getattr(self, "handle", None) is not None and self.handle.value:
+            try:
+                _lib.lib().tt_model_destroy(self.handle)
+            except Exception:  # pragma: no cover - interpreter teardown
+                pass
+            self.handle = ctypes.c_void_p()
+
+    def __del__(self) -> None:  # pragma: no cover
+        self.close()
+
+
+class B200Transformer(nn.Module):
+    """FP16 tensor-core projections/attention, FP32 residual stream, LayerNorm and GELU.
+
+    Drop-in for ``MixedPrecisionTransformer`` (mixed_precision/transformer.py:327-699):
+    same ``__init__`` signature, module tree and parameter names; the enable_*
+    switches are accepted for compatibility (the fused route is always used).
+    """
+
+    def __init__(
+        self,
+        config,
+        *,
+        enable_case11_schedule: bool = True,
+        enable_attention_output_norm_fusion: bool = True,
+        enable_full_ffn_fusion: bool = True,
+        enable_fp16_custom_attention: bool = True,
+        enable_fp16_normalized_stream: bool = True,
+    ) -> None:
+        super().__init__()
+        self.config = config
+        # Route flags the reference runner prints (mixed_precision_benchmark.py:67-77).
+        # The reference's Triton routes do not exist here; these describe the B200 route.
+        self.use_case8_triton = False
+        self.use_d128_triton = False
+        self.use_d32_triton = False
+        self.use_d128_custom_attention = False
+        self.use_case11_schedule = False
+        self.use_fp16_custom_attention = True
+        self.fuse_attention_output_norm = True
+        self.fuse_full_ffn = False
+        self.use_fp16_normalized_stream = True
+        self.layers = nn.ModuleList(
+            [
+                MixedPrecisionTransformerBlock(config.d_model, config.num_heads, config.ffn_dim)
+                for _ in range(config.num_layers)
+            ]
+        )
+        self.final_norm = nn.LayerNorm(config.d_model)
+        self.assume_all_tokens_valid = False
+        self._bias_fp32: Dict[str, torch.Tensor] = {}
+        self._plans: Dict[str, _DevicePlan] = {}
+
+    # -- reference surface ---------------------------------------------------
+    def convert_projections_to_fp16(self) -> None:
+        """Linear weights and biases to FP16, as the reference does (transformer.py:476-478).
+
+        The FP32 biases are kept aside first so the kernels can add them in
+        full precision; LayerNorm parameters stay FP32.
+        """
+        for i, layer in enumerate(self.layers):
+            for name, lin in (
+                ("attention.qkv_proj", layer.attention.qkv_proj),
+                ("attention.out_proj", layer.attention.out_proj),
+                ("ffn_in", layer.ffn_in),
+                ("ffn_out", layer.ffn_out),
+            ):
+                if lin.bias is not None and lin.bias.dtype == torch.float32:
+                    self._bias_fp32[f"layers.{i}.{name}"] = lin.bias.detach().clone()
+            layer.convert_projections_to_fp16()
+        self._drop_plans()
+
+    def route_description(self, seq_len: Optional[int] = None) -> str:
+        cfg = self.config
+        return _lib.route_describe(cfg.d_model, cfg.num_heads, seq_len or cfg.seq_len, cfg.ffn_dim)
+
+    # -- execution -------------------------------------------------------------
+    def _weights_key(self):
+        return tuple(p.data_ptr() for p in self.parameters()) + tuple(
+            t.data_ptr() for t in self._bias_fp32.values()
+        )
+
+    def _drop_plans(self) -> None:
+        for plan in self._plans.values():
+            plan.close()
+        self._plans = {}
+
+    def _plan(self, device: torch.device) -> _DevicePlan:
+        key = str(device)
+        plan = self._plans.get(key)
+        if plan is None or plan.key != self._weights_key():
+            if plan is not None:
+                plan.close()
+            plan = _DevicePlan(self, device)
+            self._plans[key] = plan
+        return plan
+
+    def _apply(self, fn, recurse=True):
+        self._drop_plans()
+        out = super()._apply(fn, recurse)
+        self._bias_fp32 = {k: fn(v) for k, v in self._bias_fp32.items()}
+        return out
+
+    def set_profiling(self, enable: bool, device: Optional[torch.device] = None) -> None:
+        """Record CUDA events around every kernel of later forwards on ``device``."""
+        dev = torch.device(device) if device is not None else next(self.parameters()).device
+        _lib.check(_lib.lib().tt_model_set_profiling(self._plan(dev).handle, int(enable)))
+
+    def profile_collect(self, device: Optional[torch.device] = None) -> Dict[str, tuple]:
+        """{kernel kind: (total device ms, launches)} since the previous collect."""
+        dev = torch.device(device) if device is not None else next(self.parameters()).device
+        n = len(_lib.KERNEL_KINDS)
+        ms = (ctypes.c_float * n)()
+        cnt = (ctypes.c_int * n)()
+        with torch.cuda.device(dev):
+            _lib.check(_lib.lib().tt_model_profile_collect(self._plan(dev).handle, ms, cnt, n))
+        return {k: (float(ms[i]), int(cnt[i])) for i, k in enumerate(_lib.KERNEL_KINDS)}
+
+    def forward(self, x: torch.Tensor, valid_token_mask: Optional[torch.Tensor] = None) -> torch.Tensor:
+        if x.dtype != torch.float32:
+            raise ValueError("mixed candidate requires an FP32 input/residual stream")
+        if not x.is_cuda:
+            raise RuntimeError("B200Transformer runs only on CUDA (sm_100a) devices; there is no CPU path")
+        if x.dim() != 3 or x.shape[-1] != self.config.d_model:
+            raise ValueError(f"expected x of shape [B, S, {self.config.d_model}], got {tuple(x.shape)}")
+        B, S, _ = x.shape
+        mask = None if self.assume_all_tokens_valid else valid_token_mask
+        x = x.contiguous()
+        out = torch.empty_like(x)
+        if B == 0 or S == 0:
+            return out
+        plan = self._plan(x.device)
+        mask_ptr = 0
+        if mask is not None:
+            if mask.shape != (B, S):
+                raise ValueError(f"valid_token_mask must have shape {(B, S)}, got {tuple(mask.shape)}")
+            mask8 = mask.to(device=x.device, dtype=torch.bool).contiguous().view(torch.uint8)
+            mask_ptr = mask8.data_ptr()
+        ws_ptr, ws_bytes = plan.workspace(B, S)
+        with torch.cuda.device(x.device):
+            stream = torch.cuda.current_stream(x.device).cuda_stream
+            _lib.check(
+                _lib.lib().tt_model_forward(
+                    plan.handle, x.data_ptr(), mask_ptr, out.data_ptr(), B, S, ws_ptr, ws_bytes, stream
+                )
+            )
+        return out
+
+
+# The reference's class name, for drop-in imports.
+MixedPrecisionTransformer = B200Transformer
+
+
+def copy_mixed_model_weights(baseline: nn.Module, mixed: nn.Module) -> None:
+    """Copy FP32 baseline weights into the mixed model, packing Q/K/V.
+
+    Same contract as mixed_precision/transformer.py:702-731: for every
+    ``attention.qkv_proj`` tensor the baseline's q/k/v tensors are
+    concatenated along dim 0; everything else is copied by name; strict load.
+    """
+    source = copy.deepcopy(baseline.state_dict())
+    mapped = {}
+    for key in mixed.state_dict():
+        for leaf in ("weight", "bias"):
+            suffix = f"attention.qkv_proj.{leaf}"
+            if key.endswith(suffix):
+                prefix = key[: -len(suffix)] + "attention."
+                mapped[key] = torch.cat(
+                    [source[f"{prefix}{n}_proj.{leaf}"] for n in ("q", "k", "v")], dim=0
+                )
+                break
+        else:
+            mapped[key] = source[key]
+    mixed.load_state_dict(mapped, strict=True)
