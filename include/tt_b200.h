@@ -87,7 +87,8 @@ int tt_qkv_projection(const void* normalized, const void* w_qkv, const float* b_
 /* ctx[b, s, h*hd:(h+1)*hd] = softmax(q k^T * scale + causal + key mask) v,
  * FP16 operands, FP32 softmax statistics and accumulation, FP16 output.
  * key_mask: [batch, seq] bytes (nonzero = valid) or NULL; kv_end must then hold
- * tt_mask_kv_end's output.  head_dim in {16, 32, 64}.
+ * tt_mask_kv_end's output.  With a mask, padded query rows get a zero context
+ * (the reference zeroes those rows on the model output).  head_dim in {16, 32, 64}.
  * Replaces fp16_causal_attention / causal_attention
  * (custom_kernel/triton_attention.py:126-232, 264-390) and the SDPA route
  * (mixed_precision/transformer.py:157-198). */

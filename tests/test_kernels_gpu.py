@@ -94,10 +94,8 @@ def test_attention(tt_lib, B, H, S, hd, causal, mask_kind):
     out = ops.attention(q, k, vt, scale, causal, mask)
     ref = _attn_ref(q, k, vt, scale, causal, mask)
     if mask is not None:
-        # Query rows whose causal window holds no valid key are defined as zero.
-        cm = torch.ones(S, S, dtype=torch.bool, device=DEV).tril() if causal else torch.ones(S, S, dtype=torch.bool, device=DEV)
-        seen = (cm[None] & mask[:, None, :]).any(-1)  # [B, S]
-        ref = ref.masked_fill(~seen[..., None], 0)
+        # Padded query rows are defined as zero context.
+        ref = ref.masked_fill(~mask[..., None], 0)
     # P is rounded to FP16 before P.V (as in the reference kernel); |ctx| <= max|v| < 5
     torch.testing.assert_close(out.float(), ref, rtol=5e-3, atol=5e-3)
 
@@ -112,7 +110,7 @@ def test_attention_fully_padded_tile_is_zero(tt_lib):
     mask[0, :100] = True
     mask[1, :300] = True
     out = ops.attention(q, k, vt, hd**-0.5, True, mask)
-    assert torch.all(out[0, 128:] == 0) and torch.all(out[1, 384:] == 0)
+    assert torch.all(out[0, 100:] == 0) and torch.all(out[1, 300:] == 0)
     ref = _attn_ref(q, k, vt, hd**-0.5, True, mask)
     torch.testing.assert_close(out[0, :100].float(), ref[0, :100], rtol=5e-3, atol=5e-3)
     torch.testing.assert_close(out[1, :300].float(), ref[1, :300], rtol=5e-3, atol=5e-3)

@@ -16,10 +16,12 @@
 //           buffered), folded into the FP32 register accumulator with the
 //           running-max correction one iteration later.
 // Key tiles strictly above the causal diagonal, and key tiles past the last
-// valid key of a padded sequence, are never loaded.  Query tiles that lie
-// wholly in a sequence's padding are written as zeros.  A query row that sees
-// no valid key produces zeros (the reference would produce NaN there; such a
-// row is always a padded row, which the model zeroes on output).
+// valid key of a padded sequence, are never loaded.  The context of every
+// padded query row (mask byte 0) is zero; query tiles that lie wholly in a
+// sequence's padding skip all work.  (The reference computes padded rows and
+// zeroes them only on the model output, mixed_precision/transformer.py:697-698;
+// valid rows never read padded rows, whose keys are masked.)  A valid query
+// row always sees at least itself as a valid key, so no row divides by zero.
 #pragma once
 
 #include "tt_ptx.cuh"
@@ -330,7 +332,10 @@ __global__ void __launch_bounds__(192, 1)
     if (ok) ok = consume_o(n_tiles - 1, corr_prev);
 
     if (ok && qi < p.seq) {
-      const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
+      // Padded query rows (mask byte 0) get a zero context, like whole padded tiles.
+      const bool row_valid =
+          p.key_mask == nullptr || p.key_mask[static_cast<size_t>(b) * p.seq + qi] != 0;
+      const float inv = (row_valid && l_run > 0.f) ? 1.f / l_run : 0.f;
       uint4* dst = reinterpret_cast<uint4*>(p.ctx + (static_cast<size_t>(b) * p.seq + qi) * D + h * HD);
 #pragma unroll
       for (int i = 0; i < HD / 8; ++i) {
