@@ -69,6 +69,8 @@ def parse_args():
     ap.add_argument("--impl", default="b200", choices=("b200", "reference"))
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-sample-seconds", type=float, default=12.0)
+    ap.add_argument("--batch", type=int, default=None,
+                    help="override the workload's global batch (smaller profiling cases)")
     return ap.parse_args()
 
 
@@ -255,8 +257,10 @@ def run_reference(args, cfg, padding_ratio, workload_name):
 def main() -> int:
     args = parse_args()
     B, S, D, H, F, L, causal, pad = WORKLOADS[args.config]
+    if args.batch is not None:
+        B = args.batch
     cfg = {"batch": B, "seq": S, "d_model": D, "heads": H, "ffn": F, "layers": L, "causal": causal}
-    workload_name = args.config
+    workload_name = args.config if args.batch is None else f"{args.config}-batch{B}"
     if args.impl == "reference":
         return run_reference(args, cfg, pad, workload_name)
 
