@@ -96,6 +96,26 @@ int tt_causal_attention(const void* q, const void* k, const void* vt, const uint
                         const int* kv_end, void* ctx, int batch, int seq, int heads, int head_dim,
                         int seq_pad, float scale, int causal, void* stream);
 
+/* Same result as tt_mask_kv_end followed by tt_causal_attention, for callers
+ * that cannot allocate device memory: the per-sequence scratch (kv_end) lives
+ * in a static device array inside the library (256 KiB per GPU that loads it,
+ * held until exit), so the caller passes only inputs and outputs.  Callers
+ * that need this include hosts capturing their launches into a CUDA graph,
+ * runtimes whose device memory belongs to an external pool, and servers that
+ * forbid allocation after start-up.
+ * Limits: batch <= 65536 (larger batches return TT_ERR_SHAPE; split them).
+ * All calls on a device share the one array, so calls that overlap on the GPU
+ * (different streams, no ordering between them) race; serialize them.  The
+ * first call on a device looks up the array's device address (that device
+ * must be current); make that first call before any stream capture.
+ * key_mask may be NULL (then no scratch is used).
+ * No counterpart in the reference: it has no C ABI and allocates through
+ * PyTorch. */
+int tt_causal_attention_masked_noalloc(const void* q, const void* k, const void* vt,
+                                       const uint8_t* key_mask, void* ctx, int batch, int seq,
+                                       int heads, int head_dim, int seq_pad, float scale, int causal,
+                                       void* stream);
+
 /* resid_out = a[N, k_in] (FP16) . w[d_model, k_in]^T + bias + resid_in (FP32);
  * norm_out = LayerNorm(resid_out) * gamma + beta (FP16 or FP32); rows whose
  * row_mask byte is 0 get norm_out = 0 (row_mask may be NULL).  d_model <= 256

@@ -356,6 +356,55 @@ int launch_attention(const CUtensorMap& tq, const CUtensorMap& tk, const CUtenso
 
 using namespace tt;
 
+// ---------------------------------------------------------------------------
+// Allocation-free masked attention: static scratch.
+//
+// Some callers cannot call cudaMalloc at all, or not at the moment they
+// launch: a host program that captures its launches into a CUDA graph, a
+// runtime whose device memory is owned by an external pool or arena, or a
+// latency-critical server that forbids allocation after start-up.  For them
+// tt_causal_attention_masked_noalloc keeps the one scratch buffer the masked
+// attention path needs (the per-sequence end of the valid keys, one int per
+// sequence) in this file-scope device array instead of a caller buffer.
+// Every GPU that loads the library holds it (256 KiB) until the process exits.
+// ---------------------------------------------------------------------------
+static constexpr int kNoAllocMaxBatch = 65536;
+static __device__ __align__(256) int g_noalloc_kv_end[kNoAllocMaxBatch];
+
+namespace {
+
+struct NoAllocScratch {
+  std::once_flag once;
+  int status = TT_OK;
+  int* kv_end = nullptr;  // device address of g_noalloc_kv_end on this device
+};
+NoAllocScratch g_noalloc[64];
+
+// In host code `g_noalloc_kv_end` names a host-side stand-in, not device
+// memory, so its device address is looked up once per device (with that
+// device current) and cached.
+int noalloc_scratch_for_current_device(int** out) {
+  int dev = 0;
+  if (int rc = check_cuda(cudaGetDevice(&dev), "cudaGetDevice")) return rc;
+  if (dev < 0 || dev >= 64) return fail(TT_ERR_ARG, "device ordinal %d out of range", dev);
+  NoAllocScratch& st = g_noalloc[dev];
+  std::call_once(st.once, [&] {
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_kv_end);
+    if (e != cudaSuccess) {
+      st.status = fail(TT_ERR_LAUNCH, "cudaGetSymbolAddress(no-alloc scratch): %s", cudaGetErrorString(e));
+      return;
+    }
+    st.kv_end = static_cast<int*>(p);
+    st.status = TT_OK;
+  });
+  if (st.status != TT_OK) return st.status;
+  *out = st.kv_end;
+  return TT_OK;
+}
+
+}  // namespace
+
 // =========================================================================
 // Whole model
 // =========================================================================
@@ -618,6 +667,49 @@ int tt_causal_attention(const void* q, const void* k, const void* vt, const uint
   ap.err = ds->err;
   ap.timeout_ns = g_timeout_ns.load();
   return launch_attention(tq, tk, tv, ap, head_dim, static_cast<cudaStream_t>(stream));
+}
+
+int tt_causal_attention_masked_noalloc(const void* q, const void* k, const void* vt,
+                                       const uint8_t* key_mask, void* ctx, int batch, int seq,
+                                       int heads, int head_dim, int seq_pad, float scale, int causal,
+                                       void* stream) {
+  // Set-up on the first call on a device (needs that device current): the
+  // scratch array's device address.  Allocates nothing, here or later.
+  DeviceState* ds;
+  if (int rc = current_device_state(&ds)) return rc;
+  int* kv_end = nullptr;
+  if (int rc = noalloc_scratch_for_current_device(&kv_end)) return rc;
+  if (!q || !k || !vt || !ctx) return fail(TT_ERR_ARG, "null argument");
+  if (batch <= 0 || seq <= 0 || heads <= 0 || seq_pad < seq || seq_pad % 8 != 0)
+    return fail(TT_ERR_SHAPE, "invalid sizes");
+  if (batch > kNoAllocMaxBatch)
+    return fail(TT_ERR_SHAPE,
+                "batch %d exceeds the %d sequences the static scratch of "
+                "tt_causal_attention_masked_noalloc holds; split the batch",
+                batch, kNoAllocMaxBatch);
+  CUtensorMap tq, tk, tv;
+  if (int rc = encode_attention_maps(&tq, &tk, &tv, q, k, vt, batch * heads, seq, head_dim, seq_pad))
+    return rc;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (key_mask) {
+    // Overwrites kv_end[0..batch); entries past `batch` are never read, so
+    // whatever an earlier call left in the shared array needs no clearing.
+    mask_kv_end_kernel<<<batch, 256, 0, s>>>(key_mask, seq, kv_end);
+    if (int rc = after_launch("mask_kv_end (no-alloc)")) return rc;
+  }
+  AttnParams ap;
+  ap.batch = batch;
+  ap.seq = seq;
+  ap.heads = heads;
+  ap.seq_pad = seq_pad;
+  ap.causal = causal ? 1 : 0;
+  ap.scale_log2 = scale * 1.4426950408889634f;
+  ap.key_mask = key_mask;
+  ap.kv_end = key_mask ? kv_end : nullptr;
+  ap.ctx = static_cast<__half*>(ctx);
+  ap.err = ds->err;
+  ap.timeout_ns = g_timeout_ns.load();
+  return launch_attention(tq, tk, tv, ap, head_dim, s);
 }
 
 int tt_linear_residual_layernorm(const void* a, const void* w, const float* bias,
