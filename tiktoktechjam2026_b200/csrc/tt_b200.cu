@@ -28,7 +28,7 @@ namespace {
 
 constexpr int kAbiVersion = 1;
 constexpr int kMaxDevices = 64;
-constexpr int kSmemBudget = 200 * 1024;
+constexpr int kSmemBudget = 225 * 1024;
 
 thread_local char g_last_error[512] = "";
 std::atomic<unsigned long long> g_launches{0};
@@ -113,9 +113,10 @@ CUtensorMapSwizzle swizzle_for_bytes(int inner_bytes) {
                               : CU_TENSOR_MAP_SWIZZLE_NONE;
 }
 
-// FP16 tensor map of rank 2 or 3 (dims innermost first, byte strides of dims 1..).
-int encode_f16(CUtensorMap* tm, const void* base, int rank, const uint64_t* dims,
-               const uint64_t* strides_bytes, const uint32_t* box) {
+// Tensor map of rank 2 or 3 (dims innermost first, byte strides of dims 1..);
+// the swizzle follows the box's inner extent in bytes (32, 64 or 128).
+int encode_tensor(CUtensorMap* tm, CUtensorMapDataType dtype, int elem_bytes, const void* base,
+                  int rank, const uint64_t* dims, const uint64_t* strides_bytes, const uint32_t* box) {
   if (int rc = get_encoder()) return rc;
   if (reinterpret_cast<uintptr_t>(base) % 16 != 0)
     return fail(TT_ERR_ALIGN, "tensor base %p is not 16-byte aligned", base);
@@ -125,13 +126,18 @@ int encode_f16(CUtensorMap* tm, const void* base, int rank, const uint64_t* dims
                   static_cast<unsigned long long>(strides_bytes[i]));
   cuuint32_t elem_strides[3] = {1, 1, 1};
   const CUresult r = g_encode(
-      tm, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, static_cast<cuuint32_t>(rank), const_cast<void*>(base),
+      tm, dtype, static_cast<cuuint32_t>(rank), const_cast<void*>(base),
       reinterpret_cast<const cuuint64_t*>(dims), reinterpret_cast<const cuuint64_t*>(strides_bytes),
       reinterpret_cast<const cuuint32_t*>(box), elem_strides, CU_TENSOR_MAP_INTERLEAVE_NONE,
-      swizzle_for_bytes(static_cast<int>(box[0]) * 2), CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+      swizzle_for_bytes(static_cast<int>(box[0]) * elem_bytes), CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
       CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return fail(TT_ERR_LAUNCH, "cuTensorMapEncodeTiled failed (%d)", int(r));
   return TT_OK;
+}
+
+int encode_f16(CUtensorMap* tm, const void* base, int rank, const uint64_t* dims,
+               const uint64_t* strides_bytes, const uint32_t* box) {
+  return encode_tensor(tm, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, base, rank, dims, strides_bytes, box);
 }
 
 // Row-major [rows, cols] FP16 matrix, box {box_cols, box_rows}.
@@ -141,6 +147,39 @@ int encode_matrix(CUtensorMap* tm, const void* base, uint64_t rows, uint64_t col
   const uint64_t strides[1] = {cols * 2};
   const uint32_t box[2] = {static_cast<uint32_t>(box_cols), static_cast<uint32_t>(box_rows)};
   return encode_f16(tm, base, 2, dims, strides, box);
+}
+
+// Row-major [rows, cols] matrix of FP32 or FP16 in [32 x 32] epilogue tiles.
+int encode_epi_tile(CUtensorMap* tm, const void* base, uint64_t rows, uint64_t cols, bool f32) {
+  const int eb = f32 ? 4 : 2;
+  const uint64_t dims[2] = {cols, rows};
+  const uint64_t strides[1] = {cols * eb};
+  const uint32_t box[2] = {32, 32};
+  return encode_tensor(tm, f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, eb,
+                       base, 2, dims, strides, box);
+}
+
+// Store maps of the QKV epilogue: Q, K [B*H, S, hd] and V^T [B*H, hd, S_pad].
+int encode_qkv_store_maps(CUtensorMap* tq, CUtensorMap* tk, CUtensorMap* tv, const void* q,
+                          const void* k, const void* vt, int bh, int seq, int hd, int seq_pad) {
+  const uint32_t w = static_cast<uint32_t>(hd < 32 ? hd : 32);
+  {
+    const uint64_t dims[3] = {static_cast<uint64_t>(hd), static_cast<uint64_t>(seq),
+                              static_cast<uint64_t>(bh)};
+    const uint64_t strides[2] = {static_cast<uint64_t>(hd) * 2, static_cast<uint64_t>(hd) * seq * 2};
+    const uint32_t box[3] = {w, 32, 1};
+    if (int rc = encode_f16(tq, q, 3, dims, strides, box)) return rc;
+    if (int rc = encode_f16(tk, k, 3, dims, strides, box)) return rc;
+  }
+  {
+    const uint64_t dims[3] = {static_cast<uint64_t>(seq_pad), static_cast<uint64_t>(hd),
+                              static_cast<uint64_t>(bh)};
+    const uint64_t strides[2] = {static_cast<uint64_t>(seq_pad) * 2,
+                                 static_cast<uint64_t>(seq_pad) * hd * 2};
+    const uint32_t box[3] = {32, w, 1};
+    if (int rc = encode_f16(tv, vt, 3, dims, strides, box)) return rc;
+  }
+  return TT_OK;
 }
 
 template <typename K>
@@ -167,6 +206,7 @@ struct Route {
   int out_nst;
   int ffn_in_bn, ffn_in_nst;
   int ffn_out_nst;
+  int attn_exp16;  // 1: probabilities from packed-FP16 exp2, 0: FP32 exp2
 };
 
 struct RouteEntry {
@@ -176,15 +216,15 @@ struct RouteEntry {
 
 const RouteEntry kRouteTable[] = {
     // C1  B64 S128  D128 H4 F128
-    {128, 4, 128, 128, {"d128-h4-s128", 128, 2, 2, 128, 2, 2}},
+    {128, 4, 128, 128, {"d128-h4-s128", 128, 2, 2, 128, 2, 2, 1}},
     // C2  B64 S1024 D128 H4 F128
-    {128, 4, 1024, 128, {"d128-h4-s1024", 128, 2, 2, 128, 2, 2}},
+    {128, 4, 1024, 128, {"d128-h4-s1024", 128, 2, 2, 128, 2, 2, 1}},
     // C3  B256 S256 D32 H2 F128
-    {32, 2, 256, 128, {"d32-h2-s256", 96, 1, 1, 128, 1, 4}},
+    {32, 2, 256, 128, {"d32-h2-s256", 96, 1, 1, 128, 1, 4, 1}},
     // C4  B16 S2048 D512 H8 F2048 (+ key padding)
-    {512, 8, 2048, 2048, {"d512-h8-s2048", 256, 4, 2, 256, 4, 2}},
+    {512, 8, 2048, 2048, {"d512-h8-s2048", 256, 4, 2, 256, 4, 2, 1}},
     // C5  B512 S1024 D256 H8 F1024
-    {256, 8, 1024, 1024, {"d256-h8-s1024", 256, 2, 2, 256, 2, 3}},
+    {256, 8, 1024, 1024, {"d256-h8-s1024", 256, 2, 2, 256, 2, 3, 1}},
 };
 
 int largest_bn_dividing(int n, int cap) {
@@ -193,12 +233,17 @@ int largest_bn_dividing(int n, int cap) {
   return 0;
 }
 
-int clamp_nst(int ksw, int bn, int k, int want) {
+int clamp_nst(int ksw, int bn, int k, int want, int epi, int n_total) {
   const int nk = k / ksw;
   int nst = want < nk ? want : nk;
-  while (nst > 1 && gemm_smem_bytes(ksw, bn, nst) > kSmemBudget) --nst;
+  if (nst > kGemmMaxStages) nst = kGemmMaxStages;
+  while (nst > 1 && gemm_smem_bytes(ksw, bn, nst, epi, n_total) > kSmemBudget) --nst;
   return nst < 1 ? 1 : nst;
 }
+
+// K-block width of a GEMM: 64 FP16 (128-byte swizzle) unless K is not a
+// multiple of 64 or the 512-column residual tile needs the smaller stage.
+int gemm_ksw(int k, int bn) { return (k % 64 == 0 && bn <= 256) ? 64 : 32; }
 
 int check_model_shape(int d_model, int heads, int ffn) {
   if (d_model <= 0 || heads <= 0 || ffn <= 0 || d_model % heads != 0)
@@ -228,38 +273,40 @@ int choose_route(int d_model, int heads, int seq, int ffn, Route* out) {
   r.ffn_in_bn = largest_bn_dividing(ffn, 256);
   r.ffn_in_nst = 4;
   r.ffn_out_nst = 4;
+  r.attn_exp16 = 1;
   if (r.qkv_bn == 0 || r.ffn_in_bn == 0)
     return fail(TT_ERR_UNSUPPORTED, "no column split for d_model=%d ffn=%d", d_model, ffn);
   *out = r;
   return TT_OK;
 }
 
-int ksw_for(int k) { return (k % 64 == 0) ? 64 : 32; }
 
 // ---------------------------------------------------------------- launchers
 template <int KSW, int EPI>
-int launch_gemm_t(const CUtensorMap& tmA, const CUtensorMap& tmW, const GemmParams& p,
-                  cudaStream_t stream) {
-  const int smem = gemm_smem_bytes(KSW, p.bn, p.nst);
+int launch_gemm_t(const GemmMaps& maps, GemmParams p, int sm_count, cudaStream_t stream) {
+  const int smem = gemm_smem_bytes(KSW, p.bn, p.nst, EPI, p.N_total);
+  if (smem > 232448) return fail(TT_ERR_UNSUPPORTED, "GEMM tile needs %d bytes of shared memory", smem);
   auto kern = gemm_kernel<KSW, EPI>;
   if (int rc = prepare_kernel(kern, smem)) return rc;
   const long long m_tiles = (static_cast<long long>(p.M) + 127) / 128;
-  const long long grid = m_tiles * p.n_splits;
-  if (grid > 0x7fffffffLL) return fail(TT_ERR_SHAPE, "grid too large");
-  kern<<<static_cast<unsigned>(grid), 192, smem, stream>>>(tmA, tmW, p);
+  const long long items = m_tiles * p.n_splits;
+  if (items > 0x7fffffffLL) return fail(TT_ERR_SHAPE, "too many tiles");
+  p.n_items = static_cast<int>(items);
+  const unsigned grid = static_cast<unsigned>(items < sm_count ? items : sm_count);
+  kern<<<grid, 192, smem, stream>>>(maps, p);
   return after_launch("gemm");
 }
 
-int launch_gemm(int ksw, int epi, const CUtensorMap& tmA, const CUtensorMap& tmW,
-                const GemmParams& p, cudaStream_t stream) {
+int launch_gemm(int ksw, int epi, const GemmMaps& maps, const GemmParams& p, int sm_count,
+                cudaStream_t stream) {
   if (ksw == 64) {
-    if (epi == EPI_QKV) return launch_gemm_t<64, EPI_QKV>(tmA, tmW, p, stream);
-    if (epi == EPI_RESID_LN) return launch_gemm_t<64, EPI_RESID_LN>(tmA, tmW, p, stream);
-    return launch_gemm_t<64, EPI_GELU>(tmA, tmW, p, stream);
+    if (epi == EPI_QKV) return launch_gemm_t<64, EPI_QKV>(maps, p, sm_count, stream);
+    if (epi == EPI_RESID_LN) return launch_gemm_t<64, EPI_RESID_LN>(maps, p, sm_count, stream);
+    return launch_gemm_t<64, EPI_GELU>(maps, p, sm_count, stream);
   }
-  if (epi == EPI_QKV) return launch_gemm_t<32, EPI_QKV>(tmA, tmW, p, stream);
-  if (epi == EPI_RESID_LN) return launch_gemm_t<32, EPI_RESID_LN>(tmA, tmW, p, stream);
-  return launch_gemm_t<32, EPI_GELU>(tmA, tmW, p, stream);
+  if (epi == EPI_QKV) return launch_gemm_t<32, EPI_QKV>(maps, p, sm_count, stream);
+  if (epi == EPI_RESID_LN) return launch_gemm_t<32, EPI_RESID_LN>(maps, p, sm_count, stream);
+  return launch_gemm_t<32, EPI_GELU>(maps, p, sm_count, stream);
 }
 
 GemmParams base_params(DeviceState* ds) {
@@ -327,23 +374,26 @@ int encode_attention_maps(CUtensorMap* tq, CUtensorMap* tk, CUtensorMap* tv, con
 }
 
 int launch_attention(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
-                     const AttnParams& ap, int hd, cudaStream_t stream) {
-  const int n_qt = (ap.seq + 127) / 128;
-  if (n_qt > 65535) return fail(TT_ERR_SHAPE, "seq %d too long", ap.seq);
-  const long long bh = static_cast<long long>(ap.batch) * ap.heads;
-  if (bh > 0x7fffffffLL) return fail(TT_ERR_SHAPE, "batch*heads too large");
-  dim3 grid(static_cast<unsigned>(bh), static_cast<unsigned>(n_qt));
-  switch (hd) {
-#define TT_ATTN_CASE(HD)                                                          \
-  case HD: {                                                                      \
-    auto kern = attn_fwd_kernel<HD>;                                              \
-    if (int rc = prepare_kernel(kern, AttnLayout<HD>::SMEM_ALLOC)) return rc;     \
-    kern<<<grid, 192, AttnLayout<HD>::SMEM_ALLOC, stream>>>(tq, tk, tv, ap);      \
-    break;                                                                        \
+                     const AttnParams& ap, int hd, bool exp16, int sm_count, cudaStream_t stream) {
+  const long long n_qt = (ap.seq + 127) / 128;
+  const long long items = static_cast<long long>(ap.batch) * ap.heads * n_qt;
+  if (items > 0x7fffffffLL) return fail(TT_ERR_SHAPE, "batch*heads*query tiles too large");
+  const int n_items = static_cast<int>(items);
+  const unsigned grid = static_cast<unsigned>(n_items < sm_count ? n_items : sm_count);
+  switch (hd * 2 + (exp16 ? 1 : 0)) {
+#define TT_ATTN_CASE(HD, E)                                                         \
+  case HD * 2 + E: {                                                                \
+    auto kern = attn_fwd_kernel<HD, E != 0>;                                        \
+    if (int rc = prepare_kernel(kern, AttnLayout<HD>::SMEM_ALLOC)) return rc;       \
+    kern<<<grid, 192, AttnLayout<HD>::SMEM_ALLOC, stream>>>(tq, tk, tv, ap, n_items); \
+    break;                                                                          \
   }
-    TT_ATTN_CASE(16)
-    TT_ATTN_CASE(32)
-    TT_ATTN_CASE(64)
+    TT_ATTN_CASE(16, 0)
+    TT_ATTN_CASE(16, 1)
+    TT_ATTN_CASE(32, 0)
+    TT_ATTN_CASE(32, 1)
+    TT_ATTN_CASE(64, 0)
+    TT_ATTN_CASE(64, 1)
 #undef TT_ATTN_CASE
     default:
       return fail(TT_ERR_UNSUPPORTED, "head_dim %d not in {16, 32, 64}", hd);
@@ -422,7 +472,11 @@ struct tt_model {
   int route_seq = -1;
   int bound_batch = -1, bound_seq = -1;
   void* bound_ws = nullptr;
+  int ksw_qkv = 64, ksw_out = 64, ksw_in = 64, ksw_out2 = 64;
+  // Operand loads (box {KSW, 128}) and attention loads.
   CUtensorMap tm_norm{}, tm_ctx{}, tm_hidden{}, tm_q{}, tm_k{}, tm_vt{};
+  // Epilogue tiles (box 32 x 32): QKV stores, residual (FP32), normalized and hidden (FP16).
+  CUtensorMap tm_q_st{}, tm_k_st{}, tm_vt_st{}, tm_resid{}, tm_norm_st{}, tm_hidden_st{};
   // Profiling.
   bool profiling = false;
   struct Rec {
@@ -495,7 +549,10 @@ int bind_workspace(tt_model* m, int batch, int seq, void* ws, cudaStream_t strea
     if (int rc = choose_route(m->D, m->H, seq, m->F, &m->route)) return rc;
     m->route_seq = seq;
     // Weight maps depend on the route's column tiles.
-    const int ksw_d = ksw_for(m->D), ksw_f = ksw_for(m->F);
+    m->ksw_qkv = gemm_ksw(m->D, m->route.qkv_bn);
+    m->ksw_out = gemm_ksw(m->D, m->D);
+    m->ksw_in = gemm_ksw(m->D, m->route.ffn_in_bn);
+    m->ksw_out2 = gemm_ksw(m->F, m->D);
     m->tm_wqkv.resize(m->L);
     m->tm_wout.resize(m->L);
     m->tm_win.resize(m->L);
@@ -503,12 +560,12 @@ int bind_workspace(tt_model* m, int batch, int seq, void* ws, cudaStream_t strea
     const int out_box = m->D > 256 ? 256 : m->D;
     for (int l = 0; l < m->L; ++l) {
       const tt_layer_weights& w = m->layers[l];
-      if (int rc = encode_matrix(&m->tm_wqkv[l], w.w_qkv, 3 * m->D, m->D, ksw_d, m->route.qkv_bn))
+      if (int rc = encode_matrix(&m->tm_wqkv[l], w.w_qkv, 3 * m->D, m->D, m->ksw_qkv, m->route.qkv_bn))
         return rc;
-      if (int rc = encode_matrix(&m->tm_wout[l], w.w_out, m->D, m->D, ksw_d, out_box)) return rc;
-      if (int rc = encode_matrix(&m->tm_win[l], w.w_ffn_in, m->F, m->D, ksw_d, m->route.ffn_in_bn))
+      if (int rc = encode_matrix(&m->tm_wout[l], w.w_out, m->D, m->D, m->ksw_out, out_box)) return rc;
+      if (int rc = encode_matrix(&m->tm_win[l], w.w_ffn_in, m->F, m->D, m->ksw_in, m->route.ffn_in_bn))
         return rc;
-      if (int rc = encode_matrix(&m->tm_wout2[l], w.w_ffn_out, m->D, m->F, ksw_f, out_box))
+      if (int rc = encode_matrix(&m->tm_wout2[l], w.w_ffn_out, m->D, m->F, m->ksw_out2, out_box))
         return rc;
     }
     m->bound_ws = nullptr;
@@ -518,13 +575,20 @@ int bind_workspace(tt_model* m, int batch, int seq, void* ws, cudaStream_t strea
   uint8_t* base = static_cast<uint8_t*>(ws);
   const uint64_t N = static_cast<uint64_t>(batch) * seq;
   const int hd = m->D / m->H;
-  const int ksw_d = ksw_for(m->D), ksw_f = ksw_for(m->F);
-  if (int rc = encode_matrix(&m->tm_norm, base + w.norm, N, m->D, ksw_d, 128)) return rc;
-  if (int rc = encode_matrix(&m->tm_ctx, base + w.ctx, N, m->D, ksw_d, 128)) return rc;
-  if (int rc = encode_matrix(&m->tm_hidden, base + w.hidden, N, m->F, ksw_f, 128)) return rc;
+  if (m->ksw_qkv != m->ksw_in) return fail(TT_ERR_UNSUPPORTED, "QKV and FFN-in K-blocks differ");
+  if (int rc = encode_matrix(&m->tm_norm, base + w.norm, N, m->D, m->ksw_qkv, 128)) return rc;
+  if (int rc = encode_matrix(&m->tm_ctx, base + w.ctx, N, m->D, m->ksw_out, 128)) return rc;
+  if (int rc = encode_matrix(&m->tm_hidden, base + w.hidden, N, m->F, m->ksw_out2, 128)) return rc;
   if (int rc = encode_attention_maps(&m->tm_q, &m->tm_k, &m->tm_vt, base + w.q, base + w.k,
                                      base + w.vt, batch * m->H, seq, hd, w.seq_pad))
     return rc;
+  if (seq % 32 == 0)
+    if (int rc = encode_qkv_store_maps(&m->tm_q_st, &m->tm_k_st, &m->tm_vt_st, base + w.q, base + w.k,
+                                       base + w.vt, batch * m->H, seq, hd, w.seq_pad))
+      return rc;
+  if (int rc = encode_epi_tile(&m->tm_resid, base + w.resid, N, m->D, true)) return rc;
+  if (int rc = encode_epi_tile(&m->tm_norm_st, base + w.norm, N, m->D, false)) return rc;
+  if (int rc = encode_epi_tile(&m->tm_hidden_st, base + w.hidden, N, m->F, false)) return rc;
   // V^T columns in [seq, seq_pad) are never written by the projection; they
   // must hold finite values because masked probabilities (0) multiply them.
   if (w.seq_pad != seq)
@@ -615,32 +679,38 @@ int tt_qkv_projection(const void* normalized, const void* w_qkv, const float* b_
   if (batch <= 0 || seq <= 0 || seq_pad < seq || seq_pad % 8 != 0)
     return fail(TT_ERR_SHAPE, "invalid batch/seq/seq_pad (%d, %d, %d)", batch, seq, seq_pad);
   if (int rc = check_model_shape(d_model, heads, 32)) return rc;
-  Route r;
-  r.qkv_bn = largest_bn_dividing(3 * d_model, d_model <= 128 ? 128 : 256);
-  r.qkv_nst = 4;
-  const int ksw = ksw_for(d_model);
-  CUtensorMap tmA, tmW;
   const uint64_t N = static_cast<uint64_t>(batch) * seq;
-  if (int rc = encode_matrix(&tmA, normalized, N, d_model, ksw, 128)) return rc;
-  if (int rc = encode_matrix(&tmW, w_qkv, 3 * d_model, d_model, ksw, r.qkv_bn)) return rc;
+  if (N > 0x7fffffffULL) return fail(TT_ERR_SHAPE, "too many rows");
+  const int bn = largest_bn_dividing(3 * d_model, d_model <= 128 ? 128 : 256);
+  const int ksw = gemm_ksw(d_model, bn);
+  const int hd = d_model / heads;
+  GemmMaps maps;
+  memset(&maps, 0, sizeof(maps));
+  if (int rc = encode_matrix(&maps.a, normalized, N, d_model, ksw, 128)) return rc;
+  if (int rc = encode_matrix(&maps.w, w_qkv, 3 * d_model, d_model, ksw, bn)) return rc;
+  const bool tma_out = seq % 32 == 0;
+  if (tma_out)
+    if (int rc = encode_qkv_store_maps(&maps.out0, &maps.out1, &maps.out2, q, k, vt, batch * heads, seq,
+                                       hd, seq_pad))
+      return rc;
   GemmParams p = base_params(ds);
   p.M = static_cast<int>(N);
   p.N_total = 3 * d_model;
   p.K = d_model;
-  p.bn = r.qkv_bn;
-  p.n_splits = p.N_total / p.bn;
-  p.nst = clamp_nst(ksw, p.bn, p.K, r.qkv_nst);
+  p.bn = bn;
+  p.n_splits = p.N_total / bn;
+  p.nst = clamp_nst(ksw, bn, p.K, 4, EPI_QKV, p.N_total);
+  p.tma_out = tma_out ? 1 : 0;
   p.bias = b_qkv;
   p.q = static_cast<__half*>(q);
   p.k = static_cast<__half*>(k);
   p.vt = static_cast<__half*>(vt);
   p.seq = seq;
   p.heads = heads;
-  p.head_dim = d_model / heads;
+  p.head_dim = hd;
   p.seq_pad = seq_pad;
   p.d_model = d_model;
-  if (N > 0x7fffffffULL) return fail(TT_ERR_SHAPE, "too many rows");
-  return launch_gemm(ksw, EPI_QKV, tmA, tmW, p, static_cast<cudaStream_t>(stream));
+  return launch_gemm(ksw, EPI_QKV, maps, p, ds->sm_count, static_cast<cudaStream_t>(stream));
 }
 
 int tt_causal_attention(const void* q, const void* k, const void* vt, const uint8_t* key_mask,
@@ -666,7 +736,7 @@ int tt_causal_attention(const void* q, const void* k, const void* vt, const uint
   ap.ctx = static_cast<__half*>(ctx);
   ap.err = ds->err;
   ap.timeout_ns = g_timeout_ns.load();
-  return launch_attention(tq, tk, tv, ap, head_dim, static_cast<cudaStream_t>(stream));
+  return launch_attention(tq, tk, tv, ap, head_dim, true, ds->sm_count, static_cast<cudaStream_t>(stream));
 }
 
 int tt_causal_attention_masked_noalloc(const void* q, const void* k, const void* vt,
@@ -709,7 +779,7 @@ int tt_causal_attention_masked_noalloc(const void* q, const void* k, const void*
   ap.ctx = static_cast<__half*>(ctx);
   ap.err = ds->err;
   ap.timeout_ns = g_timeout_ns.load();
-  return launch_attention(tq, tk, tv, ap, head_dim, s);
+  return launch_attention(tq, tk, tv, ap, head_dim, true, ds->sm_count, s);
 }
 
 int tt_linear_residual_layernorm(const void* a, const void* w, const float* bias,
@@ -725,27 +795,28 @@ int tt_linear_residual_layernorm(const void* a, const void* w, const float* bias
     return fail(TT_ERR_SHAPE, "invalid n_rows/k_in (%lld, %d)", (long long)n_rows, k_in);
   if (d_model % 32 != 0 || d_model <= 0 || (d_model > 256 && d_model != 512))
     return fail(TT_ERR_UNSUPPORTED, "d_model %d must be a multiple of 32, <= 256, or 512", d_model);
-  const int ksw = ksw_for(k_in);
-  CUtensorMap tmA, tmW;
-  if (int rc = encode_matrix(&tmA, a, n_rows, k_in, ksw, 128)) return rc;
-  if (int rc = encode_matrix(&tmW, w, d_model, k_in, ksw, d_model > 256 ? 256 : d_model)) return rc;
+  const int ksw = gemm_ksw(k_in, d_model);
+  GemmMaps maps;
+  memset(&maps, 0, sizeof(maps));
+  if (int rc = encode_matrix(&maps.a, a, n_rows, k_in, ksw, 128)) return rc;
+  if (int rc = encode_matrix(&maps.w, w, d_model, k_in, ksw, d_model > 256 ? 256 : d_model)) return rc;
+  if (int rc = encode_epi_tile(&maps.out0, resid_out, n_rows, d_model, true)) return rc;
+  if (int rc = encode_epi_tile(&maps.out1, norm_out, n_rows, d_model, norm_out_is_f16 == 0)) return rc;
+  if (int rc = encode_epi_tile(&maps.res, resid_in, n_rows, d_model, true)) return rc;
   GemmParams p = base_params(ds);
   p.M = static_cast<int>(n_rows);
   p.N_total = d_model;
   p.K = k_in;
   p.bn = d_model;
   p.n_splits = 1;
-  p.nst = clamp_nst(ksw, p.bn, p.K, 4);
+  p.nst = clamp_nst(ksw, p.bn, p.K, 4, EPI_RESID_LN, p.N_total);
   p.bias = bias;
-  p.resid_in = resid_in;
-  p.resid_out = resid_out;
   p.gamma = gamma;
   p.beta = beta;
-  p.norm_out = norm_out;
   p.norm_f16 = norm_out_is_f16 ? 1 : 0;
   p.eps = eps;
   p.row_mask = row_mask;
-  return launch_gemm(ksw, EPI_RESID_LN, tmA, tmW, p, static_cast<cudaStream_t>(stream));
+  return launch_gemm(ksw, EPI_RESID_LN, maps, p, ds->sm_count, static_cast<cudaStream_t>(stream));
 }
 
 int tt_linear_gelu(const void* a, const void* w, const float* bias, void* out, int64_t n_rows,
@@ -757,20 +828,21 @@ int tt_linear_gelu(const void* a, const void* w, const float* bias, void* out, i
     return fail(TT_ERR_SHAPE, "invalid sizes");
   const int bn = largest_bn_dividing(n_out, 256);
   if (bn == 0) return fail(TT_ERR_UNSUPPORTED, "n_out %d", n_out);
-  const int ksw = ksw_for(k_in);
-  CUtensorMap tmA, tmW;
-  if (int rc = encode_matrix(&tmA, a, n_rows, k_in, ksw, 128)) return rc;
-  if (int rc = encode_matrix(&tmW, w, n_out, k_in, ksw, bn)) return rc;
+  const int ksw = gemm_ksw(k_in, bn);
+  GemmMaps maps;
+  memset(&maps, 0, sizeof(maps));
+  if (int rc = encode_matrix(&maps.a, a, n_rows, k_in, ksw, 128)) return rc;
+  if (int rc = encode_matrix(&maps.w, w, n_out, k_in, ksw, bn)) return rc;
+  if (int rc = encode_epi_tile(&maps.out0, out, n_rows, n_out, false)) return rc;
   GemmParams p = base_params(ds);
   p.M = static_cast<int>(n_rows);
   p.N_total = n_out;
   p.K = k_in;
   p.bn = bn;
   p.n_splits = n_out / bn;
-  p.nst = clamp_nst(ksw, bn, k_in, 4);
+  p.nst = clamp_nst(ksw, bn, k_in, 4, EPI_GELU, n_out);
   p.bias = bias;
-  p.act_out = static_cast<__half*>(out);
-  return launch_gemm(ksw, EPI_GELU, tmA, tmW, p, static_cast<cudaStream_t>(stream));
+  return launch_gemm(ksw, EPI_GELU, maps, p, ds->sm_count, static_cast<cudaStream_t>(stream));
 }
 
 int tt_route_describe(int d_model, int heads, int seq, int ffn, char* buf, int buflen) {
@@ -779,8 +851,9 @@ int tt_route_describe(int d_model, int heads, int seq, int ffn, char* buf, int b
   if (buf && buflen > 0)
     snprintf(buf, buflen,
              "route=%s qkv_bn=%d qkv_nst=%d out_nst=%d ffn=split ffn_in_bn=%d ffn_in_nst=%d "
-             "ffn_out_nst=%d attn_tile=128x128",
-             r.name, r.qkv_bn, r.qkv_nst, r.out_nst, r.ffn_in_bn, r.ffn_in_nst, r.ffn_out_nst);
+             "ffn_out_nst=%d attn_tile=128x128 attn_exp=%s",
+             r.name, r.qkv_bn, r.qkv_nst, r.out_nst, r.ffn_in_bn, r.ffn_in_nst, r.ffn_out_nst,
+             r.attn_exp16 ? "f16x2" : "f32");
   return TT_OK;
 }
 
@@ -854,18 +927,19 @@ int tt_model_forward(tt_model* m, const float* x, const uint8_t* mask, float* ou
   if (int rc = bind_workspace(m, batch, seq, workspace, s)) return rc;
   const Route& r = m->route;
   uint8_t* base = static_cast<uint8_t*>(workspace);
-  float* resid = reinterpret_cast<float*>(base + w.resid);
   __half* norm = reinterpret_cast<__half*>(base + w.norm);
   __half* qb = reinterpret_cast<__half*>(base + w.q);
   __half* kb = reinterpret_cast<__half*>(base + w.k);
   __half* vtb = reinterpret_cast<__half*>(base + w.vt);
   __half* ctx = reinterpret_cast<__half*>(base + w.ctx);
-  __half* hidden = reinterpret_cast<__half*>(base + w.hidden);
   int* kv_end = reinterpret_cast<int*>(base + w.kv_end);
   const int N = static_cast<int>(Nll);
   const int D = m->D, F = m->F, H = m->H, hd = D / H;
-  const int ksw_d = ksw_for(D), ksw_f = ksw_for(F);
   cudaEvent_t ev = nullptr;
+  // Per-call maps: the caller's input (residual of layer 0) and output.
+  CUtensorMap tm_x, tm_out;
+  if (int rc = encode_epi_tile(&tm_x, x, Nll, D, true)) return rc;
+  if (int rc = encode_epi_tile(&tm_out, out, Nll, D, true)) return rc;
 
   if (mask) {
     if (int rc = record_begin(m, s, &ev)) return rc;
@@ -890,6 +964,7 @@ int tt_model_forward(tt_model* m, const float* x, const uint8_t* mask, float* ou
   ap.err = ds->err;
   ap.timeout_ns = g_timeout_ns.load();
 
+  GemmMaps maps;
   for (int l = 0; l < m->L; ++l) {
     const tt_layer_weights& lw = m->layers[l];
     const bool last = (l == m->L - 1);
@@ -901,7 +976,8 @@ int tt_model_forward(tt_model* m, const float* x, const uint8_t* mask, float* ou
       p.K = D;
       p.bn = r.qkv_bn;
       p.n_splits = p.N_total / p.bn;
-      p.nst = clamp_nst(ksw_d, p.bn, D, r.qkv_nst);
+      p.nst = clamp_nst(m->ksw_qkv, p.bn, D, r.qkv_nst, EPI_QKV, p.N_total);
+      p.tma_out = (seq % 32 == 0) ? 1 : 0;
       p.bias = lw.b_qkv;
       p.q = qb;
       p.k = kb;
@@ -911,13 +987,19 @@ int tt_model_forward(tt_model* m, const float* x, const uint8_t* mask, float* ou
       p.head_dim = hd;
       p.seq_pad = w.seq_pad;
       p.d_model = D;
+      maps.a = m->tm_norm;
+      maps.w = m->tm_wqkv[l];
+      maps.out0 = m->tm_q_st;
+      maps.out1 = m->tm_k_st;
+      maps.out2 = m->tm_vt_st;
       if (int rc = record_begin(m, s, &ev)) return rc;
-      if (int rc = launch_gemm(ksw_d, EPI_QKV, m->tm_norm, m->tm_wqkv[l], p, s)) return rc;
+      if (int rc = launch_gemm(m->ksw_qkv, EPI_QKV, maps, p, ds->sm_count, s)) return rc;
       if (int rc = record_end(m, s, TT_KERNEL_QKV, ev)) return rc;
     }
     // Attention
     if (int rc = record_begin(m, s, &ev)) return rc;
-    if (int rc = launch_attention(m->tm_q, m->tm_k, m->tm_vt, ap, hd, s)) return rc;
+    if (int rc = launch_attention(m->tm_q, m->tm_k, m->tm_vt, ap, hd, r.attn_exp16 != 0, ds->sm_count, s))
+      return rc;
     if (int rc = record_end(m, s, TT_KERNEL_ATTN, ev)) return rc;
     // Output projection + residual + norm2
     {
@@ -927,18 +1009,20 @@ int tt_model_forward(tt_model* m, const float* x, const uint8_t* mask, float* ou
       p.K = D;
       p.bn = D;
       p.n_splits = 1;
-      p.nst = clamp_nst(ksw_d, D, D, r.out_nst);
+      p.nst = clamp_nst(m->ksw_out, D, D, r.out_nst, EPI_RESID_LN, D);
       p.bias = lw.b_out;
-      p.resid_in = (l == 0) ? x : resid;
-      p.resid_out = resid;
       p.gamma = lw.ln_attn_w;
       p.beta = lw.ln_attn_b;
-      p.norm_out = norm;
       p.norm_f16 = 1;
       p.eps = m->eps;
       p.row_mask = nullptr;
+      maps.a = m->tm_ctx;
+      maps.w = m->tm_wout[l];
+      maps.out0 = m->tm_resid;
+      maps.out1 = m->tm_norm_st;
+      maps.res = (l == 0) ? tm_x : m->tm_resid;
       if (int rc = record_begin(m, s, &ev)) return rc;
-      if (int rc = launch_gemm(ksw_d, EPI_RESID_LN, m->tm_ctx, m->tm_wout[l], p, s)) return rc;
+      if (int rc = launch_gemm(m->ksw_out, EPI_RESID_LN, maps, p, ds->sm_count, s)) return rc;
       if (int rc = record_end(m, s, TT_KERNEL_OUT_LN, ev)) return rc;
     }
     // FFN in + GELU
@@ -949,11 +1033,13 @@ int tt_model_forward(tt_model* m, const float* x, const uint8_t* mask, float* ou
       p.K = D;
       p.bn = r.ffn_in_bn;
       p.n_splits = F / p.bn;
-      p.nst = clamp_nst(ksw_d, p.bn, D, r.ffn_in_nst);
+      p.nst = clamp_nst(m->ksw_in, p.bn, D, r.ffn_in_nst, EPI_GELU, F);
       p.bias = lw.b_ffn_in;
-      p.act_out = hidden;
+      maps.a = m->tm_norm;
+      maps.w = m->tm_win[l];
+      maps.out0 = m->tm_hidden_st;
       if (int rc = record_begin(m, s, &ev)) return rc;
-      if (int rc = launch_gemm(ksw_d, EPI_GELU, m->tm_norm, m->tm_win[l], p, s)) return rc;
+      if (int rc = launch_gemm(m->ksw_in, EPI_GELU, maps, p, ds->sm_count, s)) return rc;
       if (int rc = record_end(m, s, TT_KERNEL_FFN_IN, ev)) return rc;
     }
     // FFN out + residual + next norm (final_norm -> FP32 model output on the last layer)
@@ -964,18 +1050,20 @@ int tt_model_forward(tt_model* m, const float* x, const uint8_t* mask, float* ou
       p.K = F;
       p.bn = D;
       p.n_splits = 1;
-      p.nst = clamp_nst(ksw_f, D, F, r.ffn_out_nst);
+      p.nst = clamp_nst(m->ksw_out2, D, F, r.ffn_out_nst, EPI_RESID_LN, D);
       p.bias = lw.b_ffn_out;
-      p.resid_in = resid;
-      p.resid_out = resid;
       p.gamma = lw.ln_next_w;
       p.beta = lw.ln_next_b;
-      p.norm_out = last ? static_cast<void*>(out) : static_cast<void*>(norm);
       p.norm_f16 = last ? 0 : 1;
       p.eps = m->eps;
       p.row_mask = last ? mask : nullptr;
+      maps.a = m->tm_hidden;
+      maps.w = m->tm_wout2[l];
+      maps.out0 = m->tm_resid;
+      maps.out1 = last ? tm_out : m->tm_norm_st;
+      maps.res = m->tm_resid;
       if (int rc = record_begin(m, s, &ev)) return rc;
-      if (int rc = launch_gemm(ksw_f, EPI_RESID_LN, m->tm_hidden, m->tm_wout2[l], p, s)) return rc;
+      if (int rc = launch_gemm(m->ksw_out2, EPI_RESID_LN, maps, p, ds->sm_count, s)) return rc;
       if (int rc = record_end(m, s, TT_KERNEL_FFN_OUT_LN, ev)) return rc;
     }
   }

@@ -7,15 +7,25 @@
 // `_mixed_linear_add_layer_norm_kernel`) and the cuBLAS nn.Linear route of the
 // generic configurations (mixed_precision/transformer.py:138-139, 669-677).
 //
-// One CTA owns 128 rows and `bn` output columns (bn <= 256, or 512 as two
-// 256-column UMMAs).  Roles: warp 4 streams (A, W) K-blocks with TMA through
-// an `nst`-deep ring, warp 5 allocates TMEM and issues tcgen05.mma, warps 0..3
-// drain the FP32 accumulator (one row per thread) through an epilogue:
-//   EPI_QKV       + bias, FP16, scattered to Q/K [B,H,S,hd] and V^T [B,H,hd,S_pad]
-//   EPI_RESID_LN  + bias + FP32 residual -> residual out (FP32), then the
-//                 two-pass FP32 LayerNorm of the row -> FP16 or FP32
-//                 (optionally zeroing rows whose mask byte is 0)
+// Persistent kernel.  A work item is (128-row M tile, `bn`-column split);
+// CTA c takes items c, c + gridDim.x, ...  Roles:
+//   warp 4      TMA producer: (A, W) K-blocks through an `nst`-deep ring that
+//               runs continuously across items
+//   warp 5      TMEM allocator and single-thread tcgen05.mma issuer; the FP32
+//               accumulator is double buffered in TMEM (bn <= 256), so the
+//               MMAs of item i+1 overlap the epilogue of item i
+//   warps 0..3  epilogue: warp e owns rows 32e..32e+31 of the tile, one row
+//               per thread (TMEM lane = row), in 32-column chunks:
+//   EPI_QKV       + bias, FP16, to Q/K [B*H, S, hd] and V^T [B*H, hd, S_pad]
+//   EPI_RESID_LN  + bias + FP32 residual -> residual out (FP32), then a
+//                 two-pass FP32 LayerNorm of the row (the row is kept in
+//                 TMEM between passes) -> FP16 or FP32, optionally zeroing
+//                 rows whose mask byte is 0
 //   EPI_GELU      + bias, exact-erf GELU in FP32, FP16 out
+// Epilogue inputs (the residual) arrive by TMA into a per-warp ring of
+// [32 rows x 32 col] tiles; outputs are staged in swizzled shared tiles and
+// written by TMA bulk stores, so HBM sees whole lines in both directions.
+// When S is not a multiple of 32 the QKV epilogue falls back to direct stores.
 #pragma once
 
 #include "tt_ptx.cuh"
@@ -24,11 +34,18 @@ namespace tt {
 
 enum GemmEpilogue : int { EPI_QKV = 0, EPI_RESID_LN = 1, EPI_GELU = 2 };
 
+constexpr int kGemmMaxStages = 8;
+constexpr int kResRing = 2;   // residual tiles in flight per epilogue warp
+constexpr int kOutRing = 2;   // output staging tiles per epilogue warp
+constexpr int kEpiTile = 4096;  // one [32 x 32] FP32 tile
+
 struct GemmParams {
   int M, N_total, K;
-  int bn;        // output columns per CTA
+  int bn;        // output columns per item
   int n_splits;  // N_total / bn
   int nst;       // pipeline depth
+  int n_items;   // ceil(M / 128) * n_splits
+  int tma_out;   // QKV only: 1 = TMA stores (requires seq % 32 == 0)
   const float* bias;  // [N_total]
   // EPI_QKV
   __half* q;
@@ -36,41 +53,124 @@ struct GemmParams {
   __half* vt;
   int seq, heads, head_dim, seq_pad, d_model;
   // EPI_RESID_LN
-  const float* resid_in;
-  float* resid_out;
   const float* gamma;
   const float* beta;
-  void* norm_out;
   int norm_f16;
   float eps;
   const uint8_t* row_mask;
-  // EPI_GELU
-  __half* act_out;
   unsigned int* err;
   unsigned long long timeout_ns;
 };
 
-constexpr int kGemmMaxStages = 8;
+// Tensor maps of one GEMM launch.  `a`, `w`: operands (box {KSW, 128} and
+// {KSW, min(bn, 256)}).  Outputs/inputs of the epilogue, box 32 x 32:
+//   EPI_QKV       out0 = Q, out1 = K   [B*H, S, hd],   box {min(hd,32), 32, 1}
+//                 out2 = V^T [B*H, hd, S_pad],          box {32, min(hd,32), 1}
+//   EPI_RESID_LN  out0 = residual out (FP32), out1 = normalized (FP16/FP32),
+//                 res  = residual in (FP32)
+//   EPI_GELU      out0 = activation (FP16)
+struct GemmMaps {
+  CUtensorMap a, w, out0, out1, out2, res;
+};
 
 __host__ __device__ inline int gemm_stage_bytes(int ksw, int bn) { return (128 + bn) * ksw * 2; }
-__host__ __device__ inline int gemm_tmem_cols(int bn) {
+__host__ __device__ inline int gemm_acc_stride(int bn) {
   int c = 32;
   while (c < bn) c <<= 1;
   return c;
 }
-// Offsets: stages (1024-aligned) | bias[bn] | gamma[bn] | beta[bn] | barriers | misc
-__host__ __device__ inline int gemm_smem_bytes(int ksw, int bn, int nst) {
+__host__ __device__ inline int gemm_n_acc(int bn) { return bn <= 256 ? 2 : 1; }
+__host__ __device__ inline int gemm_tmem_cols(int bn) { return gemm_n_acc(bn) * gemm_acc_stride(bn); }
+__host__ __device__ inline int gemm_epi_bytes(int epi) {
+  return 4 * ((epi == EPI_RESID_LN ? kResRing : 0) + kOutRing) * kEpiTile;
+}
+// Layout: stages | epilogue tiles | bias[N_total], gamma[bn], beta[bn] | barriers | misc
+// (+1024 alignment slack)
+__host__ __device__ inline int gemm_smem_bytes(int ksw, int bn, int nst, int epi, int n_total) {
   int off = nst * gemm_stage_bytes(ksw, bn);
-  off += 3 * bn * 4;
-  off += (2 * kGemmMaxStages + 2) * 8;
+  off += gemm_epi_bytes(epi);
+  off += (n_total + 2 * bn) * 4;
+  off += (2 * kGemmMaxStages + 4 + 4 * kResRing + 1) * 8;
   off += 16;
   return off + 1024;
 }
 
+// ---- shared-tile helpers (swizzle patterns match the TMA swizzle modes) ----
+// [32 rows x 32 FP32], 128-byte rows, SWIZZLE_128B.
+__device__ __forceinline__ void stage_row_f32(uint32_t tile, int r, const float* v) {
+  const uint32_t base = tile + r * 128;
+#pragma unroll
+  for (int c = 0; c < 8; ++c)
+    st_shared_v4(base + ((c ^ (r & 7)) << 4), __float_as_uint(v[4 * c]), __float_as_uint(v[4 * c + 1]),
+                 __float_as_uint(v[4 * c + 2]), __float_as_uint(v[4 * c + 3]));
+}
+
+__device__ __forceinline__ void load_row_f32(uint32_t tile, int r, float* v) {
+  const uint32_t base = tile + r * 128;
+#pragma unroll
+  for (int c = 0; c < 8; ++c) {
+    uint32_t a, b, d, e;
+    asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(a), "=r"(b), "=r"(d), "=r"(e)
+                 : "r"(base + ((c ^ (r & 7)) << 4)));
+    v[4 * c] = __uint_as_float(a);
+    v[4 * c + 1] = __uint_as_float(b);
+    v[4 * c + 2] = __uint_as_float(d);
+    v[4 * c + 3] = __uint_as_float(e);
+  }
+}
+
+// [32 rows x 32 FP16], 64-byte rows, SWIZZLE_64B.
+__device__ __forceinline__ void stage_row_f16x32(uint32_t tile, int r, const float* v) {
+  const uint32_t base = tile + r * 64;
+#pragma unroll
+  for (int c = 0; c < 4; ++c)
+    st_shared_v4(base + ((c ^ ((r >> 1) & 3)) << 4), pack_half2(v[8 * c], v[8 * c + 1]),
+                 pack_half2(v[8 * c + 2], v[8 * c + 3]), pack_half2(v[8 * c + 4], v[8 * c + 5]),
+                 pack_half2(v[8 * c + 6], v[8 * c + 7]));
+}
+
+// [32 rows x 16 FP16], 32-byte rows, SWIZZLE_32B.
+__device__ __forceinline__ void stage_row_f16x16(uint32_t tile, int r, const float* v) {
+  const uint32_t base = tile + r * 32;
+#pragma unroll
+  for (int c = 0; c < 2; ++c)
+    st_shared_v4(base + ((c ^ ((r >> 2) & 1)) << 4), pack_half2(v[8 * c], v[8 * c + 1]),
+                 pack_half2(v[8 * c + 2], v[8 * c + 3]), pack_half2(v[8 * c + 4], v[8 * c + 5]),
+                 pack_half2(v[8 * c + 6], v[8 * c + 7]));
+}
+
+// Column s of a [w rows x 32 FP16] tile (64-byte rows, SWIZZLE_64B): v[d] -> (d, s).
+__device__ __forceinline__ void stage_col_f16(uint32_t tile, int s, const float* v, int w) {
+  for (int d = 0; d < w; ++d) {
+    const uint32_t addr = tile + d * 64 + ((((s >> 3) ^ ((d >> 1) & 3))) << 4) + (s & 7) * 2;
+    const unsigned short h = __half_as_ushort(__float2half_rn(v[d]));
+    asm volatile("st.shared.u16 [%0], %1;" ::"r"(addr), "h"(h) : "memory");
+  }
+}
+
+// Output staging ring of one epilogue warp: before a slot is rewritten, the
+// bulk store that last read it must be done reading shared memory.
+struct OutRing {
+  uint32_t base;  // shared address of slot 0
+  int count;      // slots used so far
+  __device__ __forceinline__ uint32_t acquire(int lane) {
+    if (lane == 0) bulk_wait_group_read<kOutRing - 1>();
+    __syncwarp();
+    return base + (count % kOutRing) * kEpiTile;
+  }
+  // All lanes wrote the slot with generic stores; make them visible to the
+  // async proxy before lane 0 issues the TMA store(s).
+  __device__ __forceinline__ void publish() {
+    fence_proxy_async_smem();
+    __syncwarp();
+    ++count;
+  }
+};
+
 template <int KSW, int EPI>
 __global__ void __launch_bounds__(192, 1)
-    gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmW,
-                const GemmParams p) {
+    gemm_kernel(const __grid_constant__ GemmMaps maps, const GemmParams p) {
   constexpr int A_BYTES = 128 * KSW * 2;
   constexpr uint32_t kSw = swizzle_kind_for_bytes(KSW * 2);
   constexpr uint32_t kSbo = 8 * KSW * 2;
@@ -80,22 +180,23 @@ __global__ void __launch_bounds__(192, 1)
   const int bn = p.bn, nst = p.nst;
   const int stage_bytes = gemm_stage_bytes(KSW, bn);
   const int w_bytes_half = (bn > 256 ? 256 : bn) * KSW * 2;
-  float* s_bias = reinterpret_cast<float*>(smem + nst * stage_bytes);
-  float* s_gamma = s_bias + bn;
+  uint8_t* epi = smem + nst * stage_bytes;
+  float* s_bias = reinterpret_cast<float*>(epi + gemm_epi_bytes(EPI));  // [N_total]
+  float* s_gamma = s_bias + p.N_total;                                    // [bn] (RESID_LN)
   float* s_beta = s_gamma + bn;
   uint64_t* full = reinterpret_cast<uint64_t*>(s_beta + bn);
   uint64_t* empty = full + kGemmMaxStages;
   uint64_t* acc_full = empty + kGemmMaxStages;
-  uint64_t* done = acc_full + 1;
+  uint64_t* acc_empty = acc_full + 2;
+  uint64_t* res_full = acc_empty + 2;  // [4 warps][kResRing]
+  uint64_t* done = res_full + 4 * kResRing;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int m_tile = blockIdx.x / p.n_splits;
-  const int split = blockIdx.x - m_tile * p.n_splits;
-  const int m0 = m_tile * 128;
-  const int n0 = split * bn;
   const int nk = p.K / KSW;
+  const int n_acc = gemm_n_acc(bn);
+  const int acc_stride = gemm_acc_stride(bn);
   const uint32_t tmem_cols = static_cast<uint32_t>(gemm_tmem_cols(bn));
 
   if (threadIdx.x == 0) {
@@ -103,18 +204,20 @@ __global__ void __launch_bounds__(192, 1)
       mbar_init(&full[i], 1);
       mbar_init(&empty[i], 1);
     }
-    mbar_init(acc_full, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&acc_full[i], 1);
+      mbar_init(&acc_empty[i], 4);
+    }
+    for (int i = 0; i < 4 * kResRing; ++i) mbar_init(&res_full[i], 1);
     mbar_init(done, 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
-  if (threadIdx.x < 128) {
-    for (int c = threadIdx.x; c < bn; c += 128) {
-      s_bias[c] = p.bias[n0 + c];
-      if constexpr (EPI == EPI_RESID_LN) {
-        s_gamma[c] = p.gamma[n0 + c];
-        s_beta[c] = p.beta[n0 + c];
-      }
+  for (int c = threadIdx.x; c < p.N_total; c += blockDim.x) s_bias[c] = p.bias[c];
+  if constexpr (EPI == EPI_RESID_LN) {
+    for (int c = threadIdx.x; c < bn; c += blockDim.x) {
+      s_gamma[c] = p.gamma[c];
+      s_beta[c] = p.beta[c];
     }
   }
   if (warp == 5) {
@@ -128,208 +231,295 @@ __global__ void __launch_bounds__(192, 1)
   const Watchdog wd{p.err, abort_flag, p.timeout_ns};
 
   if (warp == 4) {
+    // ------------------------------------------------------------ producer
     if (lane == 0) {
-      tma_prefetch_desc(&tmA);
-      tma_prefetch_desc(&tmW);
-      int issued = 0;
-      for (int kb = 0; kb < nk; ++kb) {
-        const int st = kb % nst;
-        if (!wait_phase(&empty[st], ((kb / nst) & 1) ^ 1, wd, 0x401)) break;
-        uint8_t* sa = smem + st * stage_bytes;
-        uint8_t* sw = sa + A_BYTES;
-        mbar_arrive_expect_tx(&full[st], stage_bytes);
-        tma_load_2d(sa, &tmA, &full[st], kb * KSW, m0);
-        tma_load_2d(sw, &tmW, &full[st], kb * KSW, n0);
-        if (bn > 256) tma_load_2d(sw + w_bytes_half, &tmW, &full[st], kb * KSW, n0 + 256);
-        issued = kb + 1;
+      tma_prefetch_desc(&maps.a);
+      tma_prefetch_desc(&maps.w);
+      int g = 0;
+      bool ok = true;
+      for (int w = blockIdx.x; ok && w < p.n_items; w += gridDim.x) {
+        const int m0 = (w / p.n_splits) * 128;
+        const int n0 = (w % p.n_splits) * bn;
+        for (int kb = 0; kb < nk; ++kb, ++g) {
+          const int st = g % nst;
+          if (!(ok = wait_phase(&empty[st], ((g / nst) & 1) ^ 1, wd, 0x401))) break;
+          uint8_t* sa = smem + st * stage_bytes;
+          uint8_t* sw = sa + A_BYTES;
+          mbar_arrive_expect_tx(&full[st], stage_bytes);
+          tma_load_2d(sa, &maps.a, &full[st], kb * KSW, m0);
+          tma_load_2d(sw, &maps.w, &full[st], kb * KSW, n0);
+          if (bn > 256) tma_load_2d(sw + w_bytes_half, &maps.w, &full[st], kb * KSW, n0 + 256);
+        }
       }
-      for (int kb = (issued > nst ? issued - nst : 0); kb < issued; ++kb)
-        wait_drain(&full[kb % nst], (kb / nst) & 1, kDrainLimitNs);
+      for (int i = (g > nst ? g - nst : 0); i < g; ++i)
+        wait_drain(&full[i % nst], (i / nst) & 1, kDrainLimitNs);
     }
   } else if (warp == 5) {
+    // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
       const uint32_t idesc = umma_idesc_f16_f32(128, bn > 256 ? 256 : bn);
       const uint32_t base = smem_u32(smem);
+      int g = 0, i = 0;
       bool ok = true;
-      for (int kb = 0; kb < nk; ++kb) {
-        const int st = kb % nst;
-        if (!(ok = wait_phase(&full[st], (kb / nst) & 1, wd, 0x402))) break;
+      for (int w = blockIdx.x; ok && w < p.n_items; w += gridDim.x, ++i) {
+        const int ab = i % n_acc;
+        if (!(ok = wait_phase(&acc_empty[ab], ((i / n_acc) & 1) ^ 1, wd, 0x403))) break;
         tc_fence_after();
-        const uint32_t sa = base + st * stage_bytes;
-        const uint32_t sw = sa + A_BYTES;
+        const uint32_t tacc = tmem_base + ab * acc_stride;
+        for (int kb = 0; kb < nk; ++kb, ++g) {
+          const int st = g % nst;
+          if (!(ok = wait_phase(&full[st], (g / nst) & 1, wd, 0x402))) break;
+          tc_fence_after();
+          const uint32_t sa = base + st * stage_bytes;
+          const uint32_t sw = sa + A_BYTES;
 #pragma unroll
-        for (int kk = 0; kk < KSW / 16; ++kk) {
-          const uint64_t da = umma_sdesc(sa + kk * 32, kSbo, kSw);
-          const uint32_t acc = (kb > 0 || kk > 0) ? 1u : 0u;
-          umma_f16(tmem_base, da, umma_sdesc(sw + kk * 32, kSbo, kSw), idesc, acc);
-          if (bn > 256)
-            umma_f16(tmem_base + 256, da, umma_sdesc(sw + w_bytes_half + kk * 32, kSbo, kSw), idesc,
-                     acc);
+          for (int kk = 0; kk < KSW / 16; ++kk) {
+            const uint64_t da = umma_sdesc(sa + kk * 32, kSbo, kSw);
+            const uint32_t acc = (kb > 0 || kk > 0) ? 1u : 0u;
+            umma_f16(tacc, da, umma_sdesc(sw + kk * 32, kSbo, kSw), idesc, acc);
+            if (bn > 256)
+              umma_f16(tacc + 256, da, umma_sdesc(sw + w_bytes_half + kk * 32, kSbo, kSw), idesc, acc);
+          }
+          umma_commit(&empty[st]);
         }
-        umma_commit(&empty[st]);
+        if (ok) umma_commit(&acc_full[ab]);
       }
-      if (ok) umma_commit(acc_full);
       umma_commit(done);
       wait_drain(done, 0, kDrainLimitNs);
     }
   } else {
     // ------------------------------------------------------------ epilogue
-    const int r = threadIdx.x;
-    const int row = m0 + r;
-    const bool valid = row < p.M;
-    const uint32_t taddr = tmem_base + (static_cast<uint32_t>(warp * 32) << 16);
-    if (warp_wait_phase(acc_full, 0, wd, 0x403)) {
+    const int r = lane;  // row within this warp's 32-row slab
+    const uint32_t lane_base = static_cast<uint32_t>(warp * 32) << 16;
+    constexpr int kRes = (EPI == EPI_RESID_LN) ? kResRing : 0;
+    const uint32_t res_base = smem_u32(epi) + warp * (kRes + kOutRing) * kEpiTile;
+    OutRing ring{res_base + kRes * kEpiTile, 0};
+    uint64_t* my_res_full = res_full + warp * kResRing;
+    int res_g = 0;  // residual tiles this warp has requested and consumed
+    int i = 0;
+    bool ok = true;
+    for (int w = blockIdx.x; ok && w < p.n_items; w += gridDim.x, ++i) {
+      const int m0 = (w / p.n_splits) * 128;
+      const int n0 = (w % p.n_splits) * bn;
+      const int r0 = m0 + warp * 32;  // first row of this warp's slab
+      const int row = r0 + r;
+      const bool valid = row < p.M;
+      const bool warp_active = r0 < p.M;
+      const int nch = bn / 32;
+      // Residual tiles of this item: the first kResRing go out now.
+      if constexpr (EPI == EPI_RESID_LN) {
+        if (lane == 0 && warp_active) {
+          for (int c = 0; c < nch && c < kResRing; ++c) {
+            const int q = res_g + c;
+            mbar_arrive_expect_tx(&my_res_full[q % kResRing], kEpiTile);
+            tma_load_2d_u32(res_base + (q % kResRing) * kEpiTile, &maps.res, &my_res_full[q % kResRing],
+                            n0 + 32 * c, r0);
+          }
+        }
+      }
+      const int ab = i % n_acc;
+      if (!(ok = warp_wait_phase(&acc_full[ab], (i / n_acc) & 1, wd, 0x404))) break;
       tc_fence_after();
+      const uint32_t taddr = tmem_base + lane_base + ab * acc_stride;
+
       if constexpr (EPI == EPI_QKV) {
         const int D = p.d_model, hd = p.head_dim;
         const int bidx = valid ? row / p.seq : 0;
         const int s = valid ? row - bidx * p.seq : 0;
-        for (int c = 0; c < bn; c += 32) {
+        const int b_w = warp_active ? r0 / p.seq : 0;
+        const int s0 = warp_active ? r0 - b_w * p.seq : 0;
+        const int wbox = hd < 32 ? hd : 32;  // columns per sub-box
+        for (int c = 0; c < nch; ++c) {
           uint32_t v[32];
           __syncwarp();
-          tmem_ld_x32(taddr + c, v);
+          tmem_ld_x32(taddr + c * 32, v);
           tmem_ld_wait();
-          if (!valid) continue;
-          const int col0 = n0 + c;
-          const int which = col0 / D;
-          const int within0 = col0 - which * D;
+          const int col0 = n0 + c * 32;
           float f[32];
 #pragma unroll
-          for (int i = 0; i < 32; ++i) f[i] = __uint_as_float(v[i]) + s_bias[c + i];
-          if (which < 2) {
-            __half* base = which == 0 ? p.q : p.k;
-#pragma unroll
-            for (int g = 0; g < 2; ++g) {
-              const int within = within0 + 16 * g;
-              const int hh = within / hd, d = within - hh * hd;
-              uint4* dst = reinterpret_cast<uint4*>(
-                  base + ((static_cast<size_t>(bidx) * p.heads + hh) * p.seq + s) * hd + d);
-              uint4 a, bq;
-              a.x = pack_half2(f[16 * g + 0], f[16 * g + 1]);
-              a.y = pack_half2(f[16 * g + 2], f[16 * g + 3]);
-              a.z = pack_half2(f[16 * g + 4], f[16 * g + 5]);
-              a.w = pack_half2(f[16 * g + 6], f[16 * g + 7]);
-              bq.x = pack_half2(f[16 * g + 8], f[16 * g + 9]);
-              bq.y = pack_half2(f[16 * g + 10], f[16 * g + 11]);
-              bq.z = pack_half2(f[16 * g + 12], f[16 * g + 13]);
-              bq.w = pack_half2(f[16 * g + 14], f[16 * g + 15]);
-              dst[0] = a;
-              dst[1] = bq;
+          for (int e = 0; e < 32; ++e) f[e] = __uint_as_float(v[e]) + s_bias[col0 + e];
+          const int which = col0 / D;
+          const int within0 = col0 - which * D;
+          if (p.tma_out) {
+            if (!warp_active) continue;
+            const uint32_t slot = ring.acquire(lane);
+            const int nsub = 32 / wbox;
+            for (int sb = 0; sb < nsub; ++sb) {
+              const uint32_t sub = slot + sb * 1024;
+              if (which < 2) {
+                if (wbox == 32)
+                  stage_row_f16x32(sub, r, f);
+                else
+                  stage_row_f16x16(sub, r, f + sb * 16);
+              } else {
+                stage_col_f16(sub, r, f + sb * wbox, wbox);
+              }
             }
-          } else {
+            ring.publish();
+            if (lane == 0) {
+              for (int sb = 0; sb < nsub; ++sb) {
+                const int within = within0 + sb * wbox;
+                const int hh = within / hd, d0 = within - hh * hd;
+                const int bh = b_w * p.heads + hh;
+                const uint32_t sub = slot + sb * 1024;
+                if (which == 0) tma_store_3d(&maps.out0, sub, d0, s0, bh);
+                else if (which == 1) tma_store_3d(&maps.out1, sub, d0, s0, bh);
+                else tma_store_3d(&maps.out2, sub, s0, d0, bh);
+              }
+              bulk_commit_group();
+            }
+          } else if (valid) {
+            if (which < 2) {
+              __half* base = which == 0 ? p.q : p.k;
 #pragma unroll
-            for (int i = 0; i < 32; ++i) {
-              const int within = within0 + i;
-              const int hh = within / hd, d = within - hh * hd;
-              p.vt[((static_cast<size_t>(bidx) * p.heads + hh) * hd + d) * p.seq_pad + s] =
-                  __float2half_rn(f[i]);
+              for (int gq = 0; gq < 2; ++gq) {
+                const int within = within0 + 16 * gq;
+                const int hh = within / hd, d = within - hh * hd;
+                uint4* dst = reinterpret_cast<uint4*>(
+                    base + ((static_cast<size_t>(bidx) * p.heads + hh) * p.seq + s) * hd + d);
+                uint4 a, bq;
+                a.x = pack_half2(f[16 * gq + 0], f[16 * gq + 1]);
+                a.y = pack_half2(f[16 * gq + 2], f[16 * gq + 3]);
+                a.z = pack_half2(f[16 * gq + 4], f[16 * gq + 5]);
+                a.w = pack_half2(f[16 * gq + 6], f[16 * gq + 7]);
+                bq.x = pack_half2(f[16 * gq + 8], f[16 * gq + 9]);
+                bq.y = pack_half2(f[16 * gq + 10], f[16 * gq + 11]);
+                bq.z = pack_half2(f[16 * gq + 12], f[16 * gq + 13]);
+                bq.w = pack_half2(f[16 * gq + 14], f[16 * gq + 15]);
+                dst[0] = a;
+                dst[1] = bq;
+              }
+            } else {
+#pragma unroll
+              for (int e = 0; e < 32; ++e) {
+                const int within = within0 + e;
+                const int hh = within / hd, d = within - hh * hd;
+                p.vt[((static_cast<size_t>(bidx) * p.heads + hh) * hd + d) * p.seq_pad + s] =
+                    __float2half_rn(f[e]);
+              }
             }
           }
         }
       } else if constexpr (EPI == EPI_GELU) {
-        for (int c = 0; c < bn; c += 32) {
+        for (int c = 0; c < nch; ++c) {
           uint32_t v[32];
           __syncwarp();
-          tmem_ld_x32(taddr + c, v);
+          tmem_ld_x32(taddr + c * 32, v);
           tmem_ld_wait();
-          if (!valid) continue;
-          uint4* dst = reinterpret_cast<uint4*>(p.act_out + static_cast<size_t>(row) * p.N_total +
-                                                n0 + c);
+          if (!warp_active) continue;
+          float gl[32];
 #pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            uint4 w;
-            float g[8];
-#pragma unroll
-            for (int e = 0; e < 8; ++e)
-              g[e] = gelu_erf(__uint_as_float(v[8 * i + e]) + s_bias[c + 8 * i + e]);
-            w.x = pack_half2(g[0], g[1]);
-            w.y = pack_half2(g[2], g[3]);
-            w.z = pack_half2(g[4], g[5]);
-            w.w = pack_half2(g[6], g[7]);
-            dst[i] = w;
+          for (int e = 0; e < 32; ++e) gl[e] = gelu_erf(__uint_as_float(v[e]) + s_bias[n0 + c * 32 + e]);
+          const uint32_t slot = ring.acquire(lane);
+          stage_row_f16x32(slot, r, gl);
+          ring.publish();
+          if (lane == 0) {
+            tma_store_2d(&maps.out0, slot, n0 + c * 32, r0);
+            bulk_commit_group();
           }
         }
       } else {
         // EPI_RESID_LN: bn == N_total == d_model (the whole row lives in TMEM).
         const int D = bn;
-        const float* rin = p.resid_in + static_cast<size_t>(valid ? row : 0) * D;
-        float* rout = p.resid_out + static_cast<size_t>(valid ? row : 0) * D;
         float sum = 0.f;
-        for (int c = 0; c < D; c += 32) {
+        for (int c = 0; c < nch; ++c) {
           uint32_t v[32];
           __syncwarp();
-          tmem_ld_x32(taddr + c, v);
+          tmem_ld_x32(taddr + c * 32, v);
           tmem_ld_wait();
-          float4 res[8];
+          float res[32];
+          const int q = res_g + c;
+          if (warp_active) {
+            if (!(ok = warp_wait_phase(&my_res_full[q % kResRing], (q / kResRing) & 1, wd, 0x405)))
+              break;
+            load_row_f32(res_base + (q % kResRing) * kEpiTile, r, res);
+            __syncwarp();
+            // The slot is read; refill it with the tile kResRing chunks ahead.
+            if (lane == 0 && c + kResRing < nch) {
+              fence_proxy_async_smem();
+              const int q2 = q + kResRing;
+              mbar_arrive_expect_tx(&my_res_full[q2 % kResRing], kEpiTile);
+              tma_load_2d_u32(res_base + (q2 % kResRing) * kEpiTile, &maps.res,
+                              &my_res_full[q2 % kResRing], n0 + 32 * (c + kResRing), r0);
+            }
+          } else {
 #pragma unroll
-          for (int i = 0; i < 8; ++i)
-            res[i] = valid ? reinterpret_cast<const float4*>(rin + c)[i] : make_float4(0, 0, 0, 0);
+            for (int e = 0; e < 32; ++e) res[e] = 0.f;
+          }
+          float rr[32];
           uint32_t out[32];
 #pragma unroll
-          for (int i = 0; i < 8; ++i) {
-            float4 t;
-            t.x = __uint_as_float(v[4 * i + 0]) + s_bias[c + 4 * i + 0] + res[i].x;
-            t.y = __uint_as_float(v[4 * i + 1]) + s_bias[c + 4 * i + 1] + res[i].y;
-            t.z = __uint_as_float(v[4 * i + 2]) + s_bias[c + 4 * i + 2] + res[i].z;
-            t.w = __uint_as_float(v[4 * i + 3]) + s_bias[c + 4 * i + 3] + res[i].w;
-            sum += (t.x + t.y) + (t.z + t.w);
-            if (valid) reinterpret_cast<float4*>(rout + c)[i] = t;
-            out[4 * i + 0] = __float_as_uint(t.x);
-            out[4 * i + 1] = __float_as_uint(t.y);
-            out[4 * i + 2] = __float_as_uint(t.z);
-            out[4 * i + 3] = __float_as_uint(t.w);
+          for (int e = 0; e < 32; ++e) {
+            rr[e] = __uint_as_float(v[e]) + s_bias[c * 32 + e] + res[e];
+            out[e] = __float_as_uint(rr[e]);
           }
+#pragma unroll
+          for (int e = 0; e < 32; e += 4) sum += (rr[e] + rr[e + 1]) + (rr[e + 2] + rr[e + 3]);
           __syncwarp();
-          tmem_st_x32(taddr + c, out);
+          tmem_st_x32(taddr + c * 32, out);
+          if (warp_active) {
+            const uint32_t slot = ring.acquire(lane);
+            stage_row_f32(slot, r, rr);
+            ring.publish();
+            if (lane == 0) {
+              tma_store_2d(&maps.out0, slot, n0 + c * 32, r0);
+              bulk_commit_group();
+            }
+          }
         }
+        if (!ok) break;
+        if (warp_active) res_g += nch;
         tmem_st_wait();
         const float mean = sum / static_cast<float>(D);
         float sq = 0.f;
-        for (int c = 0; c < D; c += 32) {
+        for (int c = 0; c < nch; ++c) {
           uint32_t v[32];
           __syncwarp();
-          tmem_ld_x32(taddr + c, v);
+          tmem_ld_x32(taddr + c * 32, v);
           tmem_ld_wait();
 #pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            const float d = __uint_as_float(v[i]) - mean;
+          for (int e = 0; e < 32; ++e) {
+            const float d = __uint_as_float(v[e]) - mean;
             sq = fmaf(d, d, sq);
           }
         }
         const float rstd = rsqrtf(sq / static_cast<float>(D) + p.eps);
         const bool zero_row = valid && p.row_mask != nullptr && p.row_mask[row] == 0;
-        for (int c = 0; c < D; c += 32) {
+        for (int c = 0; c < nch; ++c) {
           uint32_t v[32];
           __syncwarp();
-          tmem_ld_x32(taddr + c, v);
+          tmem_ld_x32(taddr + c * 32, v);
           tmem_ld_wait();
-          if (!valid) continue;
+          if (!warp_active) continue;
           float y[32];
 #pragma unroll
-          for (int i = 0; i < 32; ++i)
-            y[i] = zero_row ? 0.f
-                            : fmaf((__uint_as_float(v[i]) - mean) * rstd, s_gamma[c + i], s_beta[c + i]);
-          if (p.norm_f16) {
-            uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<__half*>(p.norm_out) +
-                                                  static_cast<size_t>(row) * D + c);
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-              uint4 w;
-              w.x = pack_half2(y[8 * i + 0], y[8 * i + 1]);
-              w.y = pack_half2(y[8 * i + 2], y[8 * i + 3]);
-              w.z = pack_half2(y[8 * i + 4], y[8 * i + 5]);
-              w.w = pack_half2(y[8 * i + 6], y[8 * i + 7]);
-              dst[i] = w;
-            }
-          } else {
-            float4* dst = reinterpret_cast<float4*>(reinterpret_cast<float*>(p.norm_out) +
-                                                    static_cast<size_t>(row) * D + c);
-#pragma unroll
-            for (int i = 0; i < 8; ++i)
-              dst[i] = make_float4(y[4 * i + 0], y[4 * i + 1], y[4 * i + 2], y[4 * i + 3]);
+          for (int e = 0; e < 32; ++e)
+            y[e] = zero_row ? 0.f
+                            : fmaf((__uint_as_float(v[e]) - mean) * rstd, s_gamma[c * 32 + e],
+                                   s_beta[c * 32 + e]);
+          const uint32_t slot = ring.acquire(lane);
+          if (p.norm_f16)
+            stage_row_f16x32(slot, r, y);
+          else
+            stage_row_f32(slot, r, y);
+          ring.publish();
+          if (lane == 0) {
+            tma_store_2d(&maps.out1, slot, n0 + c * 32, r0);
+            bulk_commit_group();
           }
         }
       }
+      // The accumulator buffer may be overwritten by the next item's MMAs.
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acc_empty[ab]);
+    }
+    if (lane == 0) bulk_wait_group_all();
+    // Residual tiles requested but never consumed (abort path) must land first.
+    if constexpr (EPI == EPI_RESID_LN) {
+      if (lane == 0 && !ok)
+        for (int k2 = 0; k2 < kResRing; ++k2)
+          wait_drain(&my_res_full[(res_g + k2) % kResRing], ((res_g + k2) / kResRing) & 1, kDrainLimitNs);
     }
   }
 
