@@ -337,8 +337,7 @@ __global__ void __launch_bounds__(192, 1)
 #pragma unroll
         for (int g = 0; g < HDX / 16; ++g) {
           uint32_t r[16];
-          tmem_ld_x16(tO + g * 16, r);
-          tmem_ld_wait();
+          tmem_ld_x16_sync(tO + g * 16, r);
 #pragma unroll
           for (int d = 0; d < 16; ++d) {
             const int col = g * 16 + d;
@@ -365,7 +364,7 @@ __global__ void __launch_bounds__(192, 1)
           vb3 = __ballot_sync(~0u, ka + 96 < p.seq && mrow[min(ka + 96, p.seq - 1)] != 0);
           mask_partial = (vb0 & vb1 & vb2 & vb3) != ~0u;
         }
-        const bool need_mask = mask_partial || (k0 + BN > row_lim);
+        const bool need_mask = __any_sync(0xffffffffu, mask_partial || (k0 + BN > row_lim));
         const int bs = t & 1;
 
         if (!(ok = warp_wait_phase(&s_full[bs], (t >> 1) & 1, wd, 0x301))) break;
@@ -374,8 +373,7 @@ __global__ void __launch_bounds__(192, 1)
 #pragma unroll
         for (int g = 0; g < BN / 32; ++g) {
           uint32_t r[32];
-          tmem_ld_x32(tmem_base + lane_base + bs * 128 + g * 32, r);
-          tmem_ld_wait();
+          tmem_ld_x32_sync(tmem_base + lane_base + bs * 128 + g * 32, r);
 #pragma unroll
           for (int i = 0; i < 32; ++i) x[g * 32 + i] = __uint_as_float(r[i]);
         }

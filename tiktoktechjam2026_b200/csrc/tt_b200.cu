@@ -16,6 +16,7 @@
 #include <vector>
 
 #include "tt_attention.cuh"
+#include "tt_attention2s.cuh"
 #include "tt_gemm.cuh"
 #include "tt_misc.cuh"
 #include "../../include/tt_b200.h"
@@ -216,15 +217,15 @@ struct RouteEntry {
 
 const RouteEntry kRouteTable[] = {
     // C1  B64 S128  D128 H4 F128
-    {128, 4, 128, 128, {"d128-h4-s128", 128, 2, 2, 128, 2, 2, 1}},
+    {128, 4, 128, 128, {"d128-h4-s128", 128, 2, 2, 128, 2, 2, 0}},
     // C2  B64 S1024 D128 H4 F128
-    {128, 4, 1024, 128, {"d128-h4-s1024", 128, 2, 2, 128, 2, 2, 1}},
+    {128, 4, 1024, 128, {"d128-h4-s1024", 128, 2, 2, 128, 2, 2, 0}},
     // C3  B256 S256 D32 H2 F128
-    {32, 2, 256, 128, {"d32-h2-s256", 96, 1, 1, 128, 1, 4, 1}},
+    {32, 2, 256, 128, {"d32-h2-s256", 96, 1, 1, 128, 1, 4, 0}},
     // C4  B16 S2048 D512 H8 F2048 (+ key padding)
-    {512, 8, 2048, 2048, {"d512-h8-s2048", 256, 4, 2, 256, 4, 2, 1}},
+    {512, 8, 2048, 2048, {"d512-h8-s2048", 256, 4, 2, 256, 4, 2, 0}},
     // C5  B512 S1024 D256 H8 F1024
-    {256, 8, 1024, 1024, {"d256-h8-s1024", 256, 2, 2, 256, 2, 3, 1}},
+    {256, 8, 1024, 1024, {"d256-h8-s1024", 256, 2, 2, 256, 2, 3, 0}},
 };
 
 int largest_bn_dividing(int n, int cap) {
@@ -273,7 +274,7 @@ int choose_route(int d_model, int heads, int seq, int ffn, Route* out) {
   r.ffn_in_bn = largest_bn_dividing(ffn, 256);
   r.ffn_in_nst = 4;
   r.ffn_out_nst = 4;
-  r.attn_exp16 = 1;
+  r.attn_exp16 = 0;
   if (r.qkv_bn == 0 || r.ffn_in_bn == 0)
     return fail(TT_ERR_UNSUPPORTED, "no column split for d_model=%d ffn=%d", d_model, ffn);
   *out = r;
@@ -380,23 +381,22 @@ int launch_attention(const CUtensorMap& tq, const CUtensorMap& tk, const CUtenso
   if (items > 0x7fffffffLL) return fail(TT_ERR_SHAPE, "batch*heads*query tiles too large");
   const int n_items = static_cast<int>(items);
   const unsigned grid = static_cast<unsigned>(n_items < sm_count ? n_items : sm_count);
-  switch (hd * 2 + (exp16 ? 1 : 0)) {
-#define TT_ATTN_CASE(HD, E)                                                         \
-  case HD * 2 + E: {                                                                \
-    auto kern = attn_fwd_kernel<HD, E != 0>;                                        \
-    if (int rc = prepare_kernel(kern, AttnLayout<HD>::SMEM_ALLOC)) return rc;       \
-    kern<<<grid, 192, AttnLayout<HD>::SMEM_ALLOC, stream>>>(tq, tk, tv, ap, n_items); \
-    break;                                                                          \
-  }
-    TT_ATTN_CASE(16, 0)
-    TT_ATTN_CASE(16, 1)
-    TT_ATTN_CASE(32, 0)
-    TT_ATTN_CASE(32, 1)
-    TT_ATTN_CASE(64, 0)
-    TT_ATTN_CASE(64, 1)
-#undef TT_ATTN_CASE
-    default:
-      return fail(TT_ERR_UNSUPPORTED, "head_dim %d not in {16, 32, 64}", hd);
+  if (hd == 16 || hd == 32) {
+    // Two softmax streams per CTA (head_dim <= 32).
+    auto kern = hd == 16 ? attn2s_fwd_kernel<16> : attn2s_fwd_kernel<32>;
+    const int smem = hd == 16 ? Attn2sLayout<16>::SMEM_ALLOC : Attn2sLayout<32>::SMEM_ALLOC;
+    if (int rc = prepare_kernel(kern, smem)) return rc;
+    const int ctas = (n_items + 1) / 2;
+    const unsigned grid2 = static_cast<unsigned>(ctas < sm_count ? ctas : sm_count);
+    kern<<<grid2, 384, smem, stream>>>(tq, tk, tv, ap, n_items);
+    (void)grid;
+    (void)exp16;
+  } else if (hd == 64) {
+    auto kern = exp16 ? attn_fwd_kernel<64, true> : attn_fwd_kernel<64, false>;
+    if (int rc = prepare_kernel(kern, AttnLayout<64>::SMEM_ALLOC)) return rc;
+    kern<<<grid, 192, AttnLayout<64>::SMEM_ALLOC, stream>>>(tq, tk, tv, ap, n_items);
+  } else {
+    return fail(TT_ERR_UNSUPPORTED, "head_dim %d not in {16, 32, 64}", hd);
   }
   return after_launch("attention");
 }
@@ -736,7 +736,7 @@ int tt_causal_attention(const void* q, const void* k, const void* vt, const uint
   ap.ctx = static_cast<__half*>(ctx);
   ap.err = ds->err;
   ap.timeout_ns = g_timeout_ns.load();
-  return launch_attention(tq, tk, tv, ap, head_dim, true, ds->sm_count, static_cast<cudaStream_t>(stream));
+  return launch_attention(tq, tk, tv, ap, head_dim, false, ds->sm_count, static_cast<cudaStream_t>(stream));
 }
 
 int tt_causal_attention_masked_noalloc(const void* q, const void* k, const void* vt,
@@ -779,7 +779,7 @@ int tt_causal_attention_masked_noalloc(const void* q, const void* k, const void*
   ap.ctx = static_cast<__half*>(ctx);
   ap.err = ds->err;
   ap.timeout_ns = g_timeout_ns.load();
-  return launch_attention(tq, tk, tv, ap, head_dim, true, ds->sm_count, s);
+  return launch_attention(tq, tk, tv, ap, head_dim, false, ds->sm_count, s);
 }
 
 int tt_linear_residual_layernorm(const void* a, const void* w, const float* bias,

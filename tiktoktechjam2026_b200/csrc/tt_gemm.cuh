@@ -332,8 +332,7 @@ __global__ void __launch_bounds__(192, 1)
         for (int c = 0; c < nch; ++c) {
           uint32_t v[32];
           __syncwarp();
-          tmem_ld_x32(taddr + c * 32, v);
-          tmem_ld_wait();
+          tmem_ld_x32_sync(taddr + c * 32, v);
           const int col0 = n0 + c * 32;
           float f[32];
 #pragma unroll
@@ -404,8 +403,7 @@ __global__ void __launch_bounds__(192, 1)
         for (int c = 0; c < nch; ++c) {
           uint32_t v[32];
           __syncwarp();
-          tmem_ld_x32(taddr + c * 32, v);
-          tmem_ld_wait();
+          tmem_ld_x32_sync(taddr + c * 32, v);
           if (!warp_active) continue;
           float gl[32];
 #pragma unroll
@@ -425,8 +423,7 @@ __global__ void __launch_bounds__(192, 1)
         for (int c = 0; c < nch; ++c) {
           uint32_t v[32];
           __syncwarp();
-          tmem_ld_x32(taddr + c * 32, v);
-          tmem_ld_wait();
+          tmem_ld_x32_sync(taddr + c * 32, v);
           float res[32];
           const int q = res_g + c;
           if (warp_active) {
@@ -475,8 +472,7 @@ __global__ void __launch_bounds__(192, 1)
         for (int c = 0; c < nch; ++c) {
           uint32_t v[32];
           __syncwarp();
-          tmem_ld_x32(taddr + c * 32, v);
-          tmem_ld_wait();
+          tmem_ld_x32_sync(taddr + c * 32, v);
 #pragma unroll
           for (int e = 0; e < 32; ++e) {
             const float d = __uint_as_float(v[e]) - mean;
@@ -488,8 +484,7 @@ __global__ void __launch_bounds__(192, 1)
         for (int c = 0; c < nch; ++c) {
           uint32_t v[32];
           __syncwarp();
-          tmem_ld_x32(taddr + c * 32, v);
-          tmem_ld_wait();
+          tmem_ld_x32_sync(taddr + c * 32, v);
           if (!warp_active) continue;
           float y[32];
 #pragma unroll
