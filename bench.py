@@ -96,6 +96,7 @@ def algorithmic(cfg, batch):
     qkv:       FLOPs 6ND^2, bytes 8ND + 6D^2
     out_ln:    FLOPs 2ND^2, bytes 12ND + 2D^2 (ctx FP16 in, residual FP32 in/out, normalized FP16 out)
     ffn (split): ffn_in FLOPs 2NDF, bytes 2ND + 2NF + 2DF; ffn_out_ln FLOPs 2NDF, bytes 2NF + 10ND + 2DF
+    ffn_fused: FLOPs 4NDF, bytes 12ND + 4DF (normalized FP16 in, residual FP32 in/out, normalized out)
     """
     S, D, F = cfg["seq"], cfg["d_model"], cfg["ffn"]
     N = batch * S
@@ -106,7 +107,9 @@ def algorithmic(cfg, batch):
         "out_ln": (2.0 * N * D * D, 12.0 * N * D + 2.0 * D * D),
         "ffn_in": (2.0 * N * D * F, 2.0 * N * D + 2.0 * N * F + 2.0 * D * F),
         "ffn_out_ln": (2.0 * N * D * F, 2.0 * N * F + 10.0 * N * D + 2.0 * D * F),
+        "ffn_fused": (4.0 * N * D * F, 12.0 * N * D + 4.0 * D * F),
         "ln0": (0.0, 6.0 * N * D),
+        "mask": (0.0, float(batch * S)),
     }
 
 

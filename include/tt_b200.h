@@ -135,6 +135,23 @@ int tt_linear_residual_layernorm(const void* a, const void* w, const float* bias
 int tt_linear_gelu(const void* a, const void* w, const float* bias, void* out, int64_t n_rows,
                    int k_in, int n_out, void* stream);
 
+/* Whole FFN block fused in one kernel:
+ *   h         = GELU_erf(a[N, D] (FP16) . w1[F, D]^T + b1)    (FP32 math; FP16 h
+ *               kept on chip, never written to memory)
+ *   resid_out = h . w2[D, F]^T + b2 + resid_in                   (FP32)
+ *   norm_out  = LayerNorm(resid_out) * gamma + beta             (FP16 or FP32)
+ * rows whose row_mask byte is 0 get norm_out = 0 (row_mask may be NULL).
+ * d_model in {32, 64, 128, 256}, ffn a multiple of 128, b1 16-byte aligned;
+ * in-place (resid_out == resid_in) is allowed.
+ * Replaces mixed_ffn_add_layer_norm (mixed_precision/triton_linear.py:128-185,
+ * 327-378; D = F = 128 there) and the ffn_in/GELU/ffn_out/fused_add_layer_norm
+ * chain of the generic route (mixed_precision/transformer.py:669-695). */
+int tt_ffn_residual_layernorm(const void* a, const void* w1, const float* b1, const void* w2,
+                              const float* b2, const float* resid_in, const float* gamma,
+                              const float* beta, float* resid_out, void* norm_out, int64_t n_rows,
+                              int d_model, int ffn, float eps, int norm_out_is_f16,
+                              const uint8_t* row_mask, void* stream);
+
 /* Writes a one-line description of the route and tile configuration the
  * shape-dispatch table selects for (d_model, heads, seq, ffn) into buf
  * (host).  Returns TT_OK, or TT_ERR_UNSUPPORTED for shapes outside it. */

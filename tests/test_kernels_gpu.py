@@ -162,3 +162,41 @@ def test_watchdog_times_out_cleanly_and_context_survives(tt_lib):
     x = torch.randn(64, 128, device=DEV)
     out = ops.layernorm_rows(x, torch.ones(128, device=DEV), torch.zeros(128, device=DEV), 1e-5, torch.float32)
     torch.testing.assert_close(out, F.layer_norm(x, (128,)), rtol=2e-5, atol=2e-5)
+
+
+FFN_SHAPES = [(1000, 128, 128), (300, 32, 128), (513, 256, 1024), (129, 64, 256), (4096, 256, 1024), (77, 128, 512)]
+
+
+@pytest.mark.parametrize("N,D,Fd", FFN_SHAPES)
+@pytest.mark.parametrize("norm_dtype", [torch.float16, torch.float32])
+def test_ffn_residual_layernorm(tt_lib, N, D, Fd, norm_dtype):
+    g = _gen(N * 7 + D + Fd)
+    a = torch.randn(N, D, generator=g).half().to(DEV)
+    w1 = (torch.randn(Fd, D, generator=g) / math.sqrt(D)).half().to(DEV)
+    b1 = (torch.randn(Fd, generator=g) * 0.1).to(DEV)
+    w2 = (torch.randn(D, Fd, generator=g) / math.sqrt(Fd)).half().to(DEV)
+    b2 = (torch.randn(D, generator=g) * 0.1).to(DEV)
+    r = torch.randn(N, D, generator=g).to(DEV)
+    gw = (1 + 0.1 * torch.randn(D, generator=g)).to(DEV)
+    gb = (0.1 * torch.randn(D, generator=g)).to(DEV)
+    mask = (torch.rand(N, generator=g) > 0.2).to(DEV)
+    resid, norm = ops.ffn_residual_layernorm(a, w1, b1, w2, b2, r, gw, gb, 1e-5, norm_dtype, mask)
+    # The reference rounds the GELU output to FP16 before the second projection.
+    h = F.gelu(a.float() @ w1.float().t() + b1, approximate="none").half().float()
+    ref_r = r + h @ w2.float().t() + b2
+    ref_n = F.layer_norm(ref_r, (D,), gw, gb, 1e-5).masked_fill(~mask[:, None], 0)
+    # The GELU differs from exact erf by < 7e-7, which rarely flips the FP16 rounding of h by one
+    # ulp (2^-9 at |h| ~ 3); through W2 (|w| <= ~0.3) that moves r by at most ~1.5e-3.
+    torch.testing.assert_close(resid, ref_r, rtol=1e-3, atol=2e-3)
+    tol = 4e-3 if norm_dtype == torch.float16 else 1e-3
+    torch.testing.assert_close(norm.float(), ref_n, rtol=tol, atol=tol)
+
+
+def test_gelu_matches_exact_erf(tt_lib):
+    """GELU of the projection epilogue against exact-erf GELU over a dense input sweep."""
+    x = torch.linspace(-12, 12, 128 * 2048, device=DEV).reshape(-1, 128)
+    eye = torch.eye(128, device=DEV).half()
+    out = ops.linear_gelu(x.half(), eye, torch.zeros(128, device=DEV))
+    ref = F.gelu(x.half().float(), approximate="none")
+    # out is FP16: within FP16 rounding of the exact value
+    torch.testing.assert_close(out.float(), ref, rtol=1e-3, atol=1e-6)

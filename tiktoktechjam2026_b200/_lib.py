@@ -93,6 +93,11 @@ SIGNATURES = {
         [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int, c_int,
          c_float, c_int, c_void_p, c_void_p],
     ),
+    "tt_ffn_residual_layernorm": (
+        c_int,
+        [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
+         c_int64, c_int, c_int, c_float, c_int, c_void_p, c_void_p],
+    ),
     "tt_linear_gelu": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int, c_int, c_void_p]),
     "tt_route_describe": (c_int, [c_int, c_int, c_int, c_int, c_char_p, c_int]),
     "tt_model_create": (c_int, [POINTER(ModelDesc), POINTER(c_void_p)]),

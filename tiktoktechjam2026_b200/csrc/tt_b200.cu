@@ -17,6 +17,7 @@
 
 #include "tt_attention.cuh"
 #include "tt_attention2s.cuh"
+#include "tt_ffn.cuh"
 #include "tt_gemm.cuh"
 #include "tt_misc.cuh"
 #include "../../include/tt_b200.h"
@@ -208,6 +209,7 @@ struct Route {
   int ffn_in_bn, ffn_in_nst;
   int ffn_out_nst;
   int attn_exp16;  // 1: probabilities from packed-FP16 exp2, 0: FP32 exp2
+  int ffn_fused;   // 1: one fused FFN kernel (d_model in {32, 64, 128, 256}); 0: split route
 };
 
 struct RouteEntry {
@@ -217,15 +219,15 @@ struct RouteEntry {
 
 const RouteEntry kRouteTable[] = {
     // C1  B64 S128  D128 H4 F128
-    {128, 4, 128, 128, {"d128-h4-s128", 128, 2, 2, 128, 2, 2, 0}},
+    {128, 4, 128, 128, {"d128-h4-s128", 128, 2, 2, 128, 2, 2, 0, 1}},
     // C2  B64 S1024 D128 H4 F128
-    {128, 4, 1024, 128, {"d128-h4-s1024", 128, 2, 2, 128, 2, 2, 0}},
+    {128, 4, 1024, 128, {"d128-h4-s1024", 128, 2, 2, 128, 2, 2, 0, 1}},
     // C3  B256 S256 D32 H2 F128
-    {32, 2, 256, 128, {"d32-h2-s256", 96, 1, 1, 128, 1, 4, 0}},
+    {32, 2, 256, 128, {"d32-h2-s256", 96, 1, 1, 128, 1, 4, 0, 1}},
     // C4  B16 S2048 D512 H8 F2048 (+ key padding)
-    {512, 8, 2048, 2048, {"d512-h8-s2048", 256, 4, 2, 256, 4, 2, 0}},
+    {512, 8, 2048, 2048, {"d512-h8-s2048", 256, 4, 2, 256, 4, 2, 0, 0}},
     // C5  B512 S1024 D256 H8 F1024
-    {256, 8, 1024, 1024, {"d256-h8-s1024", 256, 2, 2, 256, 2, 3, 0}},
+    {256, 8, 1024, 1024, {"d256-h8-s1024", 256, 2, 2, 256, 2, 3, 0, 1}},
 };
 
 int largest_bn_dividing(int n, int cap) {
@@ -245,6 +247,10 @@ int clamp_nst(int ksw, int bn, int k, int want, int epi, int n_total) {
 // K-block width of a GEMM: 64 FP16 (128-byte swizzle) unless K is not a
 // multiple of 64 or the 512-column residual tile needs the smaller stage.
 int gemm_ksw(int k, int bn) { return (k % 64 == 0 && bn <= 256) ? 64 : 32; }
+
+bool ffn_fusable(int d_model, int ffn) {
+  return (d_model == 32 || d_model == 64 || d_model == 128 || d_model == 256) && ffn % 128 == 0;
+}
 
 int check_model_shape(int d_model, int heads, int ffn) {
   if (d_model <= 0 || heads <= 0 || ffn <= 0 || d_model % heads != 0)
@@ -275,6 +281,7 @@ int choose_route(int d_model, int heads, int seq, int ffn, Route* out) {
   r.ffn_in_nst = 4;
   r.ffn_out_nst = 4;
   r.attn_exp16 = 0;
+  r.ffn_fused = ffn_fusable(d_model, ffn) ? 1 : 0;
   if (r.qkv_bn == 0 || r.ffn_in_bn == 0)
     return fail(TT_ERR_UNSUPPORTED, "no column split for d_model=%d ffn=%d", d_model, ffn);
   *out = r;
@@ -316,6 +323,45 @@ GemmParams base_params(DeviceState* ds) {
   p.err = ds->err;
   p.timeout_ns = g_timeout_ns.load();
   return p;
+}
+
+int launch_ffn(const FfnMaps& maps, FfnParams p, int sm_count, cudaStream_t stream) {
+  const long long items = (static_cast<long long>(p.M) + 127) / 128;
+  p.n_items = static_cast<int>(items);
+  const unsigned grid = static_cast<unsigned>(items < sm_count ? items : sm_count);
+  switch (p.D) {
+#define TT_FFN_CASE(DD)                                                     \
+  case DD: {                                                                \
+    auto kern = ffn_fused_kernel<DD>;                                       \
+    const int smem = FfnLayout<DD>::smem_bytes(p.F);                        \
+    if (smem > 232448) return fail(TT_ERR_UNSUPPORTED, "ffn %d too wide", p.F); \
+    if (int rc = prepare_kernel(kern, smem)) return rc;                     \
+    kern<<<grid, 320, smem, stream>>>(maps, p);                             \
+    break;                                                                  \
+  }
+    TT_FFN_CASE(32)
+    TT_FFN_CASE(64)
+    TT_FFN_CASE(128)
+    TT_FFN_CASE(256)
+#undef TT_FFN_CASE
+    default:
+      return fail(TT_ERR_UNSUPPORTED, "fused FFN: d_model %d not in {32, 64, 128, 256}", p.D);
+  }
+  return after_launch("ffn");
+}
+
+// Tensor maps of the fused FFN for one call.
+int encode_ffn_maps(FfnMaps* maps, const void* a, const void* w1, const void* w2, const float* resid_out,
+                    const void* norm_out, bool norm_f32, uint64_t rows, int D, int F) {
+  memset(maps, 0, sizeof(*maps));
+  if (int rc = encode_matrix(&maps->a, a, rows, D, 32, 128)) return rc;
+  if (int rc = encode_matrix(&maps->w1, w1, F, D, 32, 128)) return rc;
+  if (int rc = encode_matrix(&maps->w2, w2, D, F, 32, D)) return rc;
+  if (resid_out)
+    if (int rc = encode_epi_tile(&maps->out0, resid_out, rows, D, true)) return rc;
+  if (norm_out)
+    if (int rc = encode_epi_tile(&maps->out1, norm_out, rows, D, norm_f32)) return rc;
+  return TT_OK;
 }
 
 int run_layernorm(const float* x, const float* gamma, const float* beta, void* out,
@@ -465,8 +511,8 @@ struct tt_model {
   const float* ln0_w = nullptr;
   const float* ln0_b = nullptr;
   std::vector<tt_layer_weights> layers;
-  // Per-layer weight tensor maps.
-  std::vector<CUtensorMap> tm_wqkv, tm_wout, tm_win, tm_wout2;
+  // Per-layer weight tensor maps (split FFN route: tm_win/tm_wout2; fused: tm_w1f/tm_w2f).
+  std::vector<CUtensorMap> tm_wqkv, tm_wout, tm_win, tm_wout2, tm_w1f, tm_w2f;
   // Route + bound workspace (re-encoded when shape or workspace change).
   Route route{};
   int route_seq = -1;
@@ -477,6 +523,7 @@ struct tt_model {
   CUtensorMap tm_norm{}, tm_ctx{}, tm_hidden{}, tm_q{}, tm_k{}, tm_vt{};
   // Epilogue tiles (box 32 x 32): QKV stores, residual (FP32), normalized and hidden (FP16).
   CUtensorMap tm_q_st{}, tm_k_st{}, tm_vt_st{}, tm_resid{}, tm_norm_st{}, tm_hidden_st{};
+  CUtensorMap tm_norm32{};  // normalized activations as the fused FFN's A operand (box {32, 128})
   // Profiling.
   bool profiling = false;
   struct Rec {
@@ -513,7 +560,9 @@ WsLayout ws_layout(const tt_model* m, int batch, int seq) {
   w.k = take(N * m->D * 2);
   w.vt = take(static_cast<size_t>(batch) * m->H * hd * w.seq_pad * 2);
   w.ctx = take(N * m->D * 2);
-  w.hidden = take(N * m->F * 2);
+  Route r;
+  const bool fused = choose_route(m->D, m->H, seq, m->F, &r) == TT_OK && r.ffn_fused;
+  w.hidden = take(fused ? 0 : N * m->F * 2);
   w.kv_end = take(static_cast<size_t>(batch) * 4);
   w.total = off;
   return w;
@@ -567,6 +616,12 @@ int bind_workspace(tt_model* m, int batch, int seq, void* ws, cudaStream_t strea
         return rc;
       if (int rc = encode_matrix(&m->tm_wout2[l], w.w_ffn_out, m->D, m->F, m->ksw_out2, out_box))
         return rc;
+      if (m->route.ffn_fused) {
+        m->tm_w1f.resize(m->L);
+        m->tm_w2f.resize(m->L);
+        if (int rc = encode_matrix(&m->tm_w1f[l], w.w_ffn_in, m->F, m->D, 32, 128)) return rc;
+        if (int rc = encode_matrix(&m->tm_w2f[l], w.w_ffn_out, m->D, m->F, 32, m->D)) return rc;
+      }
     }
     m->bound_ws = nullptr;
   }
@@ -578,7 +633,9 @@ int bind_workspace(tt_model* m, int batch, int seq, void* ws, cudaStream_t strea
   if (m->ksw_qkv != m->ksw_in) return fail(TT_ERR_UNSUPPORTED, "QKV and FFN-in K-blocks differ");
   if (int rc = encode_matrix(&m->tm_norm, base + w.norm, N, m->D, m->ksw_qkv, 128)) return rc;
   if (int rc = encode_matrix(&m->tm_ctx, base + w.ctx, N, m->D, m->ksw_out, 128)) return rc;
-  if (int rc = encode_matrix(&m->tm_hidden, base + w.hidden, N, m->F, m->ksw_out2, 128)) return rc;
+  if (!m->route.ffn_fused)
+    if (int rc = encode_matrix(&m->tm_hidden, base + w.hidden, N, m->F, m->ksw_out2, 128)) return rc;
+  if (int rc = encode_matrix(&m->tm_norm32, base + w.norm, N, m->D, 32, 128)) return rc;
   if (int rc = encode_attention_maps(&m->tm_q, &m->tm_k, &m->tm_vt, base + w.q, base + w.k,
                                      base + w.vt, batch * m->H, seq, hd, w.seq_pad))
     return rc;
@@ -588,7 +645,8 @@ int bind_workspace(tt_model* m, int batch, int seq, void* ws, cudaStream_t strea
       return rc;
   if (int rc = encode_epi_tile(&m->tm_resid, base + w.resid, N, m->D, true)) return rc;
   if (int rc = encode_epi_tile(&m->tm_norm_st, base + w.norm, N, m->D, false)) return rc;
-  if (int rc = encode_epi_tile(&m->tm_hidden_st, base + w.hidden, N, m->F, false)) return rc;
+  if (!m->route.ffn_fused)
+    if (int rc = encode_epi_tile(&m->tm_hidden_st, base + w.hidden, N, m->F, false)) return rc;
   // V^T columns in [seq, seq_pad) are never written by the projection; they
   // must hold finite values because masked probabilities (0) multiply them.
   if (w.seq_pad != seq)
@@ -845,15 +903,55 @@ int tt_linear_gelu(const void* a, const void* w, const float* bias, void* out, i
   return launch_gemm(ksw, EPI_GELU, maps, p, ds->sm_count, static_cast<cudaStream_t>(stream));
 }
 
+int tt_ffn_residual_layernorm(const void* a, const void* w1, const float* b1, const void* w2,
+                              const float* b2, const float* resid_in, const float* gamma,
+                              const float* beta, float* resid_out, void* norm_out, int64_t n_rows,
+                              int d_model, int ffn, float eps, int norm_out_is_f16,
+                              const uint8_t* row_mask, void* stream) {
+  DeviceState* ds;
+  if (int rc = current_device_state(&ds)) return rc;
+  if (!a || !w1 || !b1 || !w2 || !b2 || !resid_in || !gamma || !beta || !resid_out || !norm_out)
+    return fail(TT_ERR_ARG, "null argument");
+  if (n_rows <= 0 || n_rows > 0x7fffffffLL) return fail(TT_ERR_SHAPE, "invalid n_rows %lld", (long long)n_rows);
+  if (!ffn_fusable(d_model, ffn))
+    return fail(TT_ERR_UNSUPPORTED,
+                "fused FFN needs d_model in {32, 64, 128, 256} and ffn %% 128 == 0 (got %d, %d)", d_model,
+                ffn);
+  if (reinterpret_cast<uintptr_t>(b1) % 16 != 0) return fail(TT_ERR_ALIGN, "b1 must be 16-byte aligned");
+  FfnMaps maps;
+  if (int rc = encode_ffn_maps(&maps, a, w1, w2, resid_out, norm_out, norm_out_is_f16 == 0, n_rows, d_model, ffn))
+    return rc;
+  FfnParams p;
+  memset(&p, 0, sizeof(p));
+  p.M = static_cast<int>(n_rows);
+  p.D = d_model;
+  p.F = ffn;
+  p.b1 = b1;
+  p.b2 = b2;
+  p.gamma = gamma;
+  p.beta = beta;
+  p.resid_in = resid_in;
+  p.norm_f16 = norm_out_is_f16 ? 1 : 0;
+  p.eps = eps;
+  p.row_mask = row_mask;
+  p.err = ds->err;
+  p.timeout_ns = g_timeout_ns.load();
+  return launch_ffn(maps, p, ds->sm_count, static_cast<cudaStream_t>(stream));
+}
+
 int tt_route_describe(int d_model, int heads, int seq, int ffn, char* buf, int buflen) {
   Route r;
   if (int rc = choose_route(d_model, heads, seq, ffn, &r)) return rc;
   if (buf && buflen > 0)
     snprintf(buf, buflen,
-             "route=%s qkv_bn=%d qkv_nst=%d out_nst=%d ffn=split ffn_in_bn=%d ffn_in_nst=%d "
+             "route=%s qkv_bn=%d qkv_nst=%d out_nst=%d ffn_in_bn=%d ffn_in_nst=%d "
              "ffn_out_nst=%d attn_tile=128x128 attn_exp=%s",
              r.name, r.qkv_bn, r.qkv_nst, r.out_nst, r.ffn_in_bn, r.ffn_in_nst, r.ffn_out_nst,
              r.attn_exp16 ? "f16x2" : "f32");
+  if (buf && buflen > 0 && r.ffn_fused) {
+    const size_t len = strlen(buf);
+    snprintf(buf + len, buflen - len > 0 ? buflen - len : 0, " ffn=fused(chunk=128)");
+  }
   return TT_OK;
 }
 
@@ -1024,6 +1122,34 @@ int tt_model_forward(tt_model* m, const float* x, const uint8_t* mask, float* ou
       if (int rc = record_begin(m, s, &ev)) return rc;
       if (int rc = launch_gemm(m->ksw_out, EPI_RESID_LN, maps, p, ds->sm_count, s)) return rc;
       if (int rc = record_end(m, s, TT_KERNEL_OUT_LN, ev)) return rc;
+    }
+    if (r.ffn_fused) {
+      // Whole FFN + residual + next norm (final_norm -> FP32 output on the last layer)
+      FfnMaps fm;
+      fm.a = m->tm_norm32;
+      fm.w1 = m->tm_w1f[l];
+      fm.w2 = m->tm_w2f[l];
+      fm.out0 = m->tm_resid;
+      fm.out1 = last ? tm_out : m->tm_norm_st;
+      FfnParams fp;
+      memset(&fp, 0, sizeof(fp));
+      fp.M = N;
+      fp.D = D;
+      fp.F = F;
+      fp.b1 = lw.b_ffn_in;
+      fp.b2 = lw.b_ffn_out;
+      fp.gamma = lw.ln_next_w;
+      fp.beta = lw.ln_next_b;
+      fp.resid_in = reinterpret_cast<const float*>(base + w.resid);
+      fp.norm_f16 = last ? 0 : 1;
+      fp.eps = m->eps;
+      fp.row_mask = last ? mask : nullptr;
+      fp.err = ds->err;
+      fp.timeout_ns = g_timeout_ns.load();
+      if (int rc = record_begin(m, s, &ev)) return rc;
+      if (int rc = launch_ffn(fm, fp, ds->sm_count, s)) return rc;
+      if (int rc = record_end(m, s, TT_KERNEL_FFN_FUSED, ev)) return rc;
+      continue;
     }
     // FFN in + GELU
     {

@@ -90,7 +90,7 @@ __host__ __device__ inline int gemm_smem_bytes(int ksw, int bn, int nst, int epi
   int off = nst * gemm_stage_bytes(ksw, bn);
   off += gemm_epi_bytes(epi);
   off += (n_total + 2 * bn) * 4;
-  off += (2 * kGemmMaxStages + 4 + 4 * kResRing + 1) * 8;
+  off += (2 * kGemmMaxStages + 5 + 4 * kResRing + 1) * 8;
   off += 16;
   return off + 1024;
 }
@@ -140,12 +140,23 @@ __device__ __forceinline__ void stage_row_f16x16(uint32_t tile, int r, const flo
                  pack_half2(v[8 * c + 6], v[8 * c + 7]));
 }
 
-// Column s of a [w rows x 32 FP16] tile (64-byte rows, SWIZZLE_64B): v[d] -> (d, s).
-__device__ __forceinline__ void stage_col_f16(uint32_t tile, int s, const float* v, int w) {
-  for (int d = 0; d < w; ++d) {
-    const uint32_t addr = tile + d * 64 + ((((s >> 3) ^ ((d >> 1) & 3))) << 4) + (s & 7) * 2;
-    const unsigned short h = __half_as_ushort(__float2half_rn(v[d]));
-    asm volatile("st.shared.u16 [%0], %1;" ::"r"(addr), "h"(h) : "memory");
+// Transposed staging of V: lane s holds v[0..W) = features d0..d0+W-1 of
+// token s; the tile is [W feature rows x 32 tokens] FP16 (64-byte rows,
+// SWIZZLE_64B).  Lane pairs (2k, 2k+1) swap halves with one shuffle per two
+// features, then each lane writes packed (token 2k, token 2k+1) words: even
+// lanes the even feature rows, odd lanes the odd ones (conflict-free).
+template <int W>
+__device__ __forceinline__ void stage_cols_f16(uint32_t tile, int lane, const float* v) {
+  const bool odd = lane & 1;
+  const int k = lane >> 1;  // word (token pair) within a 64-byte row
+#pragma unroll
+  for (int j = 0; j < W / 2; ++j) {
+    const float send = odd ? v[2 * j] : v[2 * j + 1];
+    const float recv = __shfl_xor_sync(0xffffffffu, send, 1);
+    const int d = 2 * j + (odd ? 1 : 0);
+    const uint32_t word = odd ? pack_half2(recv, v[2 * j + 1]) : pack_half2(v[2 * j], recv);
+    const uint32_t addr = tile + d * 64 + ((((k >> 2) ^ ((d >> 1) & 3))) << 4) + (k & 3) * 4;
+    asm volatile("st.shared.b32 [%0], %1;" ::"r"(addr), "r"(word) : "memory");
   }
 }
 
@@ -180,7 +191,8 @@ __global__ void __launch_bounds__(192, 1)
   const int bn = p.bn, nst = p.nst;
   const int stage_bytes = gemm_stage_bytes(KSW, bn);
   const int w_bytes_half = (bn > 256 ? 256 : bn) * KSW * 2;
-  uint8_t* epi = smem + nst * stage_bytes;
+  uint8_t* stages = smem;
+  uint8_t* epi = stages + nst * stage_bytes;
   float* s_bias = reinterpret_cast<float*>(epi + gemm_epi_bytes(EPI));  // [N_total]
   float* s_gamma = s_bias + p.N_total;                                    // [bn] (RESID_LN)
   float* s_beta = s_gamma + bn;
@@ -243,7 +255,7 @@ __global__ void __launch_bounds__(192, 1)
         for (int kb = 0; kb < nk; ++kb, ++g) {
           const int st = g % nst;
           if (!(ok = wait_phase(&empty[st], ((g / nst) & 1) ^ 1, wd, 0x401))) break;
-          uint8_t* sa = smem + st * stage_bytes;
+          uint8_t* sa = stages + st * stage_bytes;
           uint8_t* sw = sa + A_BYTES;
           mbar_arrive_expect_tx(&full[st], stage_bytes);
           tma_load_2d(sa, &maps.a, &full[st], kb * KSW, m0);
@@ -258,7 +270,7 @@ __global__ void __launch_bounds__(192, 1)
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
       const uint32_t idesc = umma_idesc_f16_f32(128, bn > 256 ? 256 : bn);
-      const uint32_t base = smem_u32(smem);
+      const uint32_t base = smem_u32(stages);
       int g = 0, i = 0;
       bool ok = true;
       for (int w = blockIdx.x; ok && w < p.n_items; w += gridDim.x, ++i) {
@@ -342,20 +354,23 @@ __global__ void __launch_bounds__(192, 1)
           if (p.tma_out) {
             if (!warp_active) continue;
             const uint32_t slot = ring.acquire(lane);
-            const int nsub = 32 / wbox;
-            for (int sb = 0; sb < nsub; ++sb) {
-              const uint32_t sub = slot + sb * 1024;
+            if (wbox == 32) {
+              if (which < 2)
+                stage_row_f16x32(slot, r, f);
+              else
+                stage_cols_f16<32>(slot, lane, f);
+            } else {
               if (which < 2) {
-                if (wbox == 32)
-                  stage_row_f16x32(sub, r, f);
-                else
-                  stage_row_f16x16(sub, r, f + sb * 16);
+                stage_row_f16x16(slot, r, f);
+                stage_row_f16x16(slot + 1024, r, f + 16);
               } else {
-                stage_col_f16(sub, r, f + sb * wbox, wbox);
+                stage_cols_f16<16>(slot, lane, f);
+                stage_cols_f16<16>(slot + 1024, lane, f + 16);
               }
             }
             ring.publish();
             if (lane == 0) {
+              const int nsub = 32 / wbox;
               for (int sb = 0; sb < nsub; ++sb) {
                 const int within = within0 + sb * wbox;
                 const int hh = within / hd, d0 = within - hh * hd;

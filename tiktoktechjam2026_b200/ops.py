@@ -133,3 +133,32 @@ def linear_gelu(a: torch.Tensor, w: torch.Tensor, bias: torch.Tensor) -> torch.T
         check(lib().tt_linear_gelu(a.data_ptr(), w.contiguous().data_ptr(), bias.float().contiguous().data_ptr(),
                                    out.data_ptr(), n, K, n_out, _stream(a)))
     return out
+
+
+def ffn_residual_layernorm(a: torch.Tensor, w1: torch.Tensor, b1: torch.Tensor, w2: torch.Tensor,
+                           b2: torch.Tensor, residual: torch.Tensor, ln_weight: torch.Tensor,
+                           ln_bias: torch.Tensor, eps: float = 1e-5,
+                           normalized_dtype: torch.dtype = torch.float16,
+                           row_mask: Optional[torch.Tensor] = None) -> Tuple[torch.Tensor, torch.Tensor]:
+    """(residual + GELU(a @ w1^T + b1) @ w2^T + b2, LayerNorm of it) in one fused kernel."""
+    _cuda(a, "a")
+    _cuda(residual, "residual")
+    _need(a.dtype == torch.float16 and w1.dtype == torch.float16 and w2.dtype == torch.float16,
+          "FP16 operands required")
+    _need(residual.dtype == torch.float32, "residual must be FP32")
+    D = residual.shape[-1]
+    n = residual.numel() // D
+    resid_out = torch.empty_like(residual)
+    norm = torch.empty(residual.shape, dtype=normalized_dtype, device=a.device)
+    mask_ptr = 0
+    if row_mask is not None:
+        m8 = row_mask.to(torch.bool).contiguous().view(torch.uint8)
+        mask_ptr = m8.data_ptr()
+    with torch.cuda.device(a.device):
+        check(lib().tt_ffn_residual_layernorm(
+            a.data_ptr(), w1.contiguous().data_ptr(), b1.float().contiguous().data_ptr(),
+            w2.contiguous().data_ptr(), b2.float().contiguous().data_ptr(), residual.data_ptr(),
+            ln_weight.float().contiguous().data_ptr(), ln_bias.float().contiguous().data_ptr(),
+            resid_out.data_ptr(), norm.data_ptr(), n, D, w1.shape[0], float(eps),
+            int(normalized_dtype == torch.float16), mask_ptr, _stream(a)))
+    return resid_out, norm
