@@ -301,7 +301,7 @@ int launch_gemm_t(const GemmMaps& maps, GemmParams p, int sm_count, cudaStream_t
   if (items > 0x7fffffffLL) return fail(TT_ERR_SHAPE, "too many tiles");
   p.n_items = static_cast<int>(items);
   const unsigned grid = static_cast<unsigned>(items < sm_count ? items : sm_count);
-  kern<<<grid, 192, smem, stream>>>(maps, p);
+  kern<<<grid, gemm_threads(EPI), smem, stream>>>(maps, p);
   return after_launch("gemm");
 }
 

@@ -81,8 +81,13 @@ __host__ __device__ inline int gemm_acc_stride(int bn) {
 }
 __host__ __device__ inline int gemm_n_acc(int bn) { return bn <= 256 ? 2 : 1; }
 __host__ __device__ inline int gemm_tmem_cols(int bn) { return gemm_n_acc(bn) * gemm_acc_stride(bn); }
+// Epilogue warps: the LayerNorm epilogue keeps a whole row per thread (4 warps,
+// one per TMEM lane quadrant); the others pair two warps on each quadrant and
+// split its columns, so every SM sub-partition has two epilogue warps.
+__host__ __device__ constexpr int gemm_epi_warps(int epi) { return epi == EPI_RESID_LN ? 4 : 8; }
+__host__ __device__ constexpr int gemm_threads(int epi) { return 32 * (gemm_epi_warps(epi) + 2); }
 __host__ __device__ inline int gemm_epi_bytes(int epi) {
-  return 4 * ((epi == EPI_RESID_LN ? kResRing : 0) + kOutRing) * kEpiTile;
+  return gemm_epi_warps(epi) * ((epi == EPI_RESID_LN ? kResRing : 0) + kOutRing) * kEpiTile;
 }
 // Layout: stages | epilogue tiles | bias[N_total], gamma[bn], beta[bn] | barriers | misc
 // (+1024 alignment slack)
@@ -180,8 +185,11 @@ struct OutRing {
 };
 
 template <int KSW, int EPI>
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(gemm_threads(EPI), 1)
     gemm_kernel(const __grid_constant__ GemmMaps maps, const GemmParams p) {
+  constexpr int NEPI = gemm_epi_warps(EPI);  // epilogue warps 0..NEPI-1
+  constexpr int NSTEP = NEPI / 4;            // warps sharing one TMEM lane quadrant
+  constexpr int W_PROD = NEPI, W_MMA = NEPI + 1;
   constexpr int A_BYTES = 128 * KSW * 2;
   constexpr uint32_t kSw = swizzle_kind_for_bytes(KSW * 2);
   constexpr uint32_t kSbo = 8 * KSW * 2;
@@ -218,7 +226,7 @@ __global__ void __launch_bounds__(192, 1)
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&acc_full[i], 1);
-      mbar_init(&acc_empty[i], 4);
+      mbar_init(&acc_empty[i], NEPI);
     }
     for (int i = 0; i < 4 * kResRing; ++i) mbar_init(&res_full[i], 1);
     mbar_init(done, 1);
@@ -232,7 +240,7 @@ __global__ void __launch_bounds__(192, 1)
       s_beta[c] = p.beta[c];
     }
   }
-  if (warp == 5) {
+  if (warp == W_MMA) {
     tmem_alloc(tmem_slot, tmem_cols);
     tmem_relinquish();
   }
@@ -242,7 +250,7 @@ __global__ void __launch_bounds__(192, 1)
   const uint32_t tmem_base = *tmem_slot;
   const Watchdog wd{p.err, abort_flag, p.timeout_ns};
 
-  if (warp == 4) {
+  if (warp == W_PROD) {
     // ------------------------------------------------------------ producer
     if (lane == 0) {
       tma_prefetch_desc(&maps.a);
@@ -266,7 +274,7 @@ __global__ void __launch_bounds__(192, 1)
       for (int i = (g > nst ? g - nst : 0); i < g; ++i)
         wait_drain(&full[i % nst], (i / nst) & 1, kDrainLimitNs);
     }
-  } else if (warp == 5) {
+  } else if (warp == W_MMA) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
       const uint32_t idesc = umma_idesc_f16_f32(128, bn > 256 ? 256 : bn);
@@ -301,8 +309,10 @@ __global__ void __launch_bounds__(192, 1)
     }
   } else {
     // ------------------------------------------------------------ epilogue
-    const int r = lane;  // row within this warp's 32-row slab
-    const uint32_t lane_base = static_cast<uint32_t>(warp * 32) << 16;
+    const int r = lane;         // row within this warp's 32-row slab
+    const int eq = warp & 3;    // TMEM lane quadrant (rows eq*32 .. eq*32+31 of the tile)
+    const int ehalf = warp >> 2;  // which of the NSTEP warps on this quadrant
+    const uint32_t lane_base = static_cast<uint32_t>(eq * 32) << 16;
     constexpr int kRes = (EPI == EPI_RESID_LN) ? kResRing : 0;
     const uint32_t res_base = smem_u32(epi) + warp * (kRes + kOutRing) * kEpiTile;
     OutRing ring{res_base + kRes * kEpiTile, 0};
@@ -313,7 +323,7 @@ __global__ void __launch_bounds__(192, 1)
     for (int w = blockIdx.x; ok && w < p.n_items; w += gridDim.x, ++i) {
       const int m0 = (w / p.n_splits) * 128;
       const int n0 = (w % p.n_splits) * bn;
-      const int r0 = m0 + warp * 32;  // first row of this warp's slab
+      const int r0 = m0 + eq * 32;  // first row of this warp's slab
       const int row = r0 + r;
       const bool valid = row < p.M;
       const bool warp_active = r0 < p.M;
@@ -341,14 +351,30 @@ __global__ void __launch_bounds__(192, 1)
         const int b_w = warp_active ? r0 / p.seq : 0;
         const int s0 = warp_active ? r0 - b_w * p.seq : 0;
         const int wbox = hd < 32 ? hd : 32;  // columns per sub-box
-        for (int c = 0; c < nch; ++c) {
-          uint32_t v[32];
+        // This warp takes chunks ehalf, ehalf + NSTEP, ...; two TMEM loads per wait.
+        for (int cb = ehalf; cb < nch; cb += 2 * NSTEP) {
+          uint32_t vv[2][32];
           __syncwarp();
-          tmem_ld_x32_sync(taddr + c * 32, v);
+          tmem_ld_x32(taddr + cb * 32, vv[0]);
+          if (cb + NSTEP < nch) tmem_ld_x32(taddr + (cb + NSTEP) * 32, vv[1]);
+          tmem_ld_wait_tied(vv[0]);
+          tmem_ld_wait_tied(vv[1]);
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {
+          const int c = cb + u * NSTEP;
+          if (c >= nch) break;
+          const uint32_t (&v)[32] = vv[u];
           const int col0 = n0 + c * 32;
           float f[32];
+          const float4* b4 = reinterpret_cast<const float4*>(s_bias + col0);
 #pragma unroll
-          for (int e = 0; e < 32; ++e) f[e] = __uint_as_float(v[e]) + s_bias[col0 + e];
+          for (int e = 0; e < 8; ++e) {
+            const float4 bb = b4[e];
+            f[4 * e + 0] = __uint_as_float(v[4 * e + 0]) + bb.x;
+            f[4 * e + 1] = __uint_as_float(v[4 * e + 1]) + bb.y;
+            f[4 * e + 2] = __uint_as_float(v[4 * e + 2]) + bb.z;
+            f[4 * e + 3] = __uint_as_float(v[4 * e + 3]) + bb.w;
+          }
           const int which = col0 / D;
           const int within0 = col0 - which * D;
           if (p.tma_out) {
@@ -414,15 +440,31 @@ __global__ void __launch_bounds__(192, 1)
             }
           }
         }
+        }
       } else if constexpr (EPI == EPI_GELU) {
-        for (int c = 0; c < nch; ++c) {
-          uint32_t v[32];
+        for (int cb = ehalf; cb < nch; cb += 2 * NSTEP) {
+          uint32_t vv[2][32];
           __syncwarp();
-          tmem_ld_x32_sync(taddr + c * 32, v);
+          tmem_ld_x32(taddr + cb * 32, vv[0]);
+          if (cb + NSTEP < nch) tmem_ld_x32(taddr + (cb + NSTEP) * 32, vv[1]);
+          tmem_ld_wait_tied(vv[0]);
+          tmem_ld_wait_tied(vv[1]);
           if (!warp_active) continue;
-          float gl[32];
 #pragma unroll
-          for (int e = 0; e < 32; ++e) gl[e] = gelu_erf(__uint_as_float(v[e]) + s_bias[n0 + c * 32 + e]);
+        for (int u = 0; u < 2; ++u) {
+          const int c = cb + u * NSTEP;
+          if (c >= nch) break;
+          const uint32_t (&v)[32] = vv[u];
+          float gl[32];
+          const float4* b4 = reinterpret_cast<const float4*>(s_bias + n0 + c * 32);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) {
+            const float4 bb = b4[e];
+            gl[4 * e + 0] = gelu_erf(__uint_as_float(v[4 * e + 0]) + bb.x);
+            gl[4 * e + 1] = gelu_erf(__uint_as_float(v[4 * e + 1]) + bb.y);
+            gl[4 * e + 2] = gelu_erf(__uint_as_float(v[4 * e + 2]) + bb.z);
+            gl[4 * e + 3] = gelu_erf(__uint_as_float(v[4 * e + 3]) + bb.w);
+          }
           const uint32_t slot = ring.acquire(lane);
           stage_row_f16x32(slot, r, gl);
           ring.publish();
@@ -430,6 +472,7 @@ __global__ void __launch_bounds__(192, 1)
             tma_store_2d(&maps.out0, slot, n0 + c * 32, r0);
             bulk_commit_group();
           }
+        }
         }
       } else {
         // EPI_RESID_LN: bn == N_total == d_model (the whole row lives in TMEM).
@@ -484,23 +527,39 @@ __global__ void __launch_bounds__(192, 1)
         tmem_st_wait();
         const float mean = sum / static_cast<float>(D);
         float sq = 0.f;
-        for (int c = 0; c < nch; ++c) {
-          uint32_t v[32];
+        for (int cb = 0; cb < nch; cb += 4) {
+          uint32_t vv[4][32];
           __syncwarp();
-          tmem_ld_x32_sync(taddr + c * 32, v);
 #pragma unroll
-          for (int e = 0; e < 32; ++e) {
-            const float d = __uint_as_float(v[e]) - mean;
-            sq = fmaf(d, d, sq);
+          for (int u = 0; u < 4; ++u)
+            if (cb + u < nch) tmem_ld_x32(taddr + (cb + u) * 32, vv[u]);
+#pragma unroll
+          for (int u = 0; u < 4; ++u) tmem_ld_wait_tied(vv[u]);
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            if (cb + u >= nch) break;
+#pragma unroll
+            for (int e = 0; e < 32; ++e) {
+              const float d = __uint_as_float(vv[u][e]) - mean;
+              sq = fmaf(d, d, sq);
+            }
           }
         }
         const float rstd = rsqrtf(sq / static_cast<float>(D) + p.eps);
         const bool zero_row = valid && p.row_mask != nullptr && p.row_mask[row] == 0;
-        for (int c = 0; c < nch; ++c) {
-          uint32_t v[32];
+        for (int cb = 0; cb < nch; cb += 2) {
+          uint32_t vv[2][32];
           __syncwarp();
-          tmem_ld_x32_sync(taddr + c * 32, v);
+          tmem_ld_x32(taddr + cb * 32, vv[0]);
+          if (cb + 1 < nch) tmem_ld_x32(taddr + (cb + 1) * 32, vv[1]);
+          tmem_ld_wait_tied(vv[0]);
+          tmem_ld_wait_tied(vv[1]);
           if (!warp_active) continue;
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {
+          const int c = cb + u;
+          if (c >= nch) break;
+          const uint32_t (&v)[32] = vv[u];
           float y[32];
 #pragma unroll
           for (int e = 0; e < 32; ++e)
@@ -517,6 +576,7 @@ __global__ void __launch_bounds__(192, 1)
             tma_store_2d(&maps.out1, slot, n0 + c * 32, r0);
             bulk_commit_group();
           }
+        }
         }
       }
       // The accumulator buffer may be overwritten by the next item's MMAs.
@@ -535,7 +595,7 @@ __global__ void __launch_bounds__(192, 1)
 
   tc_fence_before();
   __syncthreads();
-  if (warp == 5) {
+  if (warp == W_MMA) {
     tc_fence_after();
     tmem_dealloc(tmem_base, tmem_cols);
   }
