@@ -1,0 +1,454 @@
+// Causal attention forward for head_dim 16 and 32 (sm_100a).
+//
+// Same contract as attn_fwd_kernel (tt_attention.cuh; replaces
+// custom_kernel/triton_attention.py:126-232 of the reference).  At these head
+// sizes the tensor-core work is small and the softmax (one exponential per
+// score) bounds the kernel, so the layout keeps the softmax warps from ever
+// waiting on the tensor core:
+//
+//  * one CTA per SM runs two independent pipelines ("streams"), each on a
+//    128-query tile of its own work item, with 4 softmax warps (one per TMEM
+//    lane quadrant, a whole row per thread), its own TMA producer warp (8 + s)
+//    and its own MMA-issuer warp (10 + s);
+//  * key tiles are 64 wide and both the scores S (TMEM) and the probabilities
+//    P (shared memory) are double buffered, so S_{t+1} and S_{t+2} are computed
+//    and P_{t-1} is consumed while the softmax works on tile t.
+//
+// Per stream and key tile t (buffer b = t & 1):
+//   S_b = Q K_t^T           TMEM, 64 FP32 columns
+//   softmax: the 64 scores of a row come into registers in one TMEM read and
+//   S_b is released at once; row max by a 3-input max tree; the reference
+//   maximum m only moves when the tile maximum exceeds it by more than 2^8
+//   (O and l are then rescaled, rare after the first tiles), so P stays <= 256
+//   in FP16; exp2 of S*scale*log2(e) - m (MUFU, with a share of the
+//   exponentials on the FP32 pipe); l accumulates the FP32 probabilities; P is
+//   rounded to FP16 into the 128B-swizzled K-major tile P_b
+//   O += P_b V_t            TMEM, accumulated over the item's key tiles (two
+//                           buffers by item, so an item's epilogue runs after
+//                           the next item's first tile)
+// Items (sequence*head, query tile) are dealt heavy-first: stream s of CTA c
+// takes items 2c+s, 2c+s+2G, ... (G = gridDim.x).
+#pragma once
+
+#include "tt_attention.cuh"
+
+namespace tt {
+
+template <int HD>
+struct AttnDbLayout {
+  static constexpr int BM = 128, BN = 64, NST = (HD == 16 ? 8 : 6);
+  static constexpr int Q_BYTES = BM * HD * 2;
+  static constexpr int K_BYTES = BN * HD * 2;
+  static constexpr int V_BYTES = HD * 128;  // V^T block: HD rows of 64 keys (128 bytes)
+  static constexpr int P_BYTES = BM * BN * 2;
+  // Per-stream region: Q[2] | K[NST] | V[NST] | P[2]
+  static constexpr int S_Q = 0;
+  static constexpr int S_K = S_Q + 2 * Q_BYTES;
+  static constexpr int S_V = S_K + NST * K_BYTES;
+  static constexpr int S_P = S_V + NST * V_BYTES;
+  static constexpr int STREAM_BYTES = S_P + 2 * P_BYTES;
+  // Per-stream barriers: q_full[2] q_empty[2] kv_full[NST] kv_empty[NST]
+  // s_full[2] s_free[2] p_full[2] p_empty[2] o_full[2] o_free[2]
+  static constexpr int B_QF = 0, B_QE = 2, B_KF = 4, B_KE = 4 + NST, B_SF = 4 + 2 * NST,
+                       B_SR = B_SF + 2, B_PF = B_SF + 4, B_PE = B_SF + 6, B_OF = B_SF + 8,
+                       B_OR = B_SF + 10;
+  static constexpr int NBAR_STREAM = B_SF + 12;
+  static constexpr int OFF_BAR = 2 * STREAM_BYTES;
+  static constexpr int OFF_DONE = OFF_BAR + 2 * NBAR_STREAM * 8;  // done[2]
+  static constexpr int OFF_MISC = OFF_DONE + 16;
+  static constexpr int SMEM_ALLOC = OFF_MISC + 16 + 1024;
+  // TMEM per stream: S_0 at 0, S_1 at 64, O of item buffer ob at 128 + ob * HD.
+  static constexpr int TMEM_COLS = 512, TMEM_STREAM = 256, TMEM_O = 128;
+  static constexpr int THREADS = 384;  // 8 softmax warps, 2 producers, 2 MMA issuers
+  // Register split (setmaxnreg): the launch provides 384 x 168.
+  static constexpr int REGS_LAUNCH = 168, REGS_SOFTMAX = 216, REGS_OTHER = 56;
+  static_assert(256 * REGS_SOFTMAX + 128 * REGS_OTHER <= THREADS * REGS_LAUNCH, "register split");
+  static_assert(TMEM_O + 2 * HD <= TMEM_STREAM, "TMEM budget");
+  static_assert(HD == 16 || HD == 32, "this kernel covers head_dim 16 and 32");
+  static_assert(STREAM_BYTES % 1024 == 0 && S_V % 1024 == 0 && S_P % 1024 == 0 && V_BYTES % 1024 == 0,
+                "alignment");
+  static_assert(SMEM_ALLOC <= 232448, "shared memory budget");
+};
+
+// Pairs of exponentials per 8 computed by polynomial on the FP32 pipe instead
+// of MUFU.
+constexpr int kDbExpFmaOf8 = 2;
+
+template <int HD>
+__global__ void __launch_bounds__(384, 1)
+    attn_db_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                       const __grid_constant__ CUtensorMap tmV, const AttnParams p, int n_items) {
+  using L = AttnDbLayout<HD>;
+  constexpr int BM = L::BM, BN = L::BN, NST = L::NST;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n_qt = (p.seq + BM - 1) / BM;
+  const int D = p.heads * HD;
+  const int G2 = 2 * static_cast<int>(gridDim.x);
+  uint64_t* bars_all = reinterpret_cast<uint64_t*>(smem + L::OFF_BAR);
+  uint64_t* done = reinterpret_cast<uint64_t*>(smem + L::OFF_DONE);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::OFF_MISC);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::OFF_MISC + 4);
+
+  if (threadIdx.x == 0) {
+    mbar_init(&done[0], 1);
+    mbar_init(&done[1], 1);
+    for (int s = 0; s < 2; ++s) {
+      uint64_t* b = bars_all + s * L::NBAR_STREAM;
+      for (int i = 0; i < 2; ++i) {
+        mbar_init(&b[L::B_QF + i], 1);
+        mbar_init(&b[L::B_QE + i], 1);
+        mbar_init(&b[L::B_SF + i], 1);
+        mbar_init(&b[L::B_SR + i], 4);
+        mbar_init(&b[L::B_PF + i], 4);
+        mbar_init(&b[L::B_PE + i], 1);
+        mbar_init(&b[L::B_OF + i], 1);
+        mbar_init(&b[L::B_OR + i], 4);
+      }
+      for (int i = 0; i < NST; ++i) {
+        mbar_init(&b[L::B_KF + i], 1);
+        mbar_init(&b[L::B_KE + i], 1);
+      }
+    }
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 10) {
+    tmem_alloc(tmem_slot, L::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  const Watchdog wd{p.err, abort_flag, p.timeout_ns};
+
+  // Key tiles of an item (64 keys each).
+  auto n_tiles = [&](const AttnItem& it) -> int {
+    if (it.n == 0) return 0;
+    const int kv_limit = p.causal ? min(it.q0 + BM, it.kv_end) : it.kv_end;
+    return (kv_limit + BN - 1) / BN;
+  };
+  auto first_item = [&](int w) -> int {  // first item >= w of this stream with work
+    while (w < n_items && attn_item(p, w, n_qt).n == 0) w += G2;
+    return w;
+  };
+
+  if (warp == 8 || warp == 9) {
+    // ------------------------------------------------------------ producer of stream warp-8
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(L::REGS_OTHER));
+    if (lane == 0) {
+      const int s = warp - 8;
+      uint64_t* b = bars_all + s * L::NBAR_STREAM;
+      uint8_t* sb = smem + s * L::STREAM_BYTES;
+      tma_prefetch_desc(&tmQ);
+      tma_prefetch_desc(&tmK);
+      tma_prefetch_desc(&tmV);
+      int t = 0, it = 0;
+      bool ok = true;
+      for (int w = first_item(2 * static_cast<int>(blockIdx.x) + s); ok && w < n_items;
+           w = first_item(w + G2)) {
+        const AttnItem item = attn_item(p, w, n_qt);
+        const int nt = n_tiles(item);
+        const int qb = it & 1;
+        if (!(ok = wait_phase(&b[L::B_QE + qb], ((it >> 1) & 1) ^ 1, wd, 0x131))) break;
+        mbar_arrive_expect_tx(&b[L::B_QF + qb], L::Q_BYTES);
+        tma_load_3d(sb + L::S_Q + qb * L::Q_BYTES, &tmQ, &b[L::B_QF + qb], 0, item.q0, item.bh);
+        ++it;
+        for (int j = 0; j < nt; ++j) {
+          const int st = t % NST;
+          if (!(ok = wait_phase(&b[L::B_KE + st], ((t / NST) & 1) ^ 1, wd, 0x132))) break;
+          mbar_arrive_expect_tx(&b[L::B_KF + st], L::K_BYTES + L::V_BYTES);
+          tma_load_3d(sb + L::S_K + st * L::K_BYTES, &tmK, &b[L::B_KF + st], 0, j * BN, item.bh);
+          tma_load_3d(sb + L::S_V + st * L::V_BYTES, &tmV, &b[L::B_KF + st], j * BN, 0, item.bh);
+          ++t;
+        }
+      }
+      // Let every copy this stream started land before the CTA may exit.
+      for (int i = (it > 2 ? it - 2 : 0); i < it; ++i)
+        wait_drain(&b[L::B_QF + (i & 1)], (i >> 1) & 1, kDrainLimitNs);
+      for (int i = (t > NST ? t - NST : 0); i < t; ++i)
+        wait_drain(&b[L::B_KF + i % NST], (i / NST) & 1, kDrainLimitNs);
+    }
+  } else if (warp == 10 || warp == 11) {
+    // ------------------------------------------------------------ MMA issuer of stream warp-10
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(L::REGS_OTHER));
+    if (lane == 0) {
+      const int s = warp - 10;
+      uint64_t* b = bars_all + s * L::NBAR_STREAM;
+      const uint32_t sb = smem_u32(smem + s * L::STREAM_BYTES);
+      const uint32_t tS = tmem_base + s * L::TMEM_STREAM;
+      constexpr uint32_t kSwQK = swizzle_kind_for_bytes(HD * 2);
+      constexpr uint32_t kSboQK = 8 * HD * 2;
+      const uint32_t idesc_s = umma_idesc_f16_f32(BM, BN);
+      const uint32_t idesc_o = umma_idesc_f16_f32(BM, HD);
+      // S cursor: item w_s, tile j_s of n_s, stream tile u, item count it_s.
+      int w_s = first_item(2 * static_cast<int>(blockIdx.x) + s), j_s = 0, n_s = 0, u = 0, it_s = 0;
+      if (w_s < n_items) n_s = n_tiles(attn_item(p, w_s, n_qt));
+      auto issue_s = [&]() -> bool {
+        const int st = u % NST, qb = it_s & 1, bb = u & 1;
+        if (j_s == 0 && !wait_phase(&b[L::B_QF + qb], (it_s >> 1) & 1, wd, 0x231)) return false;
+        if (!wait_phase(&b[L::B_KF + st], (u / NST) & 1, wd, 0x232)) return false;
+        // S buffer bb was last read by the softmax at tile u - 2.
+        if (u >= 2 && !wait_phase(&b[L::B_SR + bb], ((u >> 1) - 1) & 1, wd, 0x233)) return false;
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < HD / 16; ++kk) {
+          const uint64_t da = umma_sdesc(sb + L::S_Q + qb * L::Q_BYTES + kk * 32, kSboQK, kSwQK);
+          const uint64_t db = umma_sdesc(sb + L::S_K + st * L::K_BYTES + kk * 32, kSboQK, kSwQK);
+          umma_f16(tS + bb * BN, da, db, idesc_s, kk > 0 ? 1u : 0u);
+        }
+        umma_commit(&b[L::B_SF + bb]);
+        if (j_s == n_s - 1) umma_commit(&b[L::B_QE + qb]);
+        ++u;
+        if (++j_s == n_s) {
+          j_s = 0;
+          ++it_s;
+          w_s = first_item(w_s + G2);
+          n_s = w_s < n_items ? n_tiles(attn_item(p, w_s, n_qt)) : 0;
+        }
+        return true;
+      };
+      // P.V cursor: items it_o (O buffer it_o & 1), tile j_o of n_o.
+      int w_o = first_item(2 * static_cast<int>(blockIdx.x) + s), j_o = 0, it_o = 0;
+      int n_o = w_o < n_items ? n_tiles(attn_item(p, w_o, n_qt)) : 0;
+      bool ok = true;
+      for (int t = 0; ok; ++t) {
+        // Keep the scores up to two tiles ahead of P.V: S_{t+2} only needs the
+        // softmax to have read S_t, which it does before publishing P_t.
+        while (ok && w_s < n_items && u <= t + 2) ok = issue_s();
+        if (!ok || t >= u) break;
+        const int bb = t & 1, st = t % NST, ob = it_o & 1;
+        if (!(ok = wait_phase(&b[L::B_PF + bb], (t >> 1) & 1, wd, 0x234))) break;
+        if (j_o == 0 && !(ok = wait_phase(&b[L::B_OR + ob], ((it_o >> 1) & 1) ^ 1, wd, 0x235))) break;
+        tc_fence_after();
+        const uint32_t tO = tS + L::TMEM_O + ob * HD;
+#pragma unroll
+        for (int kk = 0; kk < BN / 16; ++kk) {
+          const uint64_t da = umma_sdesc(sb + L::S_P + bb * L::P_BYTES + kk * 32, 1024, kSw128);
+          const uint64_t db = umma_sdesc(sb + L::S_V + st * L::V_BYTES + kk * 32, 1024, kSw128);
+          umma_f16(tO, da, db, idesc_o, (kk > 0 || j_o > 0) ? 1u : 0u);
+        }
+        umma_commit(&b[L::B_KE + st]);
+        umma_commit(&b[L::B_PE + bb]);
+        if (++j_o == n_o) {
+          umma_commit(&b[L::B_OF + ob]);  // O of this item is final
+          j_o = 0;
+          ++it_o;
+          w_o = first_item(w_o + G2);
+          n_o = w_o < n_items ? n_tiles(attn_item(p, w_o, n_qt)) : 0;
+        }
+      }
+      // All MMAs this thread issued must finish before TMEM is released.
+      umma_commit(&done[s]);
+      wait_drain(&done[s], 0, kDrainLimitNs);
+    }
+  } else {
+    // ------------------------------------------------------------ softmax
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(L::REGS_SOFTMAX));
+    const int s = warp >> 2;  // stream
+    const int q = warp & 3;   // TMEM lane quadrant
+    const int row = q * 32 + lane;
+    uint64_t* b = bars_all + s * L::NBAR_STREAM;
+    const uint32_t tS = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + s * L::TMEM_STREAM;
+    const uint32_t p_row = smem_u32(smem + s * L::STREAM_BYTES + L::S_P) + row * 128;
+    const float sl2 = p.scale_log2;
+    const uint64_t sl2x2 = f2_pack(sl2, sl2);
+    bool ok = true;
+    int t = 0, it = 0;
+    // An item's epilogue runs after the next item's first key tile, by when
+    // its last P.V has long finished.
+    bool pend = false;
+    int pend_it = 0;
+    __half* pend_dst = nullptr;
+    bool pend_store = false;
+    float pend_inv = 0.f;
+    auto finish_item = [&]() -> bool {
+      const int ob = pend_it & 1;
+      if (!warp_wait_phase(&b[L::B_OF + ob], (pend_it >> 1) & 1, wd, 0x333)) return false;
+      tc_fence_after();
+      uint32_t o[HD];
+      if constexpr (HD == 32) {
+        tmem_ld_x32(tS + L::TMEM_O + ob * HD, o);
+      } else {
+        tmem_ld_x16(tS + L::TMEM_O + ob * HD, o);
+      }
+      tmem_ld_wait_tied(o);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&b[L::B_OR + ob]);
+      pend = false;
+      if (pend_store) {
+#pragma unroll
+        for (int i = 0; i < HD / 8; ++i) {
+          uint4 v;
+          v.x = pack_half2(__uint_as_float(o[8 * i + 0]) * pend_inv, __uint_as_float(o[8 * i + 1]) * pend_inv);
+          v.y = pack_half2(__uint_as_float(o[8 * i + 2]) * pend_inv, __uint_as_float(o[8 * i + 3]) * pend_inv);
+          v.z = pack_half2(__uint_as_float(o[8 * i + 4]) * pend_inv, __uint_as_float(o[8 * i + 5]) * pend_inv);
+          v.w = pack_half2(__uint_as_float(o[8 * i + 6]) * pend_inv, __uint_as_float(o[8 * i + 7]) * pend_inv);
+          reinterpret_cast<uint4*>(pend_dst)[i] = v;
+        }
+      }
+      return true;
+    };
+
+    for (int w = 2 * static_cast<int>(blockIdx.x) + s; ok && w < n_items; w += G2) {
+      const AttnItem item = attn_item(p, w, n_qt);
+      const int qi = item.q0 + row;
+      __half* dst_row = p.ctx + (static_cast<size_t>(item.b) * p.seq + qi) * D + item.h * HD;
+      const int nt = n_tiles(item);
+      if (nt == 0) {
+        if (qi < p.seq) {
+#pragma unroll
+          for (int i = 0; i < HD / 8; ++i) reinterpret_cast<uint4*>(dst_row)[i] = make_uint4(0, 0, 0, 0);
+        }
+        continue;
+      }
+      const int row_lim = p.causal ? min(qi + 1, item.kv_end) : item.kv_end;
+      const int ob = it & 1;
+      const uint32_t tO = tS + L::TMEM_O + ob * HD;
+      float m_run = -INFINITY;  // reference maximum of this row (log2 units)
+      uint64_t l2 = 0;          // row sum, as two partial sums
+
+      for (int j = 0; j < nt; ++j, ++t) {
+        const int bb = t & 1;
+        const int k0 = j * BN;
+        uint32_t vb[2] = {~0u, ~0u};
+        bool mask_partial = false;
+        if (p.key_mask != nullptr) {
+          const uint8_t* mrow = p.key_mask + static_cast<size_t>(item.b) * p.seq;
+#pragma unroll
+          for (int g = 0; g < 2; ++g) {
+            const int ka = k0 + lane + 32 * g;
+            vb[g] = __ballot_sync(~0u, ka < p.seq && mrow[min(ka, p.seq - 1)] != 0);
+          }
+          mask_partial = (vb[0] & vb[1]) != ~0u;
+        }
+        // Warp-uniform: the masking branch sits between warp-collective TMEM operations.
+        const bool need_mask = __any_sync(0xffffffffu, mask_partial || (k0 + BN > row_lim));
+        const int lim = row_lim - k0;
+
+        if (!(ok = warp_wait_phase(&b[L::B_SF + bb], (t >> 1) & 1, wd, 0x331))) break;
+        tc_fence_after();
+        uint32_t sc[2][32];
+        tmem_ld_x32(tS + bb * BN, sc[0]);
+        tmem_ld_x32(tS + bb * BN + 32, sc[1]);
+        tmem_ld_wait_tied(sc[0]);
+        tmem_ld_wait_tied(sc[1]);
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&b[L::B_SR + bb]);
+        if (need_mask) {
+#pragma unroll
+          for (int g = 0; g < 2; ++g) {
+            const int l0 = lim - g * 32;  // keys of this group at or below the causal limit
+            const uint32_t bits = (l0 >= 32 ? ~0u : (l0 <= 0 ? 0u : ((1u << l0) - 1u))) & vb[g];
+            if (bits != ~0u) {
+#pragma unroll
+              for (int i = 0; i < 32; ++i)
+                if (!(bits & (1u << i))) sc[g][i] = 0xff800000u;  // -inf
+            }
+          }
+        }
+        float mg[2];
+#pragma unroll
+        for (int g = 0; g < 2; ++g) {
+          float a[11];
+#pragma unroll
+          for (int i = 0; i < 10; ++i)
+            a[i] = max3(__uint_as_float(sc[g][3 * i]), __uint_as_float(sc[g][3 * i + 1]),
+                        __uint_as_float(sc[g][3 * i + 2]));
+          a[10] = fmaxf(__uint_as_float(sc[g][30]), __uint_as_float(sc[g][31]));
+          mg[g] = max3(max3(a[0], a[1], a[2]), max3(a[3], a[4], a[5]), max3(a[6], a[7], max3(a[8], a[9], a[10])));
+        }
+        const float m_tile = fmaxf(mg[0], mg[1]) * sl2;
+        // Rows that have seen no valid key hold nothing in O and take the new
+        // maximum without a rescale.
+        float m_new = m_run;
+        bool resc = false;
+        if (m_tile > m_run + 8.0f) {
+          resc = (m_run != -INFINITY);
+          m_new = m_tile;
+        }
+        const float m_use = (m_new == -INFINITY) ? 0.f : m_new;
+
+        if (__any_sync(0xffffffffu, resc)) {
+          // O must hold every earlier tile: wait for P.V of tile t-1 (j > 0 here).
+          const int tp = t - 1;
+          if (!(ok = warp_wait_phase(&b[L::B_PE + (tp & 1)], (tp >> 1) & 1, wd, 0x332))) break;
+          tc_fence_after();
+          const float corr = resc ? ex2_approx(m_run - m_new) : 1.f;
+          l2 = fmul2(l2, f2_pack(corr, corr));
+#pragma unroll 1
+          for (int c = 0; c < HD; c += 16) {  // 16 columns at a time: the scores stay in registers
+            uint32_t o[16];
+            tmem_ld_x16_sync(tO + c, o);
+#pragma unroll
+            for (int d = 0; d < 16; ++d) o[d] = __float_as_uint(__uint_as_float(o[d]) * corr);
+            tmem_st_x16(tO + c, o);
+          }
+          tmem_st_wait();
+        }
+        m_run = m_new;
+
+        // P buffer bb was last read by P.V of tile t-2.
+        if (!(ok = warp_wait_phase(&b[L::B_PE + bb], ((t >> 1) & 1) ^ 1, wd, 0x334))) break;
+        // Probabilities: FP32 row sum, FP16 into P_bb.
+        const uint64_t negm = f2_pack(-m_use, -m_use);
+        const uint32_t prow = p_row + bb * L::P_BYTES;
+#pragma unroll
+        for (int g = 0; g < 2; ++g) {
+          uint32_t pk[16];
+#pragma unroll
+          for (int e = 0; e < 16; ++e) {
+            const uint64_t xx =
+                ffma2(f2_pack(__uint_as_float(sc[g][2 * e]), __uint_as_float(sc[g][2 * e + 1])), sl2x2, negm);
+            uint64_t pp;
+            if ((e & 7) < kDbExpFmaOf8)
+              pp = exp2_pair_fma(xx);
+            else
+              pp = f2_pack(ex2_approx(f2_lo(xx)), ex2_approx(f2_hi(xx)));
+            l2 = fadd2(l2, pp);
+            pk[e] = pack_half2(f2_lo(pp), f2_hi(pp));
+          }
+#pragma unroll
+          for (int qq = 0; qq < 4; ++qq) {
+            const int ch = g * 4 + qq;  // 16-byte chunk of the 128-byte row
+            st_shared_v4(prow + ((ch ^ (row & 7)) << 4), pk[4 * qq], pk[4 * qq + 1], pk[4 * qq + 2],
+                         pk[4 * qq + 3]);
+          }
+        }
+        fence_proxy_async_smem();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&b[L::B_PF + bb]);
+        if (j == 0 && pend && !(ok = finish_item())) break;
+      }
+      if (!ok) break;
+
+      pend = true;
+      pend_it = it;
+      pend_dst = dst_row;
+      pend_store = qi < p.seq;
+      {
+        const bool row_valid =
+            p.key_mask == nullptr || (pend_store && p.key_mask[static_cast<size_t>(item.b) * p.seq + qi] != 0);
+        const float lsum = f2_lo(l2) + f2_hi(l2);
+        pend_inv = (row_valid && lsum > 0.f) ? 1.f / lsum : 0.f;
+      }
+      ++it;
+    }
+    if (ok && pend) ok = finish_item();
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 10) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, L::TMEM_COLS);
+  }
+}
+
+}  // namespace tt

@@ -16,7 +16,7 @@
 #include <vector>
 
 #include "tt_attention.cuh"
-#include "tt_attention2s.cuh"
+#include "tt_attn_db.cuh"
 #include "tt_ffn.cuh"
 #include "tt_gemm.cuh"
 #include "tt_misc.cuh"
@@ -336,7 +336,7 @@ int launch_ffn(const FfnMaps& maps, FfnParams p, int sm_count, cudaStream_t stre
     const int smem = FfnLayout<DD>::smem_bytes(p.F);                        \
     if (smem > 232448) return fail(TT_ERR_UNSUPPORTED, "ffn %d too wide", p.F); \
     if (int rc = prepare_kernel(kern, smem)) return rc;                     \
-    kern<<<grid, 320, smem, stream>>>(maps, p);                             \
+    kern<<<grid, kFfnThreads, smem, stream>>>(maps, p);                     \
     break;                                                                  \
   }
     TT_FFN_CASE(32)
@@ -407,7 +407,9 @@ int encode_attention_maps(CUtensorMap* tq, CUtensorMap* tk, CUtensorMap* tv, con
                                  static_cast<uint64_t>(hd) * seq * 2};
     const uint32_t box[3] = {static_cast<uint32_t>(hd), 128, 1};
     if (int rc = encode_f16(tq, q, 3, dims, strides, box)) return rc;
-    if (int rc = encode_f16(tk, k, 3, dims, strides, box)) return rc;
+    // Key tiles: 64 keys for head_dim <= 32 (attn_db_fwd_kernel), else 128.
+    const uint32_t kbox[3] = {static_cast<uint32_t>(hd), hd <= 32 ? 64u : 128u, 1};
+    if (int rc = encode_f16(tk, k, 3, dims, strides, kbox)) return rc;
   }
   {
     const uint64_t dims[3] = {static_cast<uint64_t>(seq_pad), static_cast<uint64_t>(hd),
@@ -428,13 +430,20 @@ int launch_attention(const CUtensorMap& tq, const CUtensorMap& tk, const CUtenso
   const int n_items = static_cast<int>(items);
   const unsigned grid = static_cast<unsigned>(n_items < sm_count ? n_items : sm_count);
   if (hd == 16 || hd == 32) {
-    // Two softmax streams per CTA (head_dim <= 32).
-    auto kern = hd == 16 ? attn2s_fwd_kernel<16> : attn2s_fwd_kernel<32>;
-    const int smem = hd == 16 ? Attn2sLayout<16>::SMEM_ALLOC : Attn2sLayout<32>::SMEM_ALLOC;
+    // Two streams per CTA, 64-key tiles, double-buffered scores and probabilities.
+    auto kern = hd == 16 ? attn_db_fwd_kernel<16> : attn_db_fwd_kernel<32>;
+    const int smem = hd == 16 ? AttnDbLayout<16>::SMEM_ALLOC : AttnDbLayout<32>::SMEM_ALLOC;
     if (int rc = prepare_kernel(kern, smem)) return rc;
+    // The kernel splits its registers with setmaxnreg; that split is only sound
+    // when each thread is launched with exactly the planned register count.
+    cudaFuncAttributes fa;
+    if (int rc = check_cuda(cudaFuncGetAttributes(&fa, kern), "cudaFuncGetAttributes")) return rc;
+    if (fa.numRegs != AttnDbLayout<32>::REGS_LAUNCH)
+      return fail(TT_ERR_UNSUPPORTED, "attention kernel built with %d registers per thread, expected %d",
+                  fa.numRegs, AttnDbLayout<32>::REGS_LAUNCH);
     const int ctas = (n_items + 1) / 2;
     const unsigned grid2 = static_cast<unsigned>(ctas < sm_count ? ctas : sm_count);
-    kern<<<grid2, 384, smem, stream>>>(tq, tk, tv, ap, n_items);
+    kern<<<grid2, AttnDbLayout<32>::THREADS, smem, stream>>>(tq, tk, tv, ap, n_items);
     (void)grid;
     (void)exp16;
   } else if (hd == 64) {

@@ -13,14 +13,14 @@
 // [128 x D] is loaded once; the hidden dimension is processed in chunks of
 // FC = 128 units:
 //   G1(c)  acc1[c&1] (TMEM, 128 x FC FP32) = A . W1[c]^T
-//   GELU   warps 0..3: acc1[c&1] + b1 -> GELU -> FP16 -> H[c&1] (shared,
+//   GELU   warps 0..7: acc1[c&1] + b1 -> GELU -> FP16 -> H[c&1] (shared,
 //          128B-swizzled K-major, the A operand of G2)
 //   G2(c)  acc2 (TMEM, 128 x D FP32) += H[c&1] . W2[:, c]^T
 // issued in the order G1(0) G1(1) G2(0) G1(2) G2(1) ... so GELU of chunk c+1
-// overlaps G2(c).  Warps 4..7 then drain acc2 (bias, residual, two-pass
+// overlaps G2(c).  Warps 8..11 then drain acc2 (bias, residual, two-pass
 // LayerNorm, TMA-staged stores) while the MMAs of the next tile's G1 run.
-// Warp 8 streams A and the W1/W2 K-blocks (32 columns, 64-byte swizzle) with
-// TMA; warp 9 allocates TMEM and issues tcgen05.mma.
+// Warp 12 streams A and the W1/W2 K-blocks (32 columns, 64-byte swizzle) with
+// TMA; warp 13 allocates TMEM and issues tcgen05.mma.
 #pragma once
 
 #include "tt_gemm.cuh"
@@ -76,8 +76,14 @@ struct FfnLayout {
   static int smem_bytes(int F) { return SMEM_BASE + F * 4; }
 };
 
+// Warp roles: 0..7 GELU (warp w: TMEM lane quadrant w & 3, hidden columns
+// 64 * (w >> 2) .. +63 of each chunk), 8..11 residual + LayerNorm, 12 TMA
+// producer, 13 TMEM allocator and MMA issuer.
+constexpr int kFfnThreads = 448;
+constexpr int kFfnWarpProd = 12, kFfnWarpMma = 13;
+
 template <int D>
-__global__ void __launch_bounds__(320, 1)
+__global__ void __launch_bounds__(kFfnThreads, 1)
     ffn_fused_kernel(const __grid_constant__ FfnMaps maps, const FfnParams p) {
   using L = FfnLayout<D>;
   constexpr int FC = L::FC, KSW = L::KSW, NST = L::NST;
@@ -116,8 +122,8 @@ __global__ void __launch_bounds__(320, 1)
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&acc1_full[i], 1);
-      mbar_init(&acc1_empty[i], 4);
-      mbar_init(&h_full[i], 4);
+      mbar_init(&acc1_empty[i], 8);
+      mbar_init(&h_full[i], 8);
       mbar_init(&h_empty[i], 1);
     }
     mbar_init(acc2_full, 1);
@@ -132,7 +138,7 @@ __global__ void __launch_bounds__(320, 1)
     s_gamma[c] = p.gamma[c];
     s_beta[c] = p.beta[c];
   }
-  if (warp == 9) {
+  if (warp == kFfnWarpMma) {
     tmem_alloc(tmem_slot, 512);
     tmem_relinquish();
   }
@@ -142,7 +148,7 @@ __global__ void __launch_bounds__(320, 1)
   const uint32_t tmem_base = *tmem_slot;
   const Watchdog wd{p.err, abort_flag, p.timeout_ns};
 
-  if (warp == 8) {
+  if (warp == kFfnWarpProd) {
     // ------------------------------------------------------------ producer
     if (lane == 0) {
       tma_prefetch_desc(&maps.a);
@@ -177,7 +183,7 @@ __global__ void __launch_bounds__(320, 1)
       for (int q = (g > NST ? g - NST : 0); q < g; ++q)
         wait_drain(&w_full[q % NST], (q / NST) & 1, kDrainLimitNs);
     }
-  } else if (warp == 9) {
+  } else if (warp == kFfnWarpMma) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
       constexpr uint32_t kSw = kSw64;
@@ -246,10 +252,11 @@ __global__ void __launch_bounds__(320, 1)
       umma_commit(done);
       wait_drain(done, 0, kDrainLimitNs);
     }
-  } else if (warp < 4) {
+  } else if (warp < 8) {
     // ------------------------------------------------------------ GELU warps
-    const uint32_t lane_base = static_cast<uint32_t>(warp * 32) << 16;
-    const int r = warp * 32 + lane;  // row within the tile == TMEM lane
+    const int gq = warp & 3, gh = warp >> 2;  // lane quadrant, column half of the chunk
+    const uint32_t lane_base = static_cast<uint32_t>(gq * 32) << 16;
+    const int r = gq * 32 + lane;  // row within the tile == TMEM lane
     const uint32_t sH = smem_u32(smem + L::OFF_H);
     int cg = 0;
     bool ok = true;
@@ -258,32 +265,36 @@ __global__ void __launch_bounds__(320, 1)
         const int c = cg + cc, ab = c & 1;
         if (!(ok = warp_wait_phase(&acc1_full[ab], (c >> 1) & 1, wd, 0x521))) break;
         tc_fence_after();
+        uint32_t v[2][32];
+        const uint32_t tsrc = tmem_base + lane_base + L::TMEM_ACC1 + ab * FC + gh * 64;
+        tmem_ld_x32(tsrc, v[0]);
+        tmem_ld_x32(tsrc + 32, v[1]);
+        tmem_ld_wait_tied(v[0]);
+        tmem_ld_wait_tied(v[1]);
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&acc1_empty[ab]);  // acc1 buffer may be overwritten
         if (!(ok = warp_wait_phase(&h_empty[ab], ((c >> 1) & 1) ^ 1, wd, 0x522))) break;
-        const uint32_t hrow = sH + ab * L::H_BYTES + r * 128;
+        // H block gh (64 hidden units = 128 bytes per row, 128B-swizzled).
+        const uint32_t hrow = sH + ab * L::H_BYTES + gh * (128 * 128) + r * 128;
 #pragma unroll
-        for (int q = 0; q < FC / 32; ++q) {
-          uint32_t v[32];
-          tmem_ld_x32_sync(tmem_base + lane_base + L::TMEM_ACC1 + ab * FC + q * 32, v);
-          if (q == FC / 32 - 1) {
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&acc1_empty[ab]);  // acc1 buffer may be overwritten
-          }
-          const float4* b4 = reinterpret_cast<const float4*>(s_b1 + cc * FC + q * 32);
+        for (int g = 0; g < 2; ++g) {
+          const float4* b4 = reinterpret_cast<const float4*>(s_b1 + cc * FC + gh * 64 + g * 32);
           uint32_t pk[16];
 #pragma unroll
           for (int e = 0; e < 8; ++e) {
             const float4 bb = b4[e];  // same address in every lane: a broadcast shared load
-            pk[2 * e] = pack_half2(gelu_erf(__uint_as_float(v[4 * e]) + bb.x),
-                                   gelu_erf(__uint_as_float(v[4 * e + 1]) + bb.y));
-            pk[2 * e + 1] = pack_half2(gelu_erf(__uint_as_float(v[4 * e + 2]) + bb.z),
-                                       gelu_erf(__uint_as_float(v[4 * e + 3]) + bb.w));
+            const uint64_t h01 = gelu_erf_pair(
+                fadd2(f2_pack(__uint_as_float(v[g][4 * e]), __uint_as_float(v[g][4 * e + 1])), f2_pack(bb.x, bb.y)));
+            const uint64_t h23 = gelu_erf_pair(
+                fadd2(f2_pack(__uint_as_float(v[g][4 * e + 2]), __uint_as_float(v[g][4 * e + 3])), f2_pack(bb.z, bb.w)));
+            pk[2 * e] = pack_half2(f2_lo(h01), f2_hi(h01));
+            pk[2 * e + 1] = pack_half2(f2_lo(h23), f2_hi(h23));
           }
 #pragma unroll
           for (int u = 0; u < 4; ++u) {
-            const int ch = q * 4 + u;  // 16-byte chunk (8 hidden units) of the 128-unit row
-            const uint32_t addr = hrow + (ch >> 3) * (128 * 128) + (((ch & 7) ^ (r & 7)) << 4);
-            st_shared_v4(addr, pk[4 * u], pk[4 * u + 1], pk[4 * u + 2], pk[4 * u + 3]);
+            const int ch = g * 4 + u;  // 16-byte chunk (8 hidden units) within the 64-unit block
+            st_shared_v4(hrow + ((ch ^ (r & 7)) << 4), pk[4 * u], pk[4 * u + 1], pk[4 * u + 2], pk[4 * u + 3]);
           }
         }
         fence_proxy_async_smem();
@@ -294,7 +305,7 @@ __global__ void __launch_bounds__(320, 1)
     }
   } else {
     // ------------------------------------------------------------ residual + LayerNorm warps
-    const int ew = warp - 4;  // TMEM lane quadrant
+    const int ew = warp - 8;  // TMEM lane quadrant
     const uint32_t lane_base = static_cast<uint32_t>(ew * 32) << 16;
     const uint32_t taddr = tmem_base + lane_base;
     OutRing ring{smem_u32(smem + L::OFF_EPI) + ew * 2 * kEpiTile, 0};
@@ -397,7 +408,7 @@ __global__ void __launch_bounds__(320, 1)
 
   tc_fence_before();
   __syncthreads();
-  if (warp == 9) {
+  if (warp == kFfnWarpMma) {
     tc_fence_after();
     tmem_dealloc(tmem_base, 512);
   }

@@ -92,7 +92,7 @@ __device__ __forceinline__ bool grid_failed(const Watchdog& wd) {
   return *reinterpret_cast<volatile unsigned int*>(wd.err) != 0u;
 }
 
-__device__ __noinline__ bool wait_slow(uint64_t* bar, uint32_t parity, const Watchdog& wd,
+__device__ __forceinline__ bool wait_slow(uint64_t* bar, uint32_t parity, const Watchdog& wd,
                                        uint32_t site) {
   const unsigned long long t0 = globaltimer_ns();
   while (true) {
@@ -336,6 +336,28 @@ __device__ __forceinline__ void tmem_st_x32(uint32_t taddr, const uint32_t (&r)[
       : "memory");
 }
 
+__device__ __forceinline__ void tmem_ld_x8(uint32_t taddr, uint32_t (&r)[8]) {
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+                 "=r"(r[7])
+               : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_st_x8(uint32_t taddr, const uint32_t (&r)[8]) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"r"(taddr),
+               "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7])
+               : "memory");
+}
+
+__device__ __forceinline__ void tmem_st_x16(uint32_t taddr, const uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
+      "{%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
+      "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]),
+      "r"(r[15])
+      : "memory");
+}
+
 __device__ __forceinline__ void tmem_ld_wait() {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
@@ -365,6 +387,14 @@ __device__ __forceinline__ void tmem_ld_wait_tied(uint32_t (&r)[16]) {
       : "memory");
 }
 
+__device__ __forceinline__ void tmem_ld_wait_tied(uint32_t (&r)[8]) {
+  asm volatile("tcgen05.wait::ld.sync.aligned;"
+               : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]),
+                 "+r"(r[7])
+               :
+               : "memory");
+}
+
 // Load 32 / 16 columns and wait for them (registers tied to the wait).
 __device__ __forceinline__ void tmem_ld_x32_sync(uint32_t taddr, uint32_t (&r)[32]) {
   tmem_ld_x32(taddr, r);
@@ -387,9 +417,66 @@ __device__ __forceinline__ float ex2_approx(float x) {
   return y;
 }
 
+// Packed FP32 pair arithmetic (sm_100): one instruction for two lanes of work.
+__device__ __forceinline__ uint64_t f2_pack(float lo, float hi) {
+  return (static_cast<uint64_t>(__float_as_uint(hi)) << 32) | __float_as_uint(lo);
+}
+__device__ __forceinline__ float f2_lo(uint64_t v) { return __uint_as_float(static_cast<uint32_t>(v)); }
+__device__ __forceinline__ float f2_hi(uint64_t v) { return __uint_as_float(static_cast<uint32_t>(v >> 32)); }
+__device__ __forceinline__ uint64_t ffma2(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ uint64_t fmul2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ uint64_t fadd2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+
 __device__ __forceinline__ uint32_t pack_half2(float lo, float hi) {
   __half2 h = __floats2half2_rn(lo, hi);
   return *reinterpret_cast<uint32_t*>(&h);
+}
+
+// 2^x for a pair of inputs on the FP32 pipe (no MUFU), rounded to an FP16
+// pair.  x = j + f with j = rint(x) (the 1.5*2^23 shifter) and |f| <= 1/2;
+// 2^f comes from a degree-4 polynomial fitted for relative error on
+// [-1/2, 1/2] (max 2.7e-6, far below FP16 rounding); 2^j is added into the
+// exponent field.  Inputs are clamped to >= -125 (2^-125 and smaller all round
+// to FP16 zero), and must stay below 64.
+__device__ __forceinline__ uint64_t exp2_pair_fma(uint64_t xx) {
+  const uint64_t x = f2_pack(fmaxf(f2_lo(xx), -125.f), fmaxf(f2_hi(xx), -125.f));
+  const uint64_t t = fadd2(x, f2_pack(12582912.f, 12582912.f));
+  const uint64_t j = fadd2(t, f2_pack(-12582912.f, -12582912.f));
+  const uint64_t f = ffma2(j, f2_pack(-1.f, -1.f), x);
+  uint64_t q = ffma2(f2_pack(9.570099413394928e-3f, 9.570099413394928e-3f), f,
+                     f2_pack(5.591785907745361e-2f, 5.591785907745361e-2f));
+  q = ffma2(q, f, f2_pack(2.40247443318367e-1f, 2.40247443318367e-1f));
+  q = ffma2(q, f, f2_pack(6.931217908859253e-1f, 6.931217908859253e-1f));
+  q = ffma2(q, f, f2_pack(9.999992847442627e-1f, 9.999992847442627e-1f));
+  const uint32_t r0 = static_cast<uint32_t>(q) + (static_cast<uint32_t>(t) << 23);
+  const uint32_t r1 = static_cast<uint32_t>(q >> 32) + (static_cast<uint32_t>(t >> 32) << 23);
+  return (static_cast<uint64_t>(r1) << 32) | r0;
+}
+__device__ __forceinline__ uint32_t exp2_pair_fma_f16(uint64_t xx) {
+  const uint64_t x = f2_pack(fmaxf(f2_lo(xx), -125.f), fmaxf(f2_hi(xx), -125.f));
+  const uint64_t t = fadd2(x, f2_pack(12582912.f, 12582912.f));
+  const uint64_t j = fadd2(t, f2_pack(-12582912.f, -12582912.f));
+  const uint64_t f = ffma2(j, f2_pack(-1.f, -1.f), x);
+  uint64_t q = ffma2(f2_pack(9.570099413394928e-3f, 9.570099413394928e-3f), f,
+                     f2_pack(5.591785907745361e-2f, 5.591785907745361e-2f));
+  q = ffma2(q, f, f2_pack(2.40247443318367e-1f, 2.40247443318367e-1f));
+  q = ffma2(q, f, f2_pack(6.931217908859253e-1f, 6.931217908859253e-1f));
+  q = ffma2(q, f, f2_pack(9.999992847442627e-1f, 9.999992847442627e-1f));
+  const uint32_t r0 = static_cast<uint32_t>(q) + (static_cast<uint32_t>(t) << 23);
+  const uint32_t r1 = static_cast<uint32_t>(q >> 32) + (static_cast<uint32_t>(t >> 32) << 23);
+  return pack_half2(__uint_as_float(r0), __uint_as_float(r1));
 }
 
 __device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c,
@@ -424,6 +511,29 @@ __device__ __forceinline__ float gelu_erf(float x) {
   q = fmaf(q, z, -3.9865106e-01f);
   q = fmaf(q, z, 4.9998581e-01f);
   return fmaxf(x, 0.0f) - (z * e) * q;
+}
+
+// gelu_erf on a pair of inputs, the polynomial on packed FP32 pairs (same
+// coefficients and rounding steps, half the instructions).
+__device__ __forceinline__ uint64_t gelu_erf_pair(uint64_t xx) {
+  const float x0 = f2_lo(xx), x1 = f2_hi(xx);
+  const uint64_t z = f2_pack(fminf(fabsf(x0), 12.0f), fminf(fabsf(x1), 12.0f));
+  const uint64_t a = fmul2(fmul2(z, z), f2_pack(-0.72134752044448170f, -0.72134752044448170f));
+  const uint64_t e = f2_pack(ex2_approx(f2_lo(a)), ex2_approx(f2_hi(a)));
+#define TT_C2(c) f2_pack(c, c)
+  uint64_t q = ffma2(TT_C2(1.8272603e-07f), z, TT_C2(-6.2833151e-06f));
+  q = ffma2(q, z, TT_C2(9.4161209e-05f));
+  q = ffma2(q, z, TT_C2(-8.1654533e-04f));
+  q = ffma2(q, z, TT_C2(4.6159490e-03f));
+  q = ffma2(q, z, TT_C2(-1.8332606e-02f));
+  q = ffma2(q, z, TT_C2(5.4443646e-02f));
+  q = ffma2(q, z, TT_C2(-1.2799904e-01f));
+  q = ffma2(q, z, TT_C2(2.4824467e-01f));
+  q = ffma2(q, z, TT_C2(-3.9865106e-01f));
+  q = ffma2(q, z, TT_C2(4.9998581e-01f));
+  const uint64_t g = fmul2(fmul2(z, e), q);
+  return ffma2(g, TT_C2(-1.0f), f2_pack(fmaxf(x0, 0.0f), fmaxf(x1, 0.0f)));
+#undef TT_C2
 }
 
 }  // namespace tt
