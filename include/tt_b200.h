@@ -203,6 +203,24 @@ int tt_model_workspace_bytes(const tt_model* model, int batch, int seq, size_t* 
 int tt_model_forward(tt_model* model, const float* x, const uint8_t* mask, float* out, int batch,
                      int seq, void* workspace, size_t workspace_bytes, void* stream);
 
+/* Workspace bytes tt_model_forward_host needs for chunks of `chunk` sequences
+ * of length seq (the model workspace of one chunk plus two device copies of a
+ * chunk's input, output and mask). */
+int tt_model_host_workspace_bytes(const tt_model* model, int chunk, int seq, size_t* bytes);
+
+/* tt_model_forward over page-locked HOST buffers x, out ([B, S, D] FP32) and
+ * mask ([B, S] bytes or NULL), pipelined by chunks of `chunk` sequences: the
+ * copy-in of chunk i+1 and the copy-out of chunk i-1 run on the model's own
+ * copy streams while chunk i computes on `stream`.  The work starts after the
+ * caller's earlier work on `stream`, and `stream` completes only after the
+ * last copy-out, so synchronizing `stream` makes `out` readable.  Rejects
+ * pageable host memory.  Results equal tt_model_forward's (sequences are
+ * independent).  Replaces the reference's host-side
+ * x.to("cuda") -> MixedPrecisionTransformer.forward -> .cpu() round trip
+ * (mixed_precision_benchmark.py:60-101, torch_transformer_benchmark.py:701-720). */
+int tt_model_forward_host(tt_model* model, const float* x, const uint8_t* mask, float* out, int batch,
+                          int seq, int chunk, void* workspace, size_t workspace_bytes, void* stream);
+
 /* Kernel kinds reported by tt_model_profile_collect. */
 #define TT_KERNEL_LN0 0
 #define TT_KERNEL_MASK 1

@@ -150,3 +150,52 @@ def test_sequences_independent_of_batch(tt_lib):
         full = model(x)
         part = model(x[10:14].contiguous())
     assert torch.equal(full[10:14], part)
+
+
+@pytest.mark.parametrize("chunk", [None, 1, 3, 64])
+def test_host_pipeline_equals_device_forward(tt_lib, chunk):
+    """forward_host (pinned host buffers, copies overlapped by chunks) gives the device path's bits,
+    including a ragged last chunk and a chunk larger than the batch."""
+    cfg, _ = oracle.CONFIGS["C1"]
+    sd = oracle.seeded_state_dict(cfg)
+    model = build_model(cfg, sd)
+    x, _ = oracle.generate_case(cfg, 11)
+    x = x[:10].contiguous()
+    with torch.inference_mode():
+        ref = model(x.to(DEV)).cpu()
+        out = torch.empty_like(x).pin_memory()
+        got = model.forward_host(x.pin_memory(), out=out, chunk=chunk)
+        again = model(x)  # pageable host input is staged through a pinned copy
+    assert got.data_ptr() == out.data_ptr()
+    assert torch.equal(got, ref)
+    assert torch.equal(again, ref)
+
+
+def test_host_pipeline_with_mask(tt_lib, strict_fp32):
+    cfg = oracle.Config(6, 300, 256, 8, 512, 2, True)
+    sd = oracle.seeded_state_dict(cfg, 3)
+    model = build_model(cfg, sd)
+    x, mask = oracle.generate_case(cfg, 4, padding_ratio=0.5)
+    with torch.inference_mode():
+        dev_out = model(x.to(DEV), mask.to(DEV)).cpu()
+        host_out = model.forward_host(x.pin_memory(), mask.pin_memory(), chunk=4)
+        ref = oracle_gpu(sd, cfg, x, mask, chunk=None)
+    assert torch.equal(host_out, dev_out)
+    assert torch.all(host_out[~mask] == 0)
+    assert oracle.compare(ref, host_out.to(DEV)).failed == 0
+
+
+def test_host_pipeline_rejects_pageable_memory(tt_lib):
+    cfg, _ = oracle.CONFIGS["C1"]
+    model = build_model(cfg, oracle.seeded_state_dict(cfg))
+    plan = model._plan(DEV)
+    x = torch.zeros(2, cfg.seq_len, cfg.d_model)  # pageable
+    out = torch.zeros_like(x).pin_memory()
+    ws, ws_bytes = plan.host_workspace(2, cfg.seq_len)
+    stream = torch.cuda.current_stream(DEV).cuda_stream
+    rc = tt_lib.tt_model_forward_host(plan.handle, x.data_ptr(), None, out.data_ptr(), 2, cfg.seq_len, 2, ws,
+                                      ws_bytes, stream)
+    assert rc == _lib.TT_ERR_ARG and "page-locked" in _lib.last_error()
+    rc = tt_lib.tt_model_forward_host(plan.handle, out.data_ptr(), None, out.data_ptr(), 2, cfg.seq_len, 2, ws,
+                                      4096, stream)
+    assert rc == _lib.TT_ERR_WORKSPACE

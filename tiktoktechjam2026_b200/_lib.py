@@ -107,6 +107,11 @@ SIGNATURES = {
         c_int,
         [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_void_p, c_size_t, c_void_p],
     ),
+    "tt_model_host_workspace_bytes": (c_int, [c_void_p, c_int, c_int, POINTER(c_size_t)]),
+    "tt_model_forward_host": (
+        c_int,
+        [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_void_p, c_size_t, c_void_p],
+    ),
     "tt_model_set_profiling": (c_int, [c_void_p, c_int]),
     "tt_model_profile_collect": (c_int, [c_void_p, POINTER(c_float), POINTER(c_int), c_int]),
 }

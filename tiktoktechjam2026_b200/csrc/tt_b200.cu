@@ -541,6 +541,10 @@ struct tt_model {
   };
   std::vector<Rec> recs;
   std::vector<cudaEvent_t> pool;
+  // Host-buffer pipeline (tt_model_forward_host): one copy stream per
+  // direction and per-buffer events, created on first use.
+  cudaStream_t h2d = nullptr, d2h = nullptr;
+  cudaEvent_t ev_entry = nullptr, ev_in[2] = {}, ev_comp[2] = {}, ev_out[2] = {};
 };
 
 namespace {
@@ -575,6 +579,50 @@ WsLayout ws_layout(const tt_model* m, int batch, int seq) {
   w.kv_end = take(static_cast<size_t>(batch) * 4);
   w.total = off;
   return w;
+}
+
+// Workspace of the host-buffer pipeline: the model workspace of one chunk,
+// then two device copies (ping-pong) of a chunk's input, output and mask.
+struct HostWsLayout {
+  size_t model, x[2], out[2], mask[2], total;
+};
+
+HostWsLayout host_ws_layout(const tt_model* m, int chunk, int seq) {
+  HostWsLayout h;
+  const size_t rows = static_cast<size_t>(chunk) * seq;
+  size_t off = align_up(ws_layout(m, chunk, seq).total, 1024);
+  h.model = 0;
+  for (int b = 0; b < 2; ++b) {
+    h.x[b] = off;
+    off = align_up(off + rows * m->D * 4, 1024);
+    h.out[b] = off;
+    off = align_up(off + rows * m->D * 4, 1024);
+    h.mask[b] = off;
+    off = align_up(off + rows, 1024);
+  }
+  h.total = off;
+  return h;
+}
+
+int require_pinned(const void* p, const char* what) {
+  cudaPointerAttributes a;
+  if (int rc = check_cuda(cudaPointerGetAttributes(&a, p), "cudaPointerGetAttributes")) return rc;
+  if (a.type != cudaMemoryTypeHost)
+    return fail(TT_ERR_ARG, "%s must be page-locked host memory (cudaHostAlloc, cudaHostRegister or a pinned "
+                "tensor)", what);
+  return TT_OK;
+}
+
+int ensure_copy_streams(tt_model* m) {
+  if (m->h2d) return TT_OK;
+  if (int rc = check_cuda(cudaStreamCreateWithFlags(&m->h2d, cudaStreamNonBlocking), "cudaStreamCreate"))
+    return rc;
+  if (int rc = check_cuda(cudaStreamCreateWithFlags(&m->d2h, cudaStreamNonBlocking), "cudaStreamCreate"))
+    return rc;
+  for (cudaEvent_t* e : {&m->ev_entry, &m->ev_in[0], &m->ev_in[1], &m->ev_comp[0], &m->ev_comp[1],
+                         &m->ev_out[0], &m->ev_out[1]})
+    if (int rc = check_cuda(cudaEventCreateWithFlags(e, cudaEventDisableTiming), "cudaEventCreate")) return rc;
+  return TT_OK;
 }
 
 int record_begin(tt_model* m, cudaStream_t s, cudaEvent_t* ev) {
@@ -1001,6 +1049,11 @@ void tt_model_destroy(tt_model* m) {
     cudaEventDestroy(r.b);
   }
   for (auto e : m->pool) cudaEventDestroy(e);
+  if (m->h2d) cudaStreamDestroy(m->h2d);
+  if (m->d2h) cudaStreamDestroy(m->d2h);
+  for (cudaEvent_t e : {m->ev_entry, m->ev_in[0], m->ev_in[1], m->ev_comp[0], m->ev_comp[1], m->ev_out[0],
+                        m->ev_out[1]})
+    if (e) cudaEventDestroy(e);
   delete m;
 }
 
@@ -1203,6 +1256,73 @@ int tt_model_forward(tt_model* m, const float* x, const uint8_t* mask, float* ou
     }
   }
   return TT_OK;
+}
+
+int tt_model_host_workspace_bytes(const tt_model* m, int chunk, int seq, size_t* bytes) {
+  if (!m || !bytes) return fail(TT_ERR_ARG, "null argument");
+  if (chunk <= 0 || seq <= 0) return fail(TT_ERR_SHAPE, "invalid chunk/seq");
+  *bytes = host_ws_layout(m, chunk, seq).total;
+  return TT_OK;
+}
+
+int tt_model_forward_host(tt_model* m, const float* x, const uint8_t* mask, float* out, int batch, int seq,
+                          int chunk, void* workspace, size_t workspace_bytes, void* stream) {
+  if (!m || !x || !out || !workspace) return fail(TT_ERR_ARG, "null argument");
+  if (batch <= 0 || seq <= 0 || chunk <= 0) return fail(TT_ERR_SHAPE, "invalid batch/seq/chunk");
+  if (chunk > batch) chunk = batch;
+  const HostWsLayout h = host_ws_layout(m, chunk, seq);
+  if (workspace_bytes < h.total)
+    return fail(TT_ERR_WORKSPACE, "workspace %zu < required %zu bytes", workspace_bytes, h.total);
+  if (reinterpret_cast<uintptr_t>(workspace) % 1024 != 0)
+    return fail(TT_ERR_ALIGN, "workspace must be 1024-byte aligned");
+  if (int rc = require_pinned(x, "x")) return rc;
+  if (int rc = require_pinned(out, "out")) return rc;
+  if (mask)
+    if (int rc = require_pinned(mask, "mask")) return rc;
+  if (int rc = ensure_copy_streams(m)) return rc;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  uint8_t* base = static_cast<uint8_t*>(workspace);
+  const size_t row_bytes = static_cast<size_t>(m->D) * 4;
+  const size_t model_bytes = ws_layout(m, chunk, seq).total;
+  // Copies start after the caller's earlier work on the stream (it may still use the workspace).
+  if (int rc = check_cuda(cudaEventRecord(m->ev_entry, s), "cudaEventRecord")) return rc;
+  cudaStreamWaitEvent(m->h2d, m->ev_entry, 0);
+  cudaStreamWaitEvent(m->d2h, m->ev_entry, 0);
+  const int n = (batch + chunk - 1) / chunk;
+  for (int i = 0; i < n; ++i) {
+    const int b = i & 1;
+    const int c0 = i * chunk;
+    const int nb = batch - c0 < chunk ? batch - c0 : chunk;
+    const size_t rows0 = static_cast<size_t>(c0) * seq, rows = static_cast<size_t>(nb) * seq;
+    float* xd = reinterpret_cast<float*>(base + h.x[b]);
+    float* od = reinterpret_cast<float*>(base + h.out[b]);
+    uint8_t* md = base + h.mask[b];
+    // Input buffer b was last read by the forward of chunk i - 2.
+    if (i >= 2) cudaStreamWaitEvent(m->h2d, m->ev_comp[b], 0);
+    if (int rc = check_cuda(cudaMemcpyAsync(xd, x + rows0 * m->D, rows * row_bytes, cudaMemcpyHostToDevice,
+                                            m->h2d),
+                            "cudaMemcpyAsync(x)"))
+      return rc;
+    if (mask)
+      if (int rc = check_cuda(cudaMemcpyAsync(md, mask + rows0, rows, cudaMemcpyHostToDevice, m->h2d),
+                              "cudaMemcpyAsync(mask)"))
+        return rc;
+    if (int rc = check_cuda(cudaEventRecord(m->ev_in[b], m->h2d), "cudaEventRecord")) return rc;
+    cudaStreamWaitEvent(s, m->ev_in[b], 0);
+    // Output buffer b was last read by the copy-out of chunk i - 2.
+    if (i >= 2) cudaStreamWaitEvent(s, m->ev_out[b], 0);
+    if (int rc = tt_model_forward(m, xd, mask ? md : nullptr, od, nb, seq, base + h.model, model_bytes, stream))
+      return rc;
+    if (int rc = check_cuda(cudaEventRecord(m->ev_comp[b], s), "cudaEventRecord")) return rc;
+    cudaStreamWaitEvent(m->d2h, m->ev_comp[b], 0);
+    if (int rc = check_cuda(cudaMemcpyAsync(out + rows0 * m->D, od, rows * row_bytes, cudaMemcpyDeviceToHost,
+                                            m->d2h),
+                            "cudaMemcpyAsync(out)"))
+      return rc;
+    if (int rc = check_cuda(cudaEventRecord(m->ev_out[b], m->d2h), "cudaEventRecord")) return rc;
+  }
+  // The caller's stream completes only after the last copy-out.
+  return check_cuda(cudaStreamWaitEvent(s, m->ev_out[(n - 1) & 1], 0), "cudaStreamWaitEvent");
 }
 
 int tt_model_set_profiling(tt_model* m, int enable) {

@@ -149,7 +149,14 @@ class _DevicePlan:
     def workspace(self, batch: int, seq: int):
         nbytes = ctypes.c_size_t()
         _lib.check(_lib.lib().tt_model_workspace_bytes(self.handle, batch, seq, ctypes.byref(nbytes)))
-        need = int(nbytes.value)
+        return self._reserve(int(nbytes.value))
+
+    def host_workspace(self, chunk: int, seq: int):
+        nbytes = ctypes.c_size_t()
+        _lib.check(_lib.lib().tt_model_host_workspace_bytes(self.handle, chunk, seq, ctypes.byref(nbytes)))
+        return self._reserve(int(nbytes.value))
+
+    def _reserve(self, need: int):
         if self._ws is None or self._ws_bytes < need:
             self._ws = None
             raw = torch.empty(need + 1024, dtype=torch.uint8, device=self.device)
@@ -282,7 +289,8 @@ class B200Transformer(nn.Module):
         if x.dtype != torch.float32:
             raise ValueError("mixed candidate requires an FP32 input/residual stream")
         if not x.is_cuda:
-            raise RuntimeError("B200Transformer runs only on CUDA (sm_100a) devices; there is no CPU path")
+            # Host tensors are computed on the model's GPU through the pipelined host path.
+            return self.forward_host(x, valid_token_mask)
         if x.dim() != 3 or x.shape[-1] != self.config.d_model:
             raise ValueError(f"expected x of shape [B, S, {self.config.d_model}], got {tuple(x.shape)}")
         B, S, _ = x.shape
@@ -307,6 +315,76 @@ class B200Transformer(nn.Module):
                 )
             )
         return out
+
+
+    def forward_host(
+        self,
+        x: torch.Tensor,
+        valid_token_mask: Optional[torch.Tensor] = None,
+        *,
+        out: Optional[torch.Tensor] = None,
+        chunk: Optional[int] = None,
+    ) -> torch.Tensor:
+        """``forward`` for host tensors, on the GPU holding the model's parameters.
+
+        One ``tt_model_forward_host`` call: the batch is cut into chunks of
+        ``chunk`` sequences, and the copy-in of the next chunk and the copy-out
+        of the previous one overlap the current chunk's kernels.  ``x`` (and
+        ``out``, when given) should be pinned; pageable tensors are staged
+        through a pinned copy.  Returns ``out`` (a new pinned FP32 tensor when
+        none is given) once the result is in host memory.
+        """
+        if x.dtype != torch.float32:
+            raise ValueError("mixed candidate requires an FP32 input/residual stream")
+        if x.is_cuda:
+            raise ValueError("forward_host takes host tensors; use forward for CUDA tensors")
+        dev = next(self.parameters()).device
+        if dev.type != "cuda":
+            raise RuntimeError("B200Transformer runs only on CUDA (sm_100a) devices; there is no CPU path")
+        if x.dim() != 3 or x.shape[-1] != self.config.d_model:
+            raise ValueError(f"expected x of shape [B, S, {self.config.d_model}], got {tuple(x.shape)}")
+        B, S, _ = x.shape
+        x = x.contiguous()
+        if not x.is_pinned():
+            x = x.pin_memory()
+        if out is None:
+            out = torch.empty(x.shape, dtype=torch.float32, pin_memory=True)
+        elif out.shape != x.shape or out.dtype != torch.float32 or out.is_cuda or not out.is_contiguous() \
+                or not out.is_pinned():
+            raise ValueError("out must be a contiguous pinned FP32 host tensor shaped like x")
+        if B == 0 or S == 0:
+            return out
+        mask = None if self.assume_all_tokens_valid else valid_token_mask
+        mask_ptr = 0
+        if mask is not None:
+            if mask.shape != (B, S):
+                raise ValueError(f"valid_token_mask must have shape {(B, S)}, got {tuple(mask.shape)}")
+            mask8 = mask.to(device="cpu", dtype=torch.bool).contiguous().view(torch.uint8)
+            if not mask8.is_pinned():
+                mask8 = mask8.pin_memory()
+            mask_ptr = mask8.data_ptr()
+        if chunk is None:
+            chunk = default_host_chunk(B, S, self.config.d_model)
+        chunk = max(1, min(int(chunk), B))
+        plan = self._plan(dev)
+        ws_ptr, ws_bytes = plan.host_workspace(chunk, S)
+        with torch.cuda.device(dev):
+            stream = torch.cuda.current_stream(dev)
+            _lib.check(
+                _lib.lib().tt_model_forward_host(
+                    plan.handle, x.data_ptr(), mask_ptr, out.data_ptr(), B, S, chunk, ws_ptr, ws_bytes,
+                    stream.cuda_stream,
+                )
+            )
+            stream.synchronize()
+        return out
+
+
+def default_host_chunk(batch: int, seq: int, d_model: int) -> int:
+    """Sequences per chunk of the host pipeline: up to 8 chunks of at least 8 MiB of input each."""
+    total = batch * seq * d_model * 4
+    n_chunks = max(1, min(8, total // (8 << 20), batch))
+    return (batch + n_chunks - 1) // n_chunks
 
 
 # The reference's class name, for drop-in imports.
