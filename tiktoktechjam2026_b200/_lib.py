@@ -11,7 +11,8 @@ import os
 import threading
 from ctypes import POINTER, c_char_p, c_float, c_int, c_int64, c_size_t, c_uint, c_ulonglong, c_void_p
 
-LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "libtt_b200.so")
+# TT_B200_LIB selects another build of the same library (e.g. one compiled with different tile constants).
+LIB_PATH = os.environ.get("TT_B200_LIB") or os.path.join(os.path.dirname(os.path.abspath(__file__)), "libtt_b200.so")
 
 TT_OK = 0
 TT_ERR_SHAPE = 1

@@ -21,11 +21,14 @@
 //   maximum m only moves when the tile maximum exceeds it by more than 2^8
 //   (O and l are then rescaled, rare after the first tiles), so P stays <= 256
 //   in FP16; exp2 of S*scale*log2(e) - m (MUFU, with a share of the
-//   exponentials on the FP32 pipe); l accumulates the FP32 probabilities; P is
-//   rounded to FP16 into the 128B-swizzled K-major tile P_b
-//   O += P_b V_t            TMEM, accumulated over the item's key tiles (two
+//   exponentials on the FP32 pipe); P is rounded to FP16 into the
+//   128B-swizzled K-major tile P_b
+//   [O | l] += P_b [V_t | 1]  TMEM, accumulated over the item's key tiles (two
 //                           buffers by item, so an item's epilogue runs after
-//                           the next item's first tile)
+//                           the next item's first tile).  Each V^T stage is
+//                           followed by 16 rows of FP16 ones, so the same MMA
+//                           (N = HD + 16) also sums the FP16 probabilities
+//                           of every row: the softmax warps never add them.
 // Items (sequence*head, query tile) are dealt heavy-first: stream s of CTA c
 // takes items 2c+s, 2c+s+2G, ... (G = gridDim.x).
 #pragma once
@@ -40,12 +43,15 @@ struct AttnDbLayout {
   static constexpr int Q_BYTES = BM * HD * 2;
   static constexpr int K_BYTES = BN * HD * 2;
   static constexpr int V_BYTES = HD * 128;  // V^T block: HD rows of 64 keys (128 bytes)
+  static constexpr int ONES_BYTES = 16 * 128;           // 16 rows of 64 FP16 ones after each V^T block
+  static constexpr int V_STAGE = V_BYTES + ONES_BYTES;  // B operand of P.[V | 1], N = ON rows
+  static constexpr int ON = HD + 16;                    // accumulator columns: O, then 16 copies of l
   static constexpr int P_BYTES = BM * BN * 2;
-  // Per-stream region: Q[2] | K[NST] | V[NST] | P[2]
+  // Per-stream region: Q[2] | K[NST] | V[NST] (each with its ones block) | P[2]
   static constexpr int S_Q = 0;
   static constexpr int S_K = S_Q + 2 * Q_BYTES;
   static constexpr int S_V = S_K + NST * K_BYTES;
-  static constexpr int S_P = S_V + NST * V_BYTES;
+  static constexpr int S_P = S_V + NST * V_STAGE;
   static constexpr int STREAM_BYTES = S_P + 2 * P_BYTES;
   // Per-stream barriers: q_full[2] q_empty[2] kv_full[NST] kv_empty[NST]
   // s_full[2] s_free[2] p_full[2] p_empty[2] o_full[2] o_free[2]
@@ -57,24 +63,41 @@ struct AttnDbLayout {
   static constexpr int OFF_DONE = OFF_BAR + 2 * NBAR_STREAM * 8;  // done[2]
   static constexpr int OFF_MISC = OFF_DONE + 16;
   static constexpr int SMEM_ALLOC = OFF_MISC + 16 + 1024;
-  // TMEM per stream: S_0 at 0, S_1 at 64, O of item buffer ob at 128 + ob * HD.
+  // TMEM per stream: S_0 at 0, S_1 at 64, [O | l] of item buffer ob at 128 + ob * ON.
   static constexpr int TMEM_COLS = 512, TMEM_STREAM = 256, TMEM_O = 128;
   static constexpr int THREADS = 384;  // 8 softmax warps, 2 producers, 2 MMA issuers
   // Register split (setmaxnreg): the launch provides 384 x 168.
-  static constexpr int REGS_LAUNCH = 168, REGS_SOFTMAX = 216, REGS_OTHER = 56;
+#ifndef TT_DB_REGS_SOFTMAX
+#define TT_DB_REGS_SOFTMAX 216
+#define TT_DB_REGS_OTHER 56
+#endif
+  static constexpr int REGS_LAUNCH = 168, REGS_SOFTMAX = TT_DB_REGS_SOFTMAX, REGS_OTHER = TT_DB_REGS_OTHER;
   static_assert(256 * REGS_SOFTMAX + 128 * REGS_OTHER <= THREADS * REGS_LAUNCH, "register split");
-  static_assert(TMEM_O + 2 * HD <= TMEM_STREAM, "TMEM budget");
+  static_assert(TMEM_O + 2 * ON <= TMEM_STREAM, "TMEM budget");
   static_assert(HD == 16 || HD == 32, "this kernel covers head_dim 16 and 32");
-  static_assert(STREAM_BYTES % 1024 == 0 && S_V % 1024 == 0 && S_P % 1024 == 0 && V_BYTES % 1024 == 0,
+  static_assert(STREAM_BYTES % 1024 == 0 && S_V % 1024 == 0 && S_P % 1024 == 0 && V_STAGE % 1024 == 0,
                 "alignment");
   static_assert(SMEM_ALLOC <= 232448, "shared memory budget");
 };
 
 // Pairs of exponentials per 8 computed by polynomial on the FP32 pipe instead
 // of MUFU.
-constexpr int kDbExpFmaOf8 = 2;
+#ifndef TT_DB_EXP_FMA_OF8
+#define TT_DB_EXP_FMA_OF8 2
+#endif
+constexpr int kDbExpFmaOf8 = TT_DB_EXP_FMA_OF8;
 
-template <int HD>
+// The reference maximum moves when a tile's maximum exceeds it by more than
+// this (log2 units): FP32 exponentials tolerate 2^8; with packed-FP16
+// exponentials a smaller bound keeps the FP16 input x = s - m, whose rounding
+// error grows with |x|, accurate for the largest probabilities.
+#ifndef TT_DB_LAZY_F16
+#define TT_DB_LAZY_F16 2.0f
+#endif
+
+// EXP16: probabilities from ex2.approx.f16x2 on FP16-rounded x (two per MUFU
+// operation, already packed for the P tile); otherwise FP32 exponentials.
+template <int HD, bool EXP16>
 __global__ void __launch_bounds__(384, 1)
     attn_db_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                        const __grid_constant__ CUtensorMap tmV, const AttnParams p, int n_items) {
@@ -115,6 +138,16 @@ __global__ void __launch_bounds__(384, 1)
     *abort_flag = 0;
     fence_mbar_init();
   }
+  // The ones rows after every V^T stage (never written by TMA), made visible
+  // to the tensor core's (async proxy) reads before the first MMA.
+  for (int i = threadIdx.x; i < 2 * NST * (L::ONES_BYTES / 16); i += blockDim.x) {
+    const int s = i / (NST * (L::ONES_BYTES / 16));
+    const int rem = i % (NST * (L::ONES_BYTES / 16));
+    const int st = rem / (L::ONES_BYTES / 16), ch = rem % (L::ONES_BYTES / 16);
+    st_shared_v4(smem_u32(smem + s * L::STREAM_BYTES + L::S_V + st * L::V_STAGE + L::V_BYTES + ch * 16),
+                 0x3c003c00u, 0x3c003c00u, 0x3c003c00u, 0x3c003c00u);
+  }
+  fence_proxy_async_smem();
   if (warp == 10) {
     tmem_alloc(tmem_slot, L::TMEM_COLS);
     tmem_relinquish();
@@ -162,7 +195,7 @@ __global__ void __launch_bounds__(384, 1)
           if (!(ok = wait_phase(&b[L::B_KE + st], ((t / NST) & 1) ^ 1, wd, 0x132))) break;
           mbar_arrive_expect_tx(&b[L::B_KF + st], L::K_BYTES + L::V_BYTES);
           tma_load_3d(sb + L::S_K + st * L::K_BYTES, &tmK, &b[L::B_KF + st], 0, j * BN, item.bh);
-          tma_load_3d(sb + L::S_V + st * L::V_BYTES, &tmV, &b[L::B_KF + st], j * BN, 0, item.bh);
+          tma_load_3d(sb + L::S_V + st * L::V_STAGE, &tmV, &b[L::B_KF + st], j * BN, 0, item.bh);
           ++t;
         }
       }
@@ -183,7 +216,7 @@ __global__ void __launch_bounds__(384, 1)
       constexpr uint32_t kSwQK = swizzle_kind_for_bytes(HD * 2);
       constexpr uint32_t kSboQK = 8 * HD * 2;
       const uint32_t idesc_s = umma_idesc_f16_f32(BM, BN);
-      const uint32_t idesc_o = umma_idesc_f16_f32(BM, HD);
+      const uint32_t idesc_o = umma_idesc_f16_f32(BM, L::ON);
       // S cursor: item w_s, tile j_s of n_s, stream tile u, item count it_s.
       int w_s = first_item(2 * static_cast<int>(blockIdx.x) + s), j_s = 0, n_s = 0, u = 0, it_s = 0;
       if (w_s < n_items) n_s = n_tiles(attn_item(p, w_s, n_qt));
@@ -224,11 +257,11 @@ __global__ void __launch_bounds__(384, 1)
         if (!(ok = wait_phase(&b[L::B_PF + bb], (t >> 1) & 1, wd, 0x234))) break;
         if (j_o == 0 && !(ok = wait_phase(&b[L::B_OR + ob], ((it_o >> 1) & 1) ^ 1, wd, 0x235))) break;
         tc_fence_after();
-        const uint32_t tO = tS + L::TMEM_O + ob * HD;
+        const uint32_t tO = tS + L::TMEM_O + ob * L::ON;
 #pragma unroll
         for (int kk = 0; kk < BN / 16; ++kk) {
           const uint64_t da = umma_sdesc(sb + L::S_P + bb * L::P_BYTES + kk * 32, 1024, kSw128);
-          const uint64_t db = umma_sdesc(sb + L::S_V + st * L::V_BYTES + kk * 32, 1024, kSw128);
+          const uint64_t db = umma_sdesc(sb + L::S_V + st * L::V_STAGE + kk * 32, 1024, kSw128);
           umma_f16(tO, da, db, idesc_o, (kk > 0 || j_o > 0) ? 1u : 0u);
         }
         umma_commit(&b[L::B_KE + st]);
@@ -264,22 +297,27 @@ __global__ void __launch_bounds__(384, 1)
     int pend_it = 0;
     __half* pend_dst = nullptr;
     bool pend_store = false;
-    float pend_inv = 0.f;
+    bool pend_valid = false;
     auto finish_item = [&]() -> bool {
       const int ob = pend_it & 1;
       if (!warp_wait_phase(&b[L::B_OF + ob], (pend_it >> 1) & 1, wd, 0x333)) return false;
       tc_fence_after();
       uint32_t o[HD];
+      uint32_t lv[8];  // row sum of the FP16 probabilities (column HD of the accumulator)
       if constexpr (HD == 32) {
-        tmem_ld_x32(tS + L::TMEM_O + ob * HD, o);
+        tmem_ld_x32(tS + L::TMEM_O + ob * L::ON, o);
       } else {
-        tmem_ld_x16(tS + L::TMEM_O + ob * HD, o);
+        tmem_ld_x16(tS + L::TMEM_O + ob * L::ON, o);
       }
+      tmem_ld_x8(tS + L::TMEM_O + ob * L::ON + HD, lv);
       tmem_ld_wait_tied(o);
+      tmem_ld_wait_tied(lv);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&b[L::B_OR + ob]);
       pend = false;
+      const float lsum = __uint_as_float(lv[0]);
+      const float pend_inv = (pend_valid && lsum > 0.f) ? 1.f / lsum : 0.f;
       if (pend_store) {
 #pragma unroll
         for (int i = 0; i < HD / 8; ++i) {
@@ -308,9 +346,8 @@ __global__ void __launch_bounds__(384, 1)
       }
       const int row_lim = p.causal ? min(qi + 1, item.kv_end) : item.kv_end;
       const int ob = it & 1;
-      const uint32_t tO = tS + L::TMEM_O + ob * HD;
+      const uint32_t tO = tS + L::TMEM_O + ob * L::ON;
       float m_run = -INFINITY;  // reference maximum of this row (log2 units)
-      uint64_t l2 = 0;          // row sum, as two partial sums
 
       for (int j = 0; j < nt; ++j, ++t) {
         const int bb = t & 1;
@@ -368,7 +405,8 @@ __global__ void __launch_bounds__(384, 1)
         // maximum without a rescale.
         float m_new = m_run;
         bool resc = false;
-        if (m_tile > m_run + 8.0f) {
+        constexpr float kLazy = EXP16 ? TT_DB_LAZY_F16 : 8.0f;
+        if (m_tile > m_run + kLazy) {
           resc = (m_run != -INFINITY);
           m_new = m_tile;
         }
@@ -380,9 +418,8 @@ __global__ void __launch_bounds__(384, 1)
           if (!(ok = warp_wait_phase(&b[L::B_PE + (tp & 1)], (tp >> 1) & 1, wd, 0x332))) break;
           tc_fence_after();
           const float corr = resc ? ex2_approx(m_run - m_new) : 1.f;
-          l2 = fmul2(l2, f2_pack(corr, corr));
 #pragma unroll 1
-          for (int c = 0; c < HD; c += 16) {  // 16 columns at a time: the scores stay in registers
+          for (int c = 0; c < L::ON; c += 16) {  // O and l, 16 columns at a time: the scores stay in registers
             uint32_t o[16];
             tmem_ld_x16_sync(tO + c, o);
 #pragma unroll
@@ -395,7 +432,7 @@ __global__ void __launch_bounds__(384, 1)
 
         // P buffer bb was last read by P.V of tile t-2.
         if (!(ok = warp_wait_phase(&b[L::B_PE + bb], ((t >> 1) & 1) ^ 1, wd, 0x334))) break;
-        // Probabilities: FP32 row sum, FP16 into P_bb.
+        // Probabilities: FP16 into P_bb (their row sum comes from the P.[V | 1] MMA).
         const uint64_t negm = f2_pack(-m_use, -m_use);
         const uint32_t prow = p_row + bb * L::P_BYTES;
 #pragma unroll
@@ -405,13 +442,18 @@ __global__ void __launch_bounds__(384, 1)
           for (int e = 0; e < 16; ++e) {
             const uint64_t xx =
                 ffma2(f2_pack(__uint_as_float(sc[g][2 * e]), __uint_as_float(sc[g][2 * e + 1])), sl2x2, negm);
-            uint64_t pp;
-            if ((e & 7) < kDbExpFmaOf8)
-              pp = exp2_pair_fma(xx);
-            else
-              pp = f2_pack(ex2_approx(f2_lo(xx)), ex2_approx(f2_hi(xx)));
-            l2 = fadd2(l2, pp);
-            pk[e] = pack_half2(f2_lo(pp), f2_hi(pp));
+            if constexpr (EXP16) {
+              uint32_t h2;
+              asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(h2) : "f"(f2_hi(xx)), "f"(f2_lo(xx)));
+              asm("ex2.approx.f16x2 %0, %1;" : "=r"(pk[e]) : "r"(h2));
+            } else {
+              uint64_t pp;
+              if ((e & 7) < kDbExpFmaOf8)
+                pp = exp2_pair_fma(xx);
+              else
+                pp = f2_pack(ex2_approx(f2_lo(xx)), ex2_approx(f2_hi(xx)));
+              pk[e] = pack_half2(f2_lo(pp), f2_hi(pp));
+            }
           }
 #pragma unroll
           for (int qq = 0; qq < 4; ++qq) {
@@ -432,12 +474,8 @@ __global__ void __launch_bounds__(384, 1)
       pend_it = it;
       pend_dst = dst_row;
       pend_store = qi < p.seq;
-      {
-        const bool row_valid =
-            p.key_mask == nullptr || (pend_store && p.key_mask[static_cast<size_t>(item.b) * p.seq + qi] != 0);
-        const float lsum = f2_lo(l2) + f2_hi(l2);
-        pend_inv = (row_valid && lsum > 0.f) ? 1.f / lsum : 0.f;
-      }
+      pend_valid =
+          p.key_mask == nullptr || (pend_store && p.key_mask[static_cast<size_t>(item.b) * p.seq + qi] != 0);
       ++it;
     }
     if (ok && pend) ok = finish_item();

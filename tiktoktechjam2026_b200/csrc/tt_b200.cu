@@ -269,6 +269,9 @@ int choose_route(int d_model, int heads, int seq, int ffn, Route* out) {
   for (const RouteEntry& e : kRouteTable) {
     if (e.d_model == d_model && e.heads == heads && e.seq == seq && e.ffn == ffn) {
       *out = e.route;
+#ifdef TT_FORCE_ATTN_EXP16
+      out->attn_exp16 = TT_FORCE_ATTN_EXP16;  // build-time override of the table's exponential choice
+#endif
       return TT_OK;
     }
   }
@@ -431,7 +434,8 @@ int launch_attention(const CUtensorMap& tq, const CUtensorMap& tk, const CUtenso
   const unsigned grid = static_cast<unsigned>(n_items < sm_count ? n_items : sm_count);
   if (hd == 16 || hd == 32) {
     // Two streams per CTA, 64-key tiles, double-buffered scores and probabilities.
-    auto kern = hd == 16 ? attn_db_fwd_kernel<16> : attn_db_fwd_kernel<32>;
+    auto kern = hd == 16 ? (exp16 ? attn_db_fwd_kernel<16, true> : attn_db_fwd_kernel<16, false>)
+                         : (exp16 ? attn_db_fwd_kernel<32, true> : attn_db_fwd_kernel<32, false>);
     const int smem = hd == 16 ? AttnDbLayout<16>::SMEM_ALLOC : AttnDbLayout<32>::SMEM_ALLOC;
     if (int rc = prepare_kernel(kern, smem)) return rc;
     // The kernel splits its registers with setmaxnreg; that split is only sound
@@ -445,7 +449,6 @@ int launch_attention(const CUtensorMap& tq, const CUtensorMap& tk, const CUtenso
     const unsigned grid2 = static_cast<unsigned>(ctas < sm_count ? ctas : sm_count);
     kern<<<grid2, AttnDbLayout<32>::THREADS, smem, stream>>>(tq, tk, tv, ap, n_items);
     (void)grid;
-    (void)exp16;
   } else if (hd == 64) {
     auto kern = exp16 ? attn_fwd_kernel<64, true> : attn_fwd_kernel<64, false>;
     if (int rc = prepare_kernel(kern, AttnLayout<64>::SMEM_ALLOC)) return rc;

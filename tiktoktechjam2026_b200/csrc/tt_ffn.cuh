@@ -79,8 +79,12 @@ struct FfnLayout {
 // Warp roles: 0..7 GELU (warp w: TMEM lane quadrant w & 3, hidden columns
 // 64 * (w >> 2) .. +63 of each chunk), 8..11 residual + LayerNorm, 12 TMA
 // producer, 13 TMEM allocator and MMA issuer.
-constexpr int kFfnThreads = 448;
-constexpr int kFfnWarpProd = 12, kFfnWarpMma = 13;
+// Warp 14 is a second TMA producer: ring slot st is always filled by producer
+// st % 2, so each slot keeps a single producer and the parity-based
+// empty-slot wait stays exact (one producer thread completes only about one
+// TMA copy per ~800 cycles).
+constexpr int kFfnThreads = 480;
+constexpr int kFfnWarpProd = 12, kFfnWarpMma = 13, kFfnWarpProd2 = 14;
 
 template <int D>
 __global__ void __launch_bounds__(kFfnThreads, 1)
@@ -148,8 +152,9 @@ __global__ void __launch_bounds__(kFfnThreads, 1)
   const uint32_t tmem_base = *tmem_slot;
   const Watchdog wd{p.err, abort_flag, p.timeout_ns};
 
-  if (warp == kFfnWarpProd) {
-    // ------------------------------------------------------------ producer
+  if (warp == kFfnWarpProd || warp == kFfnWarpProd2) {
+    // ------------------------------------------------------------ producers
+    const int pidx = warp == kFfnWarpProd ? 0 : 1;
     if (lane == 0) {
       tma_prefetch_desc(&maps.a);
       tma_prefetch_desc(&maps.w1);
@@ -157,6 +162,10 @@ __global__ void __launch_bounds__(kFfnThreads, 1)
       int g = 0, i = 0;
       bool ok = true;
       auto load_w = [&](const CUtensorMap* tm, int kx, int ky, int bytes) -> bool {
+        if ((g % NST) % 2 != pidx) {
+          ++g;
+          return true;
+        }
         const int st = g % NST;
         if (!wait_phase(&w_empty[st], ((g / NST) & 1) ^ 1, wd, 0x501)) return false;
         mbar_arrive_expect_tx(&w_full[st], bytes);
@@ -166,10 +175,12 @@ __global__ void __launch_bounds__(kFfnThreads, 1)
       };
       for (int w = blockIdx.x; ok && w < p.n_items; w += gridDim.x, ++i) {
         const int m0 = w * 128;
-        if (!(ok = wait_phase(a_empty, (i & 1) ^ 1, wd, 0x502))) break;
-        mbar_arrive_expect_tx(a_full, L::A_BYTES);
-        for (int kb = 0; kb < NKA; ++kb)
-          tma_load_2d(smem + L::OFF_A + kb * L::A_BOX, &maps.a, a_full, kb * KSW, m0);
+        if (pidx == 0) {
+          if (!(ok = wait_phase(a_empty, (i & 1) ^ 1, wd, 0x502))) break;
+          mbar_arrive_expect_tx(a_full, L::A_BYTES);
+          for (int kb = 0; kb < NKA; ++kb)
+            tma_load_2d(smem + L::OFF_A + kb * L::A_BOX, &maps.a, a_full, kb * KSW, m0);
+        }
         // Same order as the MMA issuer: G1(0), G1(1), G2(0), G1(2), G2(1), ...
         for (int step = 0; ok && step <= nchunk; ++step) {
           if (step < nchunk)
@@ -179,9 +190,9 @@ __global__ void __launch_bounds__(kFfnThreads, 1)
               ok = load_w(&maps.w2, (step - 1) * FC + kb * KSW, 0, L::W2_BLK);
         }
       }
-      if (i > 0) wait_drain(a_full, (i - 1) & 1, kDrainLimitNs);
+      if (pidx == 0 && i > 0) wait_drain(a_full, (i - 1) & 1, kDrainLimitNs);
       for (int q = (g > NST ? g - NST : 0); q < g; ++q)
-        wait_drain(&w_full[q % NST], (q / NST) & 1, kDrainLimitNs);
+        if ((q % NST) % 2 == pidx) wait_drain(&w_full[q % NST], (q / NST) & 1, kDrainLimitNs);
     }
   } else if (warp == kFfnWarpMma) {
     // ------------------------------------------------------------ MMA issuer

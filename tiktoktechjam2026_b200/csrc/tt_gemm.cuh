@@ -85,7 +85,16 @@ __host__ __device__ inline int gemm_tmem_cols(int bn) { return gemm_n_acc(bn) * 
 // one per TMEM lane quadrant); the others pair two warps on each quadrant and
 // split its columns, so every SM sub-partition has two epilogue warps.
 __host__ __device__ constexpr int gemm_epi_warps(int epi) { return epi == EPI_RESID_LN ? 4 : 8; }
-__host__ __device__ constexpr int gemm_threads(int epi) { return 32 * (gemm_epi_warps(epi) + 2); }
+// Warps: epilogue warps, then the first TMA producer, the MMA issuer and
+// kGemmProducers - 1 more producers.  Ring slot st is always filled by
+// producer st % kGemmProducers: one producer per slot keeps the parity-based
+// empty-slot wait exact (a producer can never be two phases ahead on a slot
+// that another producer fills).
+#ifndef TT_GEMM_PRODUCERS
+#define TT_GEMM_PRODUCERS 2
+#endif
+constexpr int kGemmProducers = TT_GEMM_PRODUCERS;
+__host__ __device__ constexpr int gemm_threads(int epi) { return 32 * (gemm_epi_warps(epi) + 1 + kGemmProducers); }
 __host__ __device__ inline int gemm_epi_bytes(int epi) {
   return gemm_epi_warps(epi) * ((epi == EPI_RESID_LN ? kResRing : 0) + kOutRing) * kEpiTile;
 }
@@ -189,7 +198,7 @@ __global__ void __launch_bounds__(gemm_threads(EPI), 1)
     gemm_kernel(const __grid_constant__ GemmMaps maps, const GemmParams p) {
   constexpr int NEPI = gemm_epi_warps(EPI);  // epilogue warps 0..NEPI-1
   constexpr int NSTEP = NEPI / 4;            // warps sharing one TMEM lane quadrant
-  constexpr int W_PROD = NEPI, W_MMA = NEPI + 1;
+  constexpr int W_PROD = NEPI, W_MMA = NEPI + 1;  // further producers: warps NEPI + 2 ...
   constexpr int A_BYTES = 128 * KSW * 2;
   constexpr uint32_t kSw = swizzle_kind_for_bytes(KSW * 2);
   constexpr uint32_t kSbo = 8 * KSW * 2;
@@ -250,8 +259,11 @@ __global__ void __launch_bounds__(gemm_threads(EPI), 1)
   const uint32_t tmem_base = *tmem_slot;
   const Watchdog wd{p.err, abort_flag, p.timeout_ns};
 
-  if (warp == W_PROD) {
-    // ------------------------------------------------------------ producer
+  if (warp == W_PROD || warp > W_MMA) {
+    // ------------------------------------------------------------ producers
+    // A producer thread completes only about one TMA copy per ~800 cycles
+    // whatever the copy size, so the ring's slots are shared out among several.
+    const int pidx = warp == W_PROD ? 0 : warp - W_MMA;
     if (lane == 0) {
       tma_prefetch_desc(&maps.a);
       tma_prefetch_desc(&maps.w);
@@ -261,6 +273,7 @@ __global__ void __launch_bounds__(gemm_threads(EPI), 1)
         const int m0 = (w / p.n_splits) * 128;
         const int n0 = (w % p.n_splits) * bn;
         for (int kb = 0; kb < nk; ++kb, ++g) {
+          if ((g % nst) % kGemmProducers != pidx) continue;
           const int st = g % nst;
           if (!(ok = wait_phase(&empty[st], ((g / nst) & 1) ^ 1, wd, 0x401))) break;
           uint8_t* sa = stages + st * stage_bytes;
@@ -272,7 +285,7 @@ __global__ void __launch_bounds__(gemm_threads(EPI), 1)
         }
       }
       for (int i = (g > nst ? g - nst : 0); i < g; ++i)
-        wait_drain(&full[i % nst], (i / nst) & 1, kDrainLimitNs);
+        if ((i % nst) % kGemmProducers == pidx) wait_drain(&full[i % nst], (i / nst) & 1, kDrainLimitNs);
     }
   } else if (warp == W_MMA) {
     // ------------------------------------------------------------ MMA issuer
