@@ -164,7 +164,9 @@ def test_watchdog_times_out_cleanly_and_context_survives(tt_lib):
     torch.testing.assert_close(out, F.layer_norm(x, (128,)), rtol=2e-5, atol=2e-5)
 
 
-FFN_SHAPES = [(1000, 128, 128), (300, 32, 128), (513, 256, 1024), (129, 64, 256), (4096, 256, 1024), (77, 128, 512)]
+# The last two run 2-3 row tiles per CTA of the persistent kernel.
+FFN_SHAPES = [(1000, 128, 128), (300, 32, 128), (513, 256, 1024), (129, 64, 256), (4096, 256, 1024), (77, 128, 512),
+              (38000, 256, 256), (40000, 128, 128)]
 
 
 @pytest.mark.parametrize("N,D,Fd", FFN_SHAPES)

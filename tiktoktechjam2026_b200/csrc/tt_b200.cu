@@ -18,6 +18,7 @@
 #include "tt_attention.cuh"
 #include "tt_attn_db.cuh"
 #include "tt_ffn.cuh"
+#include "tt_ffn2.cuh"
 #include "tt_gemm.cuh"
 #include "tt_misc.cuh"
 #include "../../include/tt_b200.h"
@@ -353,6 +354,32 @@ int launch_ffn(const FfnMaps& maps, FfnParams p, int sm_count, cudaStream_t stre
   return after_launch("ffn");
 }
 
+// The TMEM-resident-hidden FFN (tt_ffn2.cuh) serves d_model 128 and 256.
+bool ffn2_route(int d_model, int ffn) { return (d_model == 128 || d_model == 256) && ffn % 128 == 0; }
+
+int launch_ffn2(const Ffn2Maps& maps, FfnParams p, int sm_count, cudaStream_t stream) {
+  const long long items = (static_cast<long long>(p.M) + 127) / 128;
+  p.n_items = static_cast<int>(items);
+  const unsigned grid = static_cast<unsigned>(items < sm_count ? items : sm_count);
+  if (p.D == 128) {
+    if (int rc = prepare_kernel(ffn2_kernel<128>, Ffn2Layout<128>::SMEM_ALLOC)) return rc;
+    ffn2_kernel<128><<<grid, kFfn2Threads, Ffn2Layout<128>::SMEM_ALLOC, stream>>>(maps, p);
+  } else if (p.D == 256) {
+    if (int rc = prepare_kernel(ffn2_kernel<256>, Ffn2Layout<256>::SMEM_ALLOC)) return rc;
+    ffn2_kernel<256><<<grid, kFfn2Threads, Ffn2Layout<256>::SMEM_ALLOC, stream>>>(maps, p);
+  } else {
+    return fail(TT_ERR_UNSUPPORTED, "ffn2: d_model %d not in {128, 256}", p.D);
+  }
+  return after_launch("ffn");
+}
+
+int encode_ffn2_maps(Ffn2Maps* maps, const void* a, const void* w1, const void* w2, uint64_t rows, int D, int F) {
+  memset(maps, 0, sizeof(*maps));
+  if (int rc = encode_matrix(&maps->a, a, rows, D, 64, 128)) return rc;
+  if (int rc = encode_matrix(&maps->w1, w1, F, D, 64, 128)) return rc;
+  return encode_matrix(&maps->w2, w2, D, F, 64, D < 256 ? D : 256);
+}
+
 // Tensor maps of the fused FFN for one call.
 int encode_ffn_maps(FfnMaps* maps, const void* a, const void* w1, const void* w2, const float* resid_out,
                     const void* norm_out, bool norm_f32, uint64_t rows, int D, int F) {
@@ -679,8 +706,12 @@ int bind_workspace(tt_model* m, int batch, int seq, void* ws, cudaStream_t strea
       if (m->route.ffn_fused) {
         m->tm_w1f.resize(m->L);
         m->tm_w2f.resize(m->L);
-        if (int rc = encode_matrix(&m->tm_w1f[l], w.w_ffn_in, m->F, m->D, 32, 128)) return rc;
-        if (int rc = encode_matrix(&m->tm_w2f[l], w.w_ffn_out, m->D, m->F, 32, m->D)) return rc;
+        // The TMEM-hidden kernel (d_model 128/256) reads 64-wide K-blocks, the other one 32-wide.
+        const bool f2 = ffn2_route(m->D, m->F);
+        if (int rc = encode_matrix(&m->tm_w1f[l], w.w_ffn_in, m->F, m->D, f2 ? 64 : 32, 128)) return rc;
+        if (int rc = encode_matrix(&m->tm_w2f[l], w.w_ffn_out, m->D, m->F, f2 ? 64 : 32,
+                                   f2 && m->D > 256 ? 256 : m->D))
+          return rc;
       }
     }
     m->bound_ws = nullptr;
@@ -978,6 +1009,31 @@ int tt_ffn_residual_layernorm(const void* a, const void* w1, const float* b1, co
                 "fused FFN needs d_model in {32, 64, 128, 256} and ffn %% 128 == 0 (got %d, %d)", d_model,
                 ffn);
   if (reinterpret_cast<uintptr_t>(b1) % 16 != 0) return fail(TT_ERR_ALIGN, "b1 must be 16-byte aligned");
+  if (ffn2_route(d_model, ffn)) {
+    if ((reinterpret_cast<uintptr_t>(resid_in) | reinterpret_cast<uintptr_t>(resid_out) |
+         reinterpret_cast<uintptr_t>(norm_out)) % 16 != 0)
+      return fail(TT_ERR_ALIGN, "resid_in, resid_out and norm_out must be 16-byte aligned");
+    Ffn2Maps maps2;
+    if (int rc = encode_ffn2_maps(&maps2, a, w1, w2, n_rows, d_model, ffn)) return rc;
+    FfnParams p;
+    memset(&p, 0, sizeof(p));
+    p.M = static_cast<int>(n_rows);
+    p.D = d_model;
+    p.F = ffn;
+    p.b1 = b1;
+    p.b2 = b2;
+    p.gamma = gamma;
+    p.beta = beta;
+    p.resid_in = resid_in;
+    p.resid_out = resid_out;
+    p.norm_out = norm_out;
+    p.norm_f16 = norm_out_is_f16 ? 1 : 0;
+    p.eps = eps;
+    p.row_mask = row_mask;
+    p.err = ds->err;
+    p.timeout_ns = g_timeout_ns.load();
+    return launch_ffn2(maps2, p, ds->sm_count, static_cast<cudaStream_t>(stream));
+  }
   FfnMaps maps;
   if (int rc = encode_ffn_maps(&maps, a, w1, w2, resid_out, norm_out, norm_out_is_f16 == 0, n_rows, d_model, ffn))
     return rc;
@@ -1187,6 +1243,35 @@ int tt_model_forward(tt_model* m, const float* x, const uint8_t* mask, float* ou
       if (int rc = record_begin(m, s, &ev)) return rc;
       if (int rc = launch_gemm(m->ksw_out, EPI_RESID_LN, maps, p, ds->sm_count, s)) return rc;
       if (int rc = record_end(m, s, TT_KERNEL_OUT_LN, ev)) return rc;
+    }
+    if (r.ffn_fused && ffn2_route(D, F)) {
+      // Whole FFN + residual + next norm, hidden activations in TMEM (final_norm ->
+      // FP32 output on the last layer); the residual is updated in place.
+      Ffn2Maps fm;
+      fm.a = m->tm_norm;
+      fm.w1 = m->tm_w1f[l];
+      fm.w2 = m->tm_w2f[l];
+      FfnParams fp;
+      memset(&fp, 0, sizeof(fp));
+      fp.M = N;
+      fp.D = D;
+      fp.F = F;
+      fp.b1 = lw.b_ffn_in;
+      fp.b2 = lw.b_ffn_out;
+      fp.gamma = lw.ln_next_w;
+      fp.beta = lw.ln_next_b;
+      fp.resid_in = reinterpret_cast<const float*>(base + w.resid);
+      fp.resid_out = reinterpret_cast<float*>(base + w.resid);
+      fp.norm_out = last ? static_cast<void*>(out) : static_cast<void*>(norm);
+      fp.norm_f16 = last ? 0 : 1;
+      fp.eps = m->eps;
+      fp.row_mask = last ? mask : nullptr;
+      fp.err = ds->err;
+      fp.timeout_ns = g_timeout_ns.load();
+      if (int rc = record_begin(m, s, &ev)) return rc;
+      if (int rc = launch_ffn2(fm, fp, ds->sm_count, s)) return rc;
+      if (int rc = record_end(m, s, TT_KERNEL_FFN_FUSED, ev)) return rc;
+      continue;
     }
     if (r.ffn_fused) {
       // Whole FFN + residual + next norm (final_norm -> FP32 output on the last layer)

@@ -40,6 +40,9 @@ struct FfnParams {
   const uint8_t* row_mask;
   unsigned int* err;
   unsigned long long timeout_ns;
+  // Direct outputs (ffn2_kernel): residual out [M, D] FP32, normalized [M, D] FP16 or FP32.
+  float* resid_out;
+  void* norm_out;
 };
 
 // Tensor maps: a = input [M, D] FP16 box {32, 128}; w1 = W1 [F, D] FP16 box
