@@ -373,10 +373,22 @@ int launch_ffn2(const Ffn2Maps& maps, FfnParams p, int sm_count, cudaStream_t st
   return after_launch("ffn");
 }
 
+// Row-major [rows, cols] FP16 matrix as K-blocks of 64 columns: the 3-D view
+// {64, rows, cols / 64} (byte strides {cols * 2, 128}), box {64, box_rows,
+// box_kblocks}; one copy writes box_kblocks consecutive [box_rows x 128 B]
+// swizzled blocks.
+int encode_kblocks(CUtensorMap* tm, const void* base, uint64_t rows, uint64_t cols, int box_rows,
+                   int box_kblocks) {
+  const uint64_t dims[3] = {64, rows, cols / 64};
+  const uint64_t strides[2] = {cols * 2, 128};
+  const uint32_t box[3] = {64, static_cast<uint32_t>(box_rows), static_cast<uint32_t>(box_kblocks)};
+  return encode_f16(tm, base, 3, dims, strides, box);
+}
+
 int encode_ffn2_maps(Ffn2Maps* maps, const void* a, const void* w1, const void* w2, uint64_t rows, int D, int F) {
   memset(maps, 0, sizeof(*maps));
-  if (int rc = encode_matrix(&maps->a, a, rows, D, 64, 128)) return rc;
-  if (int rc = encode_matrix(&maps->w1, w1, F, D, 64, 128)) return rc;
+  if (int rc = encode_kblocks(&maps->a, a, rows, D, 128, D / 64)) return rc;
+  if (int rc = encode_kblocks(&maps->w1, w1, F, D, 128, 2)) return rc;
   return encode_matrix(&maps->w2, w2, D, F, 64, D < 256 ? D : 256);
 }
 
@@ -563,6 +575,7 @@ struct tt_model {
   // Epilogue tiles (box 32 x 32): QKV stores, residual (FP32), normalized and hidden (FP16).
   CUtensorMap tm_q_st{}, tm_k_st{}, tm_vt_st{}, tm_resid{}, tm_norm_st{}, tm_hidden_st{};
   CUtensorMap tm_norm32{};  // normalized activations as the fused FFN's A operand (box {32, 128})
+  CUtensorMap tm_norm3{};   // the same as whole 128-row K-block tiles (ffn2_kernel)
   // Profiling.
   bool profiling = false;
   struct Rec {
@@ -708,7 +721,11 @@ int bind_workspace(tt_model* m, int batch, int seq, void* ws, cudaStream_t strea
         m->tm_w2f.resize(m->L);
         // The TMEM-hidden kernel (d_model 128/256) reads 64-wide K-blocks, the other one 32-wide.
         const bool f2 = ffn2_route(m->D, m->F);
-        if (int rc = encode_matrix(&m->tm_w1f[l], w.w_ffn_in, m->F, m->D, f2 ? 64 : 32, 128)) return rc;
+        if (f2) {
+          if (int rc = encode_kblocks(&m->tm_w1f[l], w.w_ffn_in, m->F, m->D, 128, 2)) return rc;
+        } else if (int rc = encode_matrix(&m->tm_w1f[l], w.w_ffn_in, m->F, m->D, 32, 128)) {
+          return rc;
+        }
         if (int rc = encode_matrix(&m->tm_w2f[l], w.w_ffn_out, m->D, m->F, f2 ? 64 : 32,
                                    f2 && m->D > 256 ? 256 : m->D))
           return rc;
@@ -727,6 +744,8 @@ int bind_workspace(tt_model* m, int batch, int seq, void* ws, cudaStream_t strea
   if (!m->route.ffn_fused)
     if (int rc = encode_matrix(&m->tm_hidden, base + w.hidden, N, m->F, m->ksw_out2, 128)) return rc;
   if (int rc = encode_matrix(&m->tm_norm32, base + w.norm, N, m->D, 32, 128)) return rc;
+  if (ffn2_route(m->D, m->F))
+    if (int rc = encode_kblocks(&m->tm_norm3, base + w.norm, N, m->D, 128, m->D / 64)) return rc;
   if (int rc = encode_attention_maps(&m->tm_q, &m->tm_k, &m->tm_vt, base + w.q, base + w.k,
                                      base + w.vt, batch * m->H, seq, hd, w.seq_pad))
     return rc;
@@ -1248,7 +1267,7 @@ int tt_model_forward(tt_model* m, const float* x, const uint8_t* mask, float* ou
       // Whole FFN + residual + next norm, hidden activations in TMEM (final_norm ->
       // FP32 output on the last layer); the residual is updated in place.
       Ffn2Maps fm;
-      fm.a = m->tm_norm;
+      fm.a = m->tm_norm3;
       fm.w1 = m->tm_w1f[l];
       fm.w2 = m->tm_w2f[l];
       FfnParams fp;

@@ -19,32 +19,38 @@
 // issued in the order G1(0) G1(1) G2(0) G1(2) G2(1) ...; acc1[b] is rewritten
 // by G1(c+2) only after G2(c) has read H(c) (the tensor core executes one
 // thread's MMAs in issue order).  With H out of shared memory the weight ring
-// holds 3 x 32 KB (each slot one 32 KB TMA copy or two 16 KB copies), which
-// keeps enough bytes in flight to cover the L2 round trip.
+// holds 4 x 32 KB (each slot one 32 KB TMA copy or two 16 KB copies): one
+// chunk's W1 and W2 blocks, so the next chunk's W1 streams in while G2 waits
+// for the GELU warps.
 //
 // Epilogue (4 warps, one row per thread): one TMEM pass computes
-// r' = acc2 + b2 + r (the residual rows prefetched by cp.async three 32-column
+// r' = acc2 + b2 + r (the residual rows prefetched by cp.async two 16-column
 // tiles ahead), accumulates shifted FP32 sums for the LayerNorm statistics and
 // writes r' with coalesced stores; acc2 is released right after that pass, so
 // the next tile's G2 starts while the second pass re-reads the warp's own r'
 // rows (L2 hits) and writes the normalized rows.  d_model 128 double-buffers
 // acc2 in TMEM.  Warp 12 loads A and the even ring slots, warp 14 the odd
-// ones; warp 13 allocates TMEM and issues the MMAs.
+// ones (more producers: warps 14, 15, ... share the slots round-robin); warp
+// 13 allocates TMEM and issues the MMAs.
 #pragma once
 
 #include "tt_ffn.cuh"
 
 namespace tt {
 
+// a and w1 are 3-D views {64 (k within a K-block), rows, K-blocks} with byte
+// strides {D * 2, 128}, so one TMA copy lays several K-blocks out as
+// consecutive 128-row x 128-byte swizzled blocks (a producer thread
+// completes only about one copy per ~800 cycles, whatever its size).
 struct Ffn2Maps {
-  CUtensorMap a;   // [M, D] FP16, box {64, 128}, SWIZZLE_128B
-  CUtensorMap w1;  // [F, D] FP16, box {64, 128}
-  CUtensorMap w2;  // [D, F] FP16, box {64, min(D, 256)}
+  CUtensorMap a;   // [M, D] FP16, box {64, 128, D / 64} (the whole row tile), SWIZZLE_128B
+  CUtensorMap w1;  // [F, D] FP16, box {64, 128, 2}
+  CUtensorMap w2;  // [D, F] FP16 (2-D), box {64, min(D, 256)}
 };
 
 template <int D>
 struct Ffn2Layout {
-  static constexpr int FC = 128, KB = 64, NST = 3, SLOT = 32768;
+  static constexpr int FC = 128, KB = 64, NST = 4, SLOT = 32768;
   static constexpr int NKA = D / KB;                 // K-blocks of G1
   static constexpr int A_KBLK = 128 * KB * 2;        // 16 KB
   static constexpr int A_BYTES = NKA * A_KBLK;
@@ -55,8 +61,9 @@ struct Ffn2Layout {
   static constexpr int W2_PER_SLOT = SLOT / W2_KBLK;
   static constexpr int W2_SLOTS = (FC / KB) / W2_PER_SLOT;
   static constexpr int W2_BOX_ROWS = D < 256 ? D : 256;
-  static constexpr int RING = 3;      // 32 x 32 FP32 staging tiles per epilogue warp
-  static constexpr int TILE = 4096;
+  static constexpr int JW = 16;       // columns per epilogue job
+  static constexpr int RING = 3;      // 32 x JW FP32 staging tiles per epilogue warp
+  static constexpr int TILE = 32 * JW * 4;
   static constexpr int OFF_A = 0;
   static constexpr int OFF_W = OFF_A + A_BYTES;
   static constexpr int OFF_LN = OFF_W + NST * SLOT;
@@ -77,10 +84,14 @@ struct Ffn2Layout {
 };
 
 // Warp roles: 0..7 GELU (lane quadrant w & 3, hidden half w >> 2 of each
-// chunk), 8..11 residual + LayerNorm, 12 and 14 TMA producers, 13 TMEM
+// chunk), 8..11 residual + LayerNorm, 12 and 14.. TMA producers, 13 TMEM
 // allocator and MMA issuer.
-constexpr int kFfn2Threads = 480;
-constexpr int kFfn2Prod0 = 12, kFfn2Mma = 13, kFfn2Prod1 = 14;
+#ifndef TT_FFN2_PRODUCERS
+#define TT_FFN2_PRODUCERS 2
+#endif
+constexpr int kFfn2Producers = TT_FFN2_PRODUCERS;  // warps 12, 14, 15, ...
+constexpr int kFfn2Threads = 32 * (13 + kFfn2Producers);
+constexpr int kFfn2Prod0 = 12, kFfn2Mma = 13;
 
 template <int D>
 __global__ void __launch_bounds__(kFfn2Threads, 1)
@@ -140,11 +151,11 @@ __global__ void __launch_bounds__(kFfn2Threads, 1)
   const uint32_t tmem_base = *tmem_slot;
   const Watchdog wd{p.err, abort_flag, p.timeout_ns};
 
-  if (warp == kFfn2Prod0 || warp == kFfn2Prod1) {
+  if (warp == kFfn2Prod0 || warp > kFfn2Mma) {
     // ------------------------------------------------------------ producers
-    // Ring slot st is always filled by producer st % 2 (one producer per slot
-    // keeps the parity-based empty-slot wait exact).
-    const int pidx = warp == kFfn2Prod0 ? 0 : 1;
+    // Ring slot st is always filled by producer st % kFfn2Producers (one
+    // producer per slot keeps the parity-based empty-slot wait exact).
+    const int pidx = warp == kFfn2Prod0 ? 0 : warp - kFfn2Mma;
     if (lane == 0) {
       tma_prefetch_desc(&maps.a);
       tma_prefetch_desc(&maps.w1);
@@ -154,14 +165,12 @@ __global__ void __launch_bounds__(kFfn2Threads, 1)
       // One slot: W1 K-blocks of chunk c (G1) or W2 hidden K-blocks of chunk c (G2).
       auto slot_load = [&](bool g2, int c, int s) -> bool {
         const int st = g % NST;
-        if (st % 2 == pidx) {
+        if (st % kFfn2Producers == pidx) {
           if (!wait_phase(&w_empty[st], ((g / NST) & 1) ^ 1, wd, 0x601)) return false;
           mbar_arrive_expect_tx(&w_full[st], L::SLOT);
           uint8_t* dst = smem + L::OFF_W + st * L::SLOT;
           if (!g2) {
-#pragma unroll
-            for (int q = 0; q < L::W1_PER_SLOT; ++q)
-              tma_load_2d(dst + q * L::W1_KBLK, &maps.w1, &w_full[st], (s * L::W1_PER_SLOT + q) * L::KB, c * FC);
+            tma_load_3d(dst, &maps.w1, &w_full[st], 0, c * FC, s * L::W1_PER_SLOT);
           } else {
 #pragma unroll
             for (int q = 0; q < L::W2_PER_SLOT; ++q)
@@ -177,8 +186,7 @@ __global__ void __launch_bounds__(kFfn2Threads, 1)
         if (pidx == 0) {
           if (!(ok = wait_phase(a_empty, (i & 1) ^ 1, wd, 0x602))) break;
           mbar_arrive_expect_tx(a_full, L::A_BYTES);
-          for (int kb = 0; kb < L::NKA; ++kb)
-            tma_load_2d(smem + L::OFF_A + kb * L::A_KBLK, &maps.a, a_full, kb * L::KB, m0);
+          tma_load_3d(smem + L::OFF_A, &maps.a, a_full, 0, m0, 0);
           // The epilogue of the next tile reads its residual rows: start them towards L2 now.
           const int wn = w + static_cast<int>(gridDim.x);
           if (wn < p.n_items) {
@@ -196,7 +204,7 @@ __global__ void __launch_bounds__(kFfn2Threads, 1)
       }
       if (pidx == 0 && i > 0) wait_drain(a_full, (i - 1) & 1, kDrainLimitNs);
       for (int q = (g > NST ? g - NST : 0); q < g; ++q)
-        if ((q % NST) % 2 == pidx) wait_drain(&w_full[q % NST], (q / NST) & 1, kDrainLimitNs);
+        if ((q % NST) % kFfn2Producers == pidx) wait_drain(&w_full[q % NST], (q / NST) & 1, kDrainLimitNs);
     }
   } else if (warp == kFfn2Mma) {
     // ------------------------------------------------------------ MMA issuer
@@ -313,32 +321,36 @@ __global__ void __launch_bounds__(kFfn2Threads, 1)
     const int ew = warp - 8;
     const uint32_t lane_base = static_cast<uint32_t>(ew * 32) << 16;
     const uint32_t ring = smem_u32(smem + L::OFF_LN) + ew * L::RING * L::TILE;
-    constexpr int nch = D / 32;
-    // Staging tile layout: 32 rows x 128 bytes, 16-byte piece k of row r at
-    // r * 128 + ((k ^ (r & 7)) << 4) (conflict-free by rows and by pieces).
-    // Job j of a tile: j < nch reads the residual input chunk j, j >= nch
-    // reads back this warp's own r' chunk j - nch.  Jobs run in one sequence
-    // across tiles (number jg = 2 * nch * tile_count + j) and job jg stages in
-    // slot jg % RING, two jobs ahead of the one being consumed.
+    constexpr int JW = L::JW;      // columns per job
+    constexpr int nch = D / JW;    // jobs per pass
+    constexpr int RB = JW * 4;     // bytes per staged FP32 row (64)
+    constexpr int PR = RB / 16;    // 16-byte pieces per row (4)
+    // Staging tile layout: 32 rows x 64 bytes, 16-byte piece k of row r at
+    // r * 64 + ((k ^ ((r >> 1) & 3)) << 4) (conflict-free by rows and by pieces).
+    // Job j of a tile: j < nch reads the residual input columns [j*JW, +JW),
+    // j >= nch reads back this warp's own r' columns of job j - nch.  Jobs run
+    // in one sequence across tiles (number jg = 2 * nch * tile_count + j) and
+    // job jg stages in slot jg % RING, two jobs ahead of the one consumed.
+    auto sw = [](int r, int k) { return r * RB + ((k ^ ((r >> 1) & 3)) << 4); };
     auto issue = [&](int tile, int j, int jg) {
       const int r0 = tile * 128 + ew * 32;
       const int c = j % nch;
       const float* src = (j < nch) ? p.resid_in : p.resid_out;
       const uint32_t slot = ring + (jg % L::RING) * L::TILE;
 #pragma unroll
-      for (int k = 0; k < 8; ++k) {
-        const int r = k * 4 + (lane >> 3), piece = lane & 7;
+      for (int k = 0; k < 32 / (32 / PR); ++k) {
+        const int r = k * (32 / PR) + lane / PR, piece = lane % PR;
         const int row = r0 + r;
         const bool v = row < p.M;
-        const float* g = src + static_cast<size_t>(v ? row : 0) * D + c * 32 + piece * 4;
-        cp_async_16(slot + r * 128 + ((piece ^ (r & 7)) << 4), g, v ? 16u : 0u);
+        const float* g = src + static_cast<size_t>(v ? row : 0) * D + c * JW + piece * 4;
+        cp_async_16(slot + sw(r, piece), g, v ? 16u : 0u);
       }
     };
-    // The staged tile as this thread's row (32 floats).
+    // The staged tile as this thread's row (JW floats).
     auto read_row = [&](uint32_t slot, float* x) {
 #pragma unroll
-      for (int k = 0; k < 8; ++k) {
-        const uint4 q = ld_shared_v4(slot + lane * 128 + ((k ^ (lane & 7)) << 4));
+      for (int k = 0; k < PR; ++k) {
+        const uint4 q = ld_shared_v4(slot + sw(lane, k));
         x[4 * k] = __uint_as_float(q.x);
         x[4 * k + 1] = __uint_as_float(q.y);
         x[4 * k + 2] = __uint_as_float(q.z);
@@ -347,18 +359,18 @@ __global__ void __launch_bounds__(kFfn2Threads, 1)
     };
     auto write_row = [&](uint32_t slot, const float* x) {
 #pragma unroll
-      for (int k = 0; k < 8; ++k)
-        st_shared_v4(slot + lane * 128 + ((k ^ (lane & 7)) << 4), __float_as_uint(x[4 * k]),
-                     __float_as_uint(x[4 * k + 1]), __float_as_uint(x[4 * k + 2]), __float_as_uint(x[4 * k + 3]));
+      for (int k = 0; k < PR; ++k)
+        st_shared_v4(slot + sw(lane, k), __float_as_uint(x[4 * k]), __float_as_uint(x[4 * k + 1]),
+                     __float_as_uint(x[4 * k + 2]), __float_as_uint(x[4 * k + 3]));
     };
-    // Coalesced copy-out of a staged FP32 tile (8 lanes per 128-byte row).
+    // Coalesced copy-out of a staged FP32 tile (PR lanes per row).
     auto store_f32 = [&](uint32_t slot, float* dst, int r0, int c) {
 #pragma unroll
-      for (int k = 0; k < 8; ++k) {
-        const int r = k * 4 + (lane >> 3), piece = lane & 7;
-        const uint4 q = ld_shared_v4(slot + r * 128 + ((piece ^ (r & 7)) << 4));
+      for (int k = 0; k < PR; ++k) {
+        const int r = k * (32 / PR) + lane / PR, piece = lane % PR;
+        const uint4 q = ld_shared_v4(slot + sw(r, piece));
         if (r0 + r < p.M)
-          *reinterpret_cast<uint4*>(dst + static_cast<size_t>(r0 + r) * D + c * 32 + piece * 4) = q;
+          *reinterpret_cast<uint4*>(dst + static_cast<size_t>(r0 + r) * D + c * JW + piece * 4) = q;
       }
     };
     int i = 0;
@@ -397,10 +409,10 @@ __global__ void __launch_bounds__(kFfn2Threads, 1)
       float shift = 0.f, s1 = 0.f, s2 = 0.f;
 #pragma unroll 1
       for (int c = 0; c < nch; ++c) {
-        uint32_t v[32];
-        tmem_ld_x32(tacc2 + c * 32, v);
+        uint32_t v[JW];
+        tmem_ld_x16(tacc2 + c * JW, v);
         const uint32_t slot = advance(c);
-        float x[32];
+        float x[JW];
         read_row(slot, x);
         tmem_ld_wait_tied(v);
         if (c == nch - 1) {
@@ -408,9 +420,9 @@ __global__ void __launch_bounds__(kFfn2Threads, 1)
           __syncwarp();
           if (lane == 0) mbar_arrive(&acc2_empty[ib]);  // acc2 may take the next tile's G2
         }
-        const float4* b2 = reinterpret_cast<const float4*>(s_b2 + c * 32);
+        const float4* b2 = reinterpret_cast<const float4*>(s_b2 + c * JW);
 #pragma unroll
-        for (int k = 0; k < 8; ++k) {
+        for (int k = 0; k < PR; ++k) {
           const float4 bb = b2[k];
           x[4 * k] += __uint_as_float(v[4 * k]) + bb.x;
           x[4 * k + 1] += __uint_as_float(v[4 * k + 1]) + bb.y;
@@ -419,7 +431,7 @@ __global__ void __launch_bounds__(kFfn2Threads, 1)
         }
         if (c == 0) shift = x[0];
 #pragma unroll
-        for (int e = 0; e < 32; ++e) {
+        for (int e = 0; e < JW; ++e) {
           const float d = x[e] - shift;
           s1 += d;
           s2 = fmaf(d, d, s2);
@@ -440,12 +452,12 @@ __global__ void __launch_bounds__(kFfn2Threads, 1)
 #pragma unroll 1
       for (int c = 0; c < nch; ++c) {
         const uint32_t slot = advance(nch + c);
-        float x[32];
+        float x[JW];
         read_row(slot, x);
-        const float4* g4 = reinterpret_cast<const float4*>(s_gamma + c * 32);
-        const float4* b4 = reinterpret_cast<const float4*>(s_beta + c * 32);
+        const float4* g4 = reinterpret_cast<const float4*>(s_gamma + c * JW);
+        const float4* b4 = reinterpret_cast<const float4*>(s_beta + c * JW);
 #pragma unroll
-        for (int k = 0; k < 8; ++k) {
+        for (int k = 0; k < PR; ++k) {
           const float4 gg = g4[k], bb = b4[k];
           x[4 * k] = zero_row ? 0.f : fmaf((x[4 * k] - mean) * rstd, gg.x, bb.x);
           x[4 * k + 1] = zero_row ? 0.f : fmaf((x[4 * k + 1] - mean) * rstd, gg.y, bb.y);
@@ -454,20 +466,20 @@ __global__ void __launch_bounds__(kFfn2Threads, 1)
         }
         __syncwarp();
         if (p.norm_f16) {
-          // 32 rows x 64 bytes: piece k (8 halves) of row r at r * 64 + ((k ^ ((r >> 1) & 3)) << 4).
+          // 32 rows x 32 bytes: piece k (8 halves) of row r at r * 32 + ((k ^ ((r >> 2) & 1)) << 4).
 #pragma unroll
-          for (int k = 0; k < 4; ++k)
-            st_shared_v4(slot + lane * 64 + ((k ^ ((lane >> 1) & 3)) << 4), pack_half2(x[8 * k], x[8 * k + 1]),
+          for (int k = 0; k < JW / 8; ++k)
+            st_shared_v4(slot + lane * 32 + ((k ^ ((lane >> 2) & 1)) << 4), pack_half2(x[8 * k], x[8 * k + 1]),
                          pack_half2(x[8 * k + 2], x[8 * k + 3]), pack_half2(x[8 * k + 4], x[8 * k + 5]),
                          pack_half2(x[8 * k + 6], x[8 * k + 7]));
           __syncwarp();
           __half* dst = static_cast<__half*>(p.norm_out);
 #pragma unroll
-          for (int k = 0; k < 4; ++k) {
-            const int r = k * 8 + (lane >> 2), piece = lane & 3;
-            const uint4 q = ld_shared_v4(slot + r * 64 + ((piece ^ ((r >> 1) & 3)) << 4));
+          for (int k = 0; k < JW / 8; ++k) {
+            const int r = k * 16 + (lane >> 1), piece = lane & 1;
+            const uint4 q = ld_shared_v4(slot + r * 32 + ((piece ^ ((r >> 2) & 1)) << 4));
             if (r0 + r < p.M)
-              *reinterpret_cast<uint4*>(dst + static_cast<size_t>(r0 + r) * D + c * 32 + piece * 8) = q;
+              *reinterpret_cast<uint4*>(dst + static_cast<size_t>(r0 + r) * D + c * JW + piece * 8) = q;
           }
         } else {
           write_row(slot, x);
