@@ -390,39 +390,10 @@ __global__ void __launch_bounds__(gemm_threads(EPI), 1)
           }
           const int which = col0 / D;
           const int within0 = col0 - which * D;
-          if (p.tma_out) {
-            if (!warp_active) continue;
-            const uint32_t slot = ring.acquire(lane);
-            if (wbox == 32) {
-              if (which < 2)
-                stage_row_f16x32(slot, r, f);
-              else
-                stage_cols_f16<32>(slot, lane, f);
-            } else {
-              if (which < 2) {
-                stage_row_f16x16(slot, r, f);
-                stage_row_f16x16(slot + 1024, r, f + 16);
-              } else {
-                stage_cols_f16<16>(slot, lane, f);
-                stage_cols_f16<16>(slot + 1024, lane, f + 16);
-              }
-            }
-            ring.publish();
-            if (lane == 0) {
-              const int nsub = 32 / wbox;
-              for (int sb = 0; sb < nsub; ++sb) {
-                const int within = within0 + sb * wbox;
-                const int hh = within / hd, d0 = within - hh * hd;
-                const int bh = b_w * p.heads + hh;
-                const uint32_t sub = slot + sb * 1024;
-                if (which == 0) tma_store_3d(&maps.out0, sub, d0, s0, bh);
-                else if (which == 1) tma_store_3d(&maps.out1, sub, d0, s0, bh);
-                else tma_store_3d(&maps.out2, sub, s0, d0, bh);
-              }
-              bulk_commit_group();
-            }
-          } else if (valid) {
-            if (which < 2) {
+          if (which < 2) {
+            // Q / K: a thread's 32 values are consecutive features of its row, in runs of
+            // 16 that are each 32 contiguous bytes of [B*H, S, hd].
+            if (valid) {
               __half* base = which == 0 ? p.q : p.k;
 #pragma unroll
               for (int gq = 0; gq < 2; ++gq) {
@@ -442,14 +413,39 @@ __global__ void __launch_bounds__(gemm_threads(EPI), 1)
                 dst[0] = a;
                 dst[1] = bq;
               }
+            }
+          } else if (p.tma_out) {
+            // V^T: transpose the 32 rows through this warp's staging tile, then write
+            // [wbox features x 32 tokens] as 64-byte rows of [B*H, hd, S_pad] with
+            // coalesced 16-byte stores (the slab lies within one sequence: S % 32 == 0).
+            if (!warp_active) continue;
+            const uint32_t slot = ring.base;
+            __syncwarp();
+            if (wbox == 32) {
+              stage_cols_f16<32>(slot, lane, f);
             } else {
-#pragma unroll
-              for (int e = 0; e < 32; ++e) {
-                const int within = within0 + e;
-                const int hh = within / hd, d = within - hh * hd;
-                p.vt[((static_cast<size_t>(bidx) * p.heads + hh) * hd + d) * p.seq_pad + s] =
-                    __float2half_rn(f[e]);
+              stage_cols_f16<16>(slot, lane, f);
+              stage_cols_f16<16>(slot + 1024, lane, f + 16);
+            }
+            __syncwarp();
+#pragma unroll 1
+            for (int sb = 0; sb < 32 / wbox; ++sb) {
+              const int within = within0 + sb * wbox;
+              const int hh = within / hd, d0 = within - hh * hd;
+              const size_t bh = static_cast<size_t>(b_w) * p.heads + hh;
+              for (int k = 0; k < wbox / 8; ++k) {
+                const int d = k * 8 + (lane >> 2), pc = lane & 3;
+                const uint4 q = ld_shared_v4(slot + sb * 1024 + d * 64 + ((pc ^ ((d >> 1) & 3)) << 4));
+                *reinterpret_cast<uint4*>(p.vt + (bh * hd + d0 + d) * p.seq_pad + s0 + pc * 8) = q;
               }
+            }
+          } else if (valid) {
+#pragma unroll
+            for (int e = 0; e < 32; ++e) {
+              const int within = within0 + e;
+              const int hh = within / hd, d = within - hh * hd;
+              p.vt[((static_cast<size_t>(bidx) * p.heads + hh) * hd + d) * p.seq_pad + s] =
+                  __float2half_rn(f[e]);
             }
           }
         }
