@@ -10,9 +10,12 @@
 //    128-query tile of its own work item, with 4 softmax warps (one per TMEM
 //    lane quadrant, a whole row per thread), its own TMA producer warp (8 + s)
 //    and its own MMA-issuer warp (10 + s);
-//  * key tiles are 64 wide and both the scores S (TMEM) and the probabilities
-//    P (shared memory) are double buffered, so S_{t+1} and S_{t+2} are computed
-//    and P_{t-1} is consumed while the softmax works on tile t.
+//  * key tiles are 64 wide and the scores S are double buffered in TMEM; the
+//    softmax writes the FP16 probabilities P back over the first 32 columns of
+//    the S buffer it has just read (one tcgen05.st, no shared memory and no
+//    proxy fence), and P.V reads them as a TMEM A operand.  S_{t+2} is issued
+//    right after P.V of tile t into the same buffer: one thread's MMAs execute
+//    in issue order, so P_t is read before it is overwritten.
 //
 // Per stream and key tile t (buffer b = t & 1):
 //   S_b = Q K_t^T           TMEM, 64 FP32 columns
@@ -21,8 +24,8 @@
 //   maximum m only moves when the tile maximum exceeds it by more than 2^8
 //   (O and l are then rescaled, rare after the first tiles), so P stays <= 256
 //   in FP16; exp2 of S*scale*log2(e) - m (MUFU, with a share of the
-//   exponentials on the FP32 pipe); P is rounded to FP16 into the
-//   128B-swizzled K-major tile P_b
+//   exponentials on the FP32 pipe); P is rounded to FP16 pairs into
+//   columns 0..31 of S_b
 //   [O | l] += P_b [V_t | 1]  TMEM, accumulated over the item's key tiles (two
 //                           buffers by item, so an item's epilogue runs after
 //                           the next item's first tile).  Each V^T stage is
@@ -46,15 +49,13 @@ struct AttnDbLayout {
   static constexpr int ONES_BYTES = 16 * 128;           // 16 rows of 64 FP16 ones after each V^T block
   static constexpr int V_STAGE = V_BYTES + ONES_BYTES;  // B operand of P.[V | 1], N = ON rows
   static constexpr int ON = HD + 16;                    // accumulator columns: O, then 16 copies of l
-  static constexpr int P_BYTES = BM * BN * 2;
-  // Per-stream region: Q[2] | K[NST] | V[NST] (each with its ones block) | P[2]
+  // Per-stream region: Q[2] | K[NST] | V[NST] (each with its ones block)
   static constexpr int S_Q = 0;
   static constexpr int S_K = S_Q + 2 * Q_BYTES;
   static constexpr int S_V = S_K + NST * K_BYTES;
-  static constexpr int S_P = S_V + NST * V_STAGE;
-  static constexpr int STREAM_BYTES = S_P + 2 * P_BYTES;
+  static constexpr int STREAM_BYTES = S_V + NST * V_STAGE;
   // Per-stream barriers: q_full[2] q_empty[2] kv_full[NST] kv_empty[NST]
-  // s_full[2] s_free[2] p_full[2] p_empty[2] o_full[2] o_free[2]
+  // s_full[2] (unused)[2] p_full[2] pv_done[2] o_full[2] o_free[2]
   static constexpr int B_QF = 0, B_QE = 2, B_KF = 4, B_KE = 4 + NST, B_SF = 4 + 2 * NST,
                        B_SR = B_SF + 2, B_PF = B_SF + 4, B_PE = B_SF + 6, B_OF = B_SF + 8,
                        B_OR = B_SF + 10;
@@ -75,8 +76,7 @@ struct AttnDbLayout {
   static_assert(256 * REGS_SOFTMAX + 128 * REGS_OTHER <= THREADS * REGS_LAUNCH, "register split");
   static_assert(TMEM_O + 2 * ON <= TMEM_STREAM, "TMEM budget");
   static_assert(HD == 16 || HD == 32, "this kernel covers head_dim 16 and 32");
-  static_assert(STREAM_BYTES % 1024 == 0 && S_V % 1024 == 0 && S_P % 1024 == 0 && V_STAGE % 1024 == 0,
-                "alignment");
+  static_assert(STREAM_BYTES % 1024 == 0 && S_V % 1024 == 0 && V_STAGE % 1024 == 0, "alignment");
   static_assert(SMEM_ALLOC <= 232448, "shared memory budget");
 };
 
@@ -224,8 +224,8 @@ __global__ void __launch_bounds__(384, 1)
         const int st = u % NST, qb = it_s & 1, bb = u & 1;
         if (j_s == 0 && !wait_phase(&b[L::B_QF + qb], (it_s >> 1) & 1, wd, 0x231)) return false;
         if (!wait_phase(&b[L::B_KF + st], (u / NST) & 1, wd, 0x232)) return false;
-        // S buffer bb was last read by the softmax at tile u - 2.
-        if (u >= 2 && !wait_phase(&b[L::B_SR + bb], ((u >> 1) - 1) & 1, wd, 0x233)) return false;
+        // S buffer bb last held P_{u-2}, read by P.V of tile u - 2, which this
+        // thread issued before this MMA (same-thread MMAs execute in order).
         tc_fence_after();
 #pragma unroll
         for (int kk = 0; kk < HD / 16; ++kk) {
@@ -248,11 +248,9 @@ __global__ void __launch_bounds__(384, 1)
       int w_o = first_item(2 * static_cast<int>(blockIdx.x) + s), j_o = 0, it_o = 0;
       int n_o = w_o < n_items ? n_tiles(attn_item(p, w_o, n_qt)) : 0;
       bool ok = true;
-      for (int t = 0; ok; ++t) {
-        // Keep the scores up to two tiles ahead of P.V: S_{t+2} only needs the
-        // softmax to have read S_t, which it does before publishing P_t.
-        while (ok && w_s < n_items && u <= t + 2) ok = issue_s();
-        if (!ok || t >= u) break;
+      // Scores of the first two tiles, then per tile t: P.V_t, then S_{t+2}.
+      for (int k = 0; ok && k < 2 && w_s < n_items; ++k) ok = issue_s();
+      for (int t = 0; ok && t < u; ++t) {
         const int bb = t & 1, st = t % NST, ob = it_o & 1;
         if (!(ok = wait_phase(&b[L::B_PF + bb], (t >> 1) & 1, wd, 0x234))) break;
         if (j_o == 0 && !(ok = wait_phase(&b[L::B_OR + ob], ((it_o >> 1) & 1) ^ 1, wd, 0x235))) break;
@@ -260,12 +258,12 @@ __global__ void __launch_bounds__(384, 1)
         const uint32_t tO = tS + L::TMEM_O + ob * L::ON;
 #pragma unroll
         for (int kk = 0; kk < BN / 16; ++kk) {
-          const uint64_t da = umma_sdesc(sb + L::S_P + bb * L::P_BYTES + kk * 32, 1024, kSw128);
+          // Keys 16kk .. 16kk+15 of P_t: columns 8kk .. 8kk+7 of S buffer bb (FP16 pairs).
           const uint64_t db = umma_sdesc(sb + L::S_V + st * L::V_STAGE + kk * 32, 1024, kSw128);
-          umma_f16(tO, da, db, idesc_o, (kk > 0 || j_o > 0) ? 1u : 0u);
+          umma_f16_ts(tO, tS + bb * BN + kk * 8, db, idesc_o, (kk > 0 || j_o > 0) ? 1u : 0u);
         }
         umma_commit(&b[L::B_KE + st]);
-        umma_commit(&b[L::B_PE + bb]);
+        umma_commit(&b[L::B_PE + bb]);  // P.V of tile t done (the rescale path waits on it)
         if (++j_o == n_o) {
           umma_commit(&b[L::B_OF + ob]);  // O of this item is final
           j_o = 0;
@@ -273,6 +271,7 @@ __global__ void __launch_bounds__(384, 1)
           w_o = first_item(w_o + G2);
           n_o = w_o < n_items ? n_tiles(attn_item(p, w_o, n_qt)) : 0;
         }
+        if (w_s < n_items) ok = issue_s();  // S_{t+2} into buffer bb
       }
       // All MMAs this thread issued must finish before TMEM is released.
       umma_commit(&done[s]);
@@ -286,7 +285,6 @@ __global__ void __launch_bounds__(384, 1)
     const int row = q * 32 + lane;
     uint64_t* b = bars_all + s * L::NBAR_STREAM;
     const uint32_t tS = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + s * L::TMEM_STREAM;
-    const uint32_t p_row = smem_u32(smem + s * L::STREAM_BYTES + L::S_P) + row * 128;
     const float sl2 = p.scale_log2;
     const uint64_t sl2x2 = f2_pack(sl2, sl2);
     bool ok = true;
@@ -374,9 +372,6 @@ __global__ void __launch_bounds__(384, 1)
         tmem_ld_x32(tS + bb * BN + 32, sc[1]);
         tmem_ld_wait_tied(sc[0]);
         tmem_ld_wait_tied(sc[1]);
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&b[L::B_SR + bb]);
         if (need_mask) {
 #pragma unroll
           for (int g = 0; g < 2; ++g) {
@@ -430,14 +425,14 @@ __global__ void __launch_bounds__(384, 1)
         }
         m_run = m_new;
 
-        // P buffer bb was last read by P.V of tile t-2.
-        if (!(ok = warp_wait_phase(&b[L::B_PE + bb], ((t >> 1) & 1) ^ 1, wd, 0x334))) break;
-        // Probabilities: FP16 into P_bb (their row sum comes from the P.[V | 1] MMA).
+        // Probabilities: FP16 pairs over columns 0..31 of S_bb (their row sum
+        // comes from the P.[V | 1] MMA).  P.V of tile t-2, the last reader of
+        // this buffer, finished before S_t was computed into it.
         const uint64_t negm = f2_pack(-m_use, -m_use);
-        const uint32_t prow = p_row + bb * L::P_BYTES;
+        uint32_t pk_all[32];
 #pragma unroll
         for (int g = 0; g < 2; ++g) {
-          uint32_t pk[16];
+          uint32_t* pk = pk_all + 16 * g;
 #pragma unroll
           for (int e = 0; e < 16; ++e) {
             const uint64_t xx =
@@ -455,14 +450,9 @@ __global__ void __launch_bounds__(384, 1)
               pk[e] = pack_half2(f2_lo(pp), f2_hi(pp));
             }
           }
-#pragma unroll
-          for (int qq = 0; qq < 4; ++qq) {
-            const int ch = g * 4 + qq;  // 16-byte chunk of the 128-byte row
-            st_shared_v4(prow + ((ch ^ (row & 7)) << 4), pk[4 * qq], pk[4 * qq + 1], pk[4 * qq + 2],
-                         pk[4 * qq + 3]);
-          }
         }
-        fence_proxy_async_smem();
+        tmem_st_x32(tS + bb * BN, pk_all);
+        tmem_st_wait();
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&b[L::B_PF + bb]);
