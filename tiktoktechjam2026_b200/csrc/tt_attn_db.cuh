@@ -6,18 +6,21 @@
 // score) bounds the kernel, so the layout keeps the softmax warps from ever
 // waiting on the tensor core:
 //
-//  * one CTA per SM runs two independent pipelines ("streams"), each on a
-//    128-query tile of its own work item, with 4 softmax warps (one per TMEM
-//    lane quadrant, a whole row per thread), its own TMA producer warp (8 + s)
-//    and its own MMA-issuer warp (10 + s);
-//  * key tiles are 64 wide and the scores S are double buffered in TMEM; the
-//    softmax writes the FP16 probabilities P back over the first 32 columns of
-//    the S buffer it has just read (one tcgen05.st, no shared memory and no
-//    proxy fence), and P.V reads them as a TMEM A operand.  S_{t+2} is issued
-//    right after P.V of tile t into the same buffer: one thread's MMAs execute
-//    in issue order, so P_t is read before it is overwritten.
+//  * one CTA per SM runs NS independent pipelines ("streams", 2 by default),
+//    each on a 128-query tile of its own work item, with 4 softmax warps (one
+//    per TMEM lane quadrant, a whole row per thread), its own TMA producer warp
+//    (4 NS + s) and its own MMA-issuer warp (5 NS + s); idle warps complete
+//    the last warpgroup (setmaxnreg acts on whole warpgroups);
+//  * key tiles are 64 wide; each stream has NSB score buffers S in TMEM (1 with
+//    3 streams, 2 with 2 streams); the softmax writes the FP16 probabilities P
+//    back over the first 32 columns of the S buffer it has just read (one
+//    tcgen05.st, no shared memory and no proxy fence), and P.V reads them as a
+//    TMEM A operand.  S_{t+NSB} is issued right after P.V of tile t into the
+//    same buffer: one thread's MMAs execute in issue order, so P_t is read
+//    before it is overwritten.  With one buffer the softmax of a stream waits
+//    for its next S after publishing P; the other streams' warps fill that gap.
 //
-// Per stream and key tile t (buffer b = t & 1):
+// Per stream and key tile t (buffer b = t % NSB):
 //   S_b = Q K_t^T           TMEM, 64 FP32 columns
 //   softmax: the 64 scores of a row come into registers in one TMEM read and
 //   S_b is released at once; row max by a 3-input max tree; the reference
@@ -33,16 +36,24 @@
 //                           (N = HD + 16) also sums the FP16 probabilities
 //                           of every row: the softmax warps never add them.
 // Items (sequence*head, query tile) are dealt heavy-first: stream s of CTA c
-// takes items 2c+s, 2c+s+2G, ... (G = gridDim.x).
+// takes items NS c + s, NS c + s + NS G, ... (G = gridDim.x).
 #pragma once
 
 #include "tt_attention.cuh"
 
 namespace tt {
 
+// Streams per CTA (3: one S buffer each; 2: two S buffers each).
+#ifndef TT_DB_STREAMS
+#define TT_DB_STREAMS 2
+#endif
+
 template <int HD>
 struct AttnDbLayout {
-  static constexpr int BM = 128, BN = 64, NST = (HD == 16 ? 8 : 6);
+  static constexpr int NS = TT_DB_STREAMS;         // independent pipelines per CTA
+  static constexpr int NSB = NS == 3 ? 1 : 2;      // S (and P) buffers per stream
+  static constexpr int BM = 128, BN = 64;
+  static constexpr int NST = NS == 3 ? (HD == 16 ? 6 : 4) : (HD == 16 ? 8 : 6);
   static constexpr int Q_BYTES = BM * HD * 2;
   static constexpr int K_BYTES = BN * HD * 2;
   static constexpr int V_BYTES = HD * 128;  // V^T block: HD rows of 64 keys (128 bytes)
@@ -60,21 +71,29 @@ struct AttnDbLayout {
                        B_SR = B_SF + 2, B_PF = B_SF + 4, B_PE = B_SF + 6, B_OF = B_SF + 8,
                        B_OR = B_SF + 10;
   static constexpr int NBAR_STREAM = B_SF + 12;
-  static constexpr int OFF_BAR = 2 * STREAM_BYTES;
-  static constexpr int OFF_DONE = OFF_BAR + 2 * NBAR_STREAM * 8;  // done[2]
-  static constexpr int OFF_MISC = OFF_DONE + 16;
+  static constexpr int OFF_BAR = NS * STREAM_BYTES;
+  static constexpr int OFF_DONE = OFF_BAR + NS * NBAR_STREAM * 8;  // done[NS]
+  static constexpr int OFF_MISC = OFF_DONE + 32;
   static constexpr int SMEM_ALLOC = OFF_MISC + 16 + 1024;
-  // TMEM per stream: S_0 at 0, S_1 at 64, [O | l] of item buffer ob at 128 + ob * ON.
-  static constexpr int TMEM_COLS = 512, TMEM_STREAM = 256, TMEM_O = 128;
-  static constexpr int THREADS = 384;  // 8 softmax warps, 2 producers, 2 MMA issuers
-  // Register split (setmaxnreg): the launch provides 384 x 168.
-#ifndef TT_DB_REGS_SOFTMAX
-#define TT_DB_REGS_SOFTMAX 216
-#define TT_DB_REGS_OTHER 56
-#endif
-  static constexpr int REGS_LAUNCH = 168, REGS_SOFTMAX = TT_DB_REGS_SOFTMAX, REGS_OTHER = TT_DB_REGS_OTHER;
-  static_assert(256 * REGS_SOFTMAX + 128 * REGS_OTHER <= THREADS * REGS_LAUNCH, "register split");
-  static_assert(TMEM_O + 2 * ON <= TMEM_STREAM, "TMEM budget");
+  // TMEM per stream: S buffers at 0, 64, ..., [O | l] of item buffer ob at NSB * 64 + ob * ON.
+  static constexpr int TMEM_COLS = 512, TMEM_O = NSB * BN, TMEM_STREAM = TMEM_O + 2 * ON;
+  // Warps: 4 NS softmax (stream w / 4, lane quadrant w % 4), NS producers, NS
+  // MMA issuers, then idle warps up to a whole number of warpgroups:
+  // setmaxnreg is a warpgroup operation, so every warpgroup must be complete.
+  static constexpr int W_PROD = 4 * NS, W_MMA = 5 * NS;
+  static constexpr int NWARPS = 4 * NS + (2 * NS + 3) / 4 * 4;
+  static constexpr int THREADS = 32 * NWARPS;
+  // Register split (setmaxnreg): the launch provides THREADS x REGS_LAUNCH;
+  // the 4 NS softmax warps take REGS_SOFTMAX each, all other warps REGS_OTHER.
+  // The launcher refuses to start the kernel unless it was built with exactly
+  // REGS_LAUNCH registers per thread (a split above the launch total would make
+  // setmaxnreg.inc wait forever).
+  static constexpr int REGS_LAUNCH = NS == 3 ? 96 : 168;
+  static constexpr int REGS_SOFTMAX = NS == 3 ? 128 : 216, REGS_OTHER = NS == 3 ? 48 : 56;
+  static_assert(NWARPS % 4 == 0, "whole warpgroups");
+  static_assert(128 * NS * REGS_SOFTMAX + 32 * (NWARPS - 4 * NS) * REGS_OTHER <= THREADS * REGS_LAUNCH,
+                "register split");
+  static_assert(NS * TMEM_STREAM <= TMEM_COLS, "TMEM budget");
   static_assert(HD == 16 || HD == 32, "this kernel covers head_dim 16 and 32");
   static_assert(STREAM_BYTES % 1024 == 0 && S_V % 1024 == 0 && V_STAGE % 1024 == 0, "alignment");
   static_assert(SMEM_ALLOC <= 232448, "shared memory budget");
@@ -98,7 +117,7 @@ constexpr int kDbExpFmaOf8 = TT_DB_EXP_FMA_OF8;
 // EXP16: probabilities from ex2.approx.f16x2 on FP16-rounded x (two per MUFU
 // operation, already packed for the P tile); otherwise FP32 exponentials.
 template <int HD, bool EXP16>
-__global__ void __launch_bounds__(384, 1)
+__global__ void __launch_bounds__(AttnDbLayout<HD>::THREADS, 1)
     attn_db_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                        const __grid_constant__ CUtensorMap tmV, const AttnParams p, int n_items) {
   using L = AttnDbLayout<HD>;
@@ -109,16 +128,16 @@ __global__ void __launch_bounds__(384, 1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n_qt = (p.seq + BM - 1) / BM;
   const int D = p.heads * HD;
-  const int G2 = 2 * static_cast<int>(gridDim.x);
+  constexpr int NS = L::NS, NSB = L::NSB;
+  const int G2 = NS * static_cast<int>(gridDim.x);  // item stride of one stream
   uint64_t* bars_all = reinterpret_cast<uint64_t*>(smem + L::OFF_BAR);
   uint64_t* done = reinterpret_cast<uint64_t*>(smem + L::OFF_DONE);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::OFF_MISC);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::OFF_MISC + 4);
 
   if (threadIdx.x == 0) {
-    mbar_init(&done[0], 1);
-    mbar_init(&done[1], 1);
-    for (int s = 0; s < 2; ++s) {
+    for (int s = 0; s < NS; ++s) mbar_init(&done[s], 1);
+    for (int s = 0; s < NS; ++s) {
       uint64_t* b = bars_all + s * L::NBAR_STREAM;
       for (int i = 0; i < 2; ++i) {
         mbar_init(&b[L::B_QF + i], 1);
@@ -140,7 +159,7 @@ __global__ void __launch_bounds__(384, 1)
   }
   // The ones rows after every V^T stage (never written by TMA), made visible
   // to the tensor core's (async proxy) reads before the first MMA.
-  for (int i = threadIdx.x; i < 2 * NST * (L::ONES_BYTES / 16); i += blockDim.x) {
+  for (int i = threadIdx.x; i < NS * NST * (L::ONES_BYTES / 16); i += blockDim.x) {
     const int s = i / (NST * (L::ONES_BYTES / 16));
     const int rem = i % (NST * (L::ONES_BYTES / 16));
     const int st = rem / (L::ONES_BYTES / 16), ch = rem % (L::ONES_BYTES / 16);
@@ -148,7 +167,7 @@ __global__ void __launch_bounds__(384, 1)
                  0x3c003c00u, 0x3c003c00u, 0x3c003c00u, 0x3c003c00u);
   }
   fence_proxy_async_smem();
-  if (warp == 10) {
+  if (warp == L::W_MMA) {
     tmem_alloc(tmem_slot, L::TMEM_COLS);
     tmem_relinquish();
   }
@@ -169,11 +188,11 @@ __global__ void __launch_bounds__(384, 1)
     return w;
   };
 
-  if (warp == 8 || warp == 9) {
-    // ------------------------------------------------------------ producer of stream warp-8
+  if (warp >= L::W_PROD && warp < L::W_MMA) {
+    // ------------------------------------------------------------ producer of stream warp - W_PROD
     asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(L::REGS_OTHER));
     if (lane == 0) {
-      const int s = warp - 8;
+      const int s = warp - L::W_PROD;
       uint64_t* b = bars_all + s * L::NBAR_STREAM;
       uint8_t* sb = smem + s * L::STREAM_BYTES;
       tma_prefetch_desc(&tmQ);
@@ -181,7 +200,7 @@ __global__ void __launch_bounds__(384, 1)
       tma_prefetch_desc(&tmV);
       int t = 0, it = 0;
       bool ok = true;
-      for (int w = first_item(2 * static_cast<int>(blockIdx.x) + s); ok && w < n_items;
+      for (int w = first_item(NS * static_cast<int>(blockIdx.x) + s); ok && w < n_items;
            w = first_item(w + G2)) {
         const AttnItem item = attn_item(p, w, n_qt);
         const int nt = n_tiles(item);
@@ -205,11 +224,14 @@ __global__ void __launch_bounds__(384, 1)
       for (int i = (t > NST ? t - NST : 0); i < t; ++i)
         wait_drain(&b[L::B_KF + i % NST], (i / NST) & 1, kDrainLimitNs);
     }
-  } else if (warp == 10 || warp == 11) {
-    // ------------------------------------------------------------ MMA issuer of stream warp-10
+  } else if (warp >= 6 * NS) {
+    // ------------------------------------------------------------ idle warps (whole warpgroups)
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(L::REGS_OTHER));
+  } else if (warp >= L::W_MMA) {
+    // ------------------------------------------------------------ MMA issuer of stream warp - W_MMA
     asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(L::REGS_OTHER));
     if (lane == 0) {
-      const int s = warp - 10;
+      const int s = warp - L::W_MMA;
       uint64_t* b = bars_all + s * L::NBAR_STREAM;
       const uint32_t sb = smem_u32(smem + s * L::STREAM_BYTES);
       const uint32_t tS = tmem_base + s * L::TMEM_STREAM;
@@ -218,14 +240,14 @@ __global__ void __launch_bounds__(384, 1)
       const uint32_t idesc_s = umma_idesc_f16_f32(BM, BN);
       const uint32_t idesc_o = umma_idesc_f16_f32(BM, L::ON);
       // S cursor: item w_s, tile j_s of n_s, stream tile u, item count it_s.
-      int w_s = first_item(2 * static_cast<int>(blockIdx.x) + s), j_s = 0, n_s = 0, u = 0, it_s = 0;
+      int w_s = first_item(NS * static_cast<int>(blockIdx.x) + s), j_s = 0, n_s = 0, u = 0, it_s = 0;
       if (w_s < n_items) n_s = n_tiles(attn_item(p, w_s, n_qt));
       auto issue_s = [&]() -> bool {
-        const int st = u % NST, qb = it_s & 1, bb = u & 1;
+        const int st = u % NST, qb = it_s & 1, bb = u % NSB;
         if (j_s == 0 && !wait_phase(&b[L::B_QF + qb], (it_s >> 1) & 1, wd, 0x231)) return false;
         if (!wait_phase(&b[L::B_KF + st], (u / NST) & 1, wd, 0x232)) return false;
-        // S buffer bb last held P_{u-2}, read by P.V of tile u - 2, which this
-        // thread issued before this MMA (same-thread MMAs execute in order).
+        // S buffer bb last held P_{u-NSB}, read by P.V of tile u - NSB, which
+        // this thread issued before this MMA (same-thread MMAs execute in order).
         tc_fence_after();
 #pragma unroll
         for (int kk = 0; kk < HD / 16; ++kk) {
@@ -245,14 +267,14 @@ __global__ void __launch_bounds__(384, 1)
         return true;
       };
       // P.V cursor: items it_o (O buffer it_o & 1), tile j_o of n_o.
-      int w_o = first_item(2 * static_cast<int>(blockIdx.x) + s), j_o = 0, it_o = 0;
+      int w_o = first_item(NS * static_cast<int>(blockIdx.x) + s), j_o = 0, it_o = 0;
       int n_o = w_o < n_items ? n_tiles(attn_item(p, w_o, n_qt)) : 0;
       bool ok = true;
-      // Scores of the first two tiles, then per tile t: P.V_t, then S_{t+2}.
-      for (int k = 0; ok && k < 2 && w_s < n_items; ++k) ok = issue_s();
+      // Scores of the first NSB tiles, then per tile t: P.V_t, then S_{t+NSB}.
+      for (int k = 0; ok && k < NSB && w_s < n_items; ++k) ok = issue_s();
       for (int t = 0; ok && t < u; ++t) {
-        const int bb = t & 1, st = t % NST, ob = it_o & 1;
-        if (!(ok = wait_phase(&b[L::B_PF + bb], (t >> 1) & 1, wd, 0x234))) break;
+        const int bb = t % NSB, st = t % NST, ob = it_o & 1;
+        if (!(ok = wait_phase(&b[L::B_PF + bb], (t / NSB) & 1, wd, 0x234))) break;
         if (j_o == 0 && !(ok = wait_phase(&b[L::B_OR + ob], ((it_o >> 1) & 1) ^ 1, wd, 0x235))) break;
         tc_fence_after();
         const uint32_t tO = tS + L::TMEM_O + ob * L::ON;
@@ -271,7 +293,7 @@ __global__ void __launch_bounds__(384, 1)
           w_o = first_item(w_o + G2);
           n_o = w_o < n_items ? n_tiles(attn_item(p, w_o, n_qt)) : 0;
         }
-        if (w_s < n_items) ok = issue_s();  // S_{t+2} into buffer bb
+        if (w_s < n_items) ok = issue_s();  // S_{t+NSB} into buffer bb
       }
       // All MMAs this thread issued must finish before TMEM is released.
       umma_commit(&done[s]);
@@ -281,7 +303,7 @@ __global__ void __launch_bounds__(384, 1)
     // ------------------------------------------------------------ softmax
     asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(L::REGS_SOFTMAX));
     const int s = warp >> 2;  // stream
-    const int q = warp & 3;   // TMEM lane quadrant
+    const int q = warp & 3;   // TMEM lane quadrant (warp % 4)
     const int row = q * 32 + lane;
     uint64_t* b = bars_all + s * L::NBAR_STREAM;
     const uint32_t tS = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + s * L::TMEM_STREAM;
@@ -330,7 +352,7 @@ __global__ void __launch_bounds__(384, 1)
       return true;
     };
 
-    for (int w = 2 * static_cast<int>(blockIdx.x) + s; ok && w < n_items; w += G2) {
+    for (int w = NS * static_cast<int>(blockIdx.x) + s; ok && w < n_items; w += G2) {
       const AttnItem item = attn_item(p, w, n_qt);
       const int qi = item.q0 + row;
       __half* dst_row = p.ctx + (static_cast<size_t>(item.b) * p.seq + qi) * D + item.h * HD;
@@ -348,7 +370,7 @@ __global__ void __launch_bounds__(384, 1)
       float m_run = -INFINITY;  // reference maximum of this row (log2 units)
 
       for (int j = 0; j < nt; ++j, ++t) {
-        const int bb = t & 1;
+        const int bb = t % NSB;
         const int k0 = j * BN;
         uint32_t vb[2] = {~0u, ~0u};
         bool mask_partial = false;
@@ -365,7 +387,7 @@ __global__ void __launch_bounds__(384, 1)
         const bool need_mask = __any_sync(0xffffffffu, mask_partial || (k0 + BN > row_lim));
         const int lim = row_lim - k0;
 
-        if (!(ok = warp_wait_phase(&b[L::B_SF + bb], (t >> 1) & 1, wd, 0x331))) break;
+        if (!(ok = warp_wait_phase(&b[L::B_SF + bb], (t / NSB) & 1, wd, 0x331))) break;
         tc_fence_after();
         uint32_t sc[2][32];
         tmem_ld_x32(tS + bb * BN, sc[0]);
@@ -410,7 +432,7 @@ __global__ void __launch_bounds__(384, 1)
         if (__any_sync(0xffffffffu, resc)) {
           // O must hold every earlier tile: wait for P.V of tile t-1 (j > 0 here).
           const int tp = t - 1;
-          if (!(ok = warp_wait_phase(&b[L::B_PE + (tp & 1)], (tp >> 1) & 1, wd, 0x332))) break;
+          if (!(ok = warp_wait_phase(&b[L::B_PE + (tp % NSB)], (tp / NSB) & 1, wd, 0x332))) break;
           tc_fence_after();
           const float corr = resc ? ex2_approx(m_run - m_new) : 1.f;
 #pragma unroll 1
@@ -429,10 +451,9 @@ __global__ void __launch_bounds__(384, 1)
         // comes from the P.[V | 1] MMA).  P.V of tile t-2, the last reader of
         // this buffer, finished before S_t was computed into it.
         const uint64_t negm = f2_pack(-m_use, -m_use);
-        uint32_t pk_all[32];
 #pragma unroll
         for (int g = 0; g < 2; ++g) {
-          uint32_t* pk = pk_all + 16 * g;
+          uint32_t pk[16];
 #pragma unroll
           for (int e = 0; e < 16; ++e) {
             const uint64_t xx =
@@ -450,8 +471,8 @@ __global__ void __launch_bounds__(384, 1)
               pk[e] = pack_half2(f2_lo(pp), f2_hi(pp));
             }
           }
+          tmem_st_x16(tS + bb * BN + 16 * g, pk);
         }
-        tmem_st_x32(tS + bb * BN, pk_all);
         tmem_st_wait();
         tc_fence_before();
         __syncwarp();
@@ -473,7 +494,7 @@ __global__ void __launch_bounds__(384, 1)
 
   tc_fence_before();
   __syncthreads();
-  if (warp == 10) {
+  if (warp == L::W_MMA) {
     tc_fence_after();
     tmem_dealloc(tmem_base, L::TMEM_COLS);
   }

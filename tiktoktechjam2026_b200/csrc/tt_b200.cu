@@ -484,7 +484,7 @@ int launch_attention(const CUtensorMap& tq, const CUtensorMap& tk, const CUtenso
     if (fa.numRegs != AttnDbLayout<32>::REGS_LAUNCH)
       return fail(TT_ERR_UNSUPPORTED, "attention kernel built with %d registers per thread, expected %d",
                   fa.numRegs, AttnDbLayout<32>::REGS_LAUNCH);
-    const int ctas = (n_items + 1) / 2;
+    const int ctas = (n_items + AttnDbLayout<32>::NS - 1) / AttnDbLayout<32>::NS;
     const unsigned grid2 = static_cast<unsigned>(ctas < sm_count ? ctas : sm_count);
     kern<<<grid2, AttnDbLayout<32>::THREADS, smem, stream>>>(tq, tk, tv, ap, n_items);
     (void)grid;
