@@ -57,9 +57,19 @@ WORKLOADS = {
 METRIC = "sequences/sec (forward, FP32 in/out)"
 UNIT = "seq/s"
 SEED = 1234 + 100000  # the reference's timing-input seed (torch_transformer_benchmark.py:747)
-KERNEL_KIND_LABEL = {"attn": "attn_fwd_kernel", "qkv": "gemm_kernel<EPI_QKV>", "out_ln": "gemm_kernel<EPI_RESID_LN>",
+KERNEL_KIND_LABEL = {"qkv": "gemm_kernel<EPI_QKV>", "out_ln": "gemm_kernel<EPI_RESID_LN>",
                      "ffn_in": "gemm_kernel<EPI_GELU>", "ffn_out_ln": "gemm_kernel<EPI_RESID_LN>",
-                     "ln0": "layernorm_rows_kernel", "mask": "mask_kv_end_kernel", "ffn_fused": "ffn_fused_kernel"}
+                     "ln0": "layernorm_rows_kernel", "mask": "mask_kv_end_kernel"}
+
+
+def kernel_label(kind, cfg):
+    """Name of the kernel a kind of launch runs for this shape (the library's dispatch)."""
+    hd = cfg["d_model"] // cfg["heads"]
+    if kind == "attn":
+        return f"attn_db_fwd_kernel<{hd}>" if hd in (16, 32) else f"attn_fwd_kernel<{hd}>"
+    if kind == "ffn_fused":
+        return f"ffn2_kernel<{cfg['d_model']}>" if cfg["d_model"] in (128, 256) else f"ffn_fused_kernel<{cfg['d_model']}>"
+    return KERNEL_KIND_LABEL.get(kind, kind)
 
 
 def parse_args():
@@ -377,7 +387,7 @@ def main() -> int:
         roof = {"bound": "hbm", "achieved": nbytes / per_launch_s / 1e9, "peak": hbm_peak, "unit": "GB/s"}
     roof["frac"] = roof["achieved"] / roof["peak"]
     roof["traffic"] = load_traffic(workload_name, nb, kind)
-    roof["kernel"] = KERNEL_KIND_LABEL.get(kind, kind)
+    roof["kernel"] = kernel_label(kind, cfg)
     roof["mean_launch_us"] = per_launch_s * 1e6
     roof["algorithmic_per_launch"] = {"flops": flops, "bytes": nbytes}
     roof["peak_source"] = f"{peak_src} ({'bf16_tflops burst' if roof['bound'] == 'tensor' else 'hbm_gbs'})"
