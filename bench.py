@@ -83,6 +83,8 @@ def parse_args():
     ap.add_argument("--cpu-sample-seconds", type=float, default=12.0)
     ap.add_argument("--chunk", type=int, default=None,
                     help="sequences per chunk of the host-buffer pipeline (e2e); default: up to 8 chunks")
+    ap.add_argument("--graph", action="store_true",
+                    help="time replays of one captured CUDA graph of the forward (small workloads)")
     ap.add_argument("--batch", type=int, default=None,
                     help="override the workload's global batch (smaller profiling cases)")
     return ap.parse_args()
@@ -334,8 +336,21 @@ def main() -> int:
         barrier()
 
         # ---------------- value: device-resident inputs ----------------
-        model.set_profiling(True, dev)
-        model.profile_collect(dev)
+        # --graph replays one captured forward per step (tt_model_graph_create);
+        # the per-kernel breakdown then comes from a separate profiled eager pass.
+        graphed = None
+        kernels_per_forward = 0
+        if args.graph:
+            l0 = _lib.lib().tt_launch_count()
+            model(x_dev, mask_dev)
+            kernels_per_forward = _lib.lib().tt_launch_count() - l0
+            graphed = model.capture_graph(x_dev, mask_dev)
+            for _ in range(3):
+                graphed()
+            barrier()
+        else:
+            model.set_profiling(True, dev)
+            model.profile_collect(dev)
         starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
         ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
         sampler = ClockSampler() if rank == 0 else None
@@ -346,11 +361,21 @@ def main() -> int:
         for i in range(args.steps):
             flush.zero_()
             starts[i].record(stream)
-            model(x_dev, mask_dev)
+            if graphed is not None:
+                graphed()
+            else:
+                model(x_dev, mask_dev)
             ends[i].record(stream)
         barrier()
-        launches = _lib.lib().tt_launch_count() - launches0
+        launches = _lib.lib().tt_launch_count() - launches0 + kernels_per_forward * args.steps
         step_ms = [a.elapsed_time(b) for a, b in zip(starts, ends)]
+        if graphed is not None:
+            model.set_profiling(True, dev)
+            model.profile_collect(dev)
+            for _ in range(args.steps):
+                flush.zero_()
+                model(x_dev, mask_dev)
+            barrier()
         prof = model.profile_collect(dev)
         model.set_profiling(False, dev)
         total_ms = max_over_ranks(sum(step_ms))
@@ -406,7 +431,8 @@ def main() -> int:
                                    f"layers {L}, causal{', key padding' if pad > 0 else ''}",
                        "global_batch": B, "per_gpu_batch": nb, "seq_len": S, "d_model": D, "heads": H, "ffn": F,
                        "layers": L, "parallelism": f"batch-sharded x{world}, no collective in the data path",
-                       "l2": "flushed between timed steps (256 MiB write, untimed)"},
+                       "l2": "flushed between timed steps (256 MiB write, untimed)",
+                       "launch": "one CUDA graph replay per step" if args.graph else "eager (one host call per step)"},
             "e2e": {"value": e2e_value, "unit": UNIT, "ms_per_step": e2e_ms / args.steps, "chunk": chunk,
                     "path": "model.forward_host -> tt_model_forward_host (pinned host in/out, copies overlapped "
                             "with compute by chunks)",

@@ -221,6 +221,21 @@ int tt_model_host_workspace_bytes(const tt_model* model, int chunk, int seq, siz
 int tt_model_forward_host(tt_model* model, const float* x, const uint8_t* mask, float* out, int batch,
                           int seq, int chunk, void* workspace, size_t workspace_bytes, void* stream);
 
+/* One forward captured as a CUDA graph: the pointers, shapes and tile
+ * configuration of this call are baked in (the caller keeps x, mask, out and
+ * the workspace alive and at the same addresses, and writes new inputs into x
+ * before each replay).  Replaying removes the per-kernel launch gaps that
+ * dominate small workloads.  Capture happens on a private stream; the model
+ * handle stays usable for ordinary calls.  Replaces the reference runner's
+ * torch.compile(mode="reduce-overhead") graph capture of the forward
+ * (mixed_precision_benchmark.py:86-90). */
+typedef struct tt_graph tt_graph;
+int tt_model_graph_create(tt_model* model, const float* x, const uint8_t* mask, float* out, int batch, int seq,
+                          void* workspace, size_t workspace_bytes, tt_graph** graph);
+/* Enqueues one replay of the captured forward on `stream`. */
+int tt_graph_launch(tt_graph* graph, void* stream);
+void tt_graph_destroy(tt_graph* graph);
+
 /* Kernel kinds reported by tt_model_profile_collect. */
 #define TT_KERNEL_LN0 0
 #define TT_KERNEL_MASK 1

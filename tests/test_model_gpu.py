@@ -199,3 +199,38 @@ def test_host_pipeline_rejects_pageable_memory(tt_lib):
     rc = tt_lib.tt_model_forward_host(plan.handle, out.data_ptr(), None, out.data_ptr(), 2, cfg.seq_len, 2, ws,
                                       4096, stream)
     assert rc == _lib.TT_ERR_WORKSPACE
+
+
+def test_graph_replay_equals_eager(tt_lib):
+    """A captured forward replays to the eager forward's bits, and follows new data written into its input."""
+    cfg, _ = oracle.CONFIGS["C1"]
+    sd = oracle.seeded_state_dict(cfg)
+    model = build_model(cfg, sd)
+    model.assume_all_tokens_valid = True
+    x1, _ = oracle.generate_case(cfg, 21)
+    x2, _ = oracle.generate_case(cfg, 22)
+    with torch.inference_mode():
+        ref1 = model(x1.to(DEV))
+        ref2 = model(x2.to(DEV))
+        g = model.capture_graph(x1.to(DEV).clone())
+        a = g().clone()
+        g.x.copy_(x2.to(DEV))
+        b = g().clone()
+        c = model(x1.to(DEV))  # the model still runs ordinary calls after a capture
+        torch.cuda.synchronize()
+    assert torch.equal(a, ref1) and torch.equal(b, ref2) and torch.equal(c, ref1)
+    g.close()
+
+
+def test_graph_replay_with_mask(tt_lib, strict_fp32):
+    cfg = oracle.Config(3, 130, 128, 4, 128, 2, True)
+    sd = oracle.seeded_state_dict(cfg, 8)
+    model = build_model(cfg, sd)
+    x, mask = oracle.generate_case(cfg, 9, padding_ratio=0.5)
+    with torch.inference_mode():
+        eager = model(x.to(DEV), mask.to(DEV))
+        g = model.capture_graph(x.to(DEV).clone(), mask.to(DEV))
+        got = g().clone()
+        torch.cuda.synchronize()
+    assert torch.equal(got, eager)
+    assert torch.all(got[~mask.to(DEV)] == 0)

@@ -113,6 +113,12 @@ SIGNATURES = {
         c_int,
         [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_void_p, c_size_t, c_void_p],
     ),
+    "tt_model_graph_create": (
+        c_int,
+        [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_void_p, c_size_t, POINTER(c_void_p)],
+    ),
+    "tt_graph_launch": (c_int, [c_void_p, c_void_p]),
+    "tt_graph_destroy": (None, [c_void_p]),
     "tt_model_set_profiling": (c_int, [c_void_p, c_int]),
     "tt_model_profile_collect": (c_int, [c_void_p, POINTER(c_float), POINTER(c_int), c_int]),
 }

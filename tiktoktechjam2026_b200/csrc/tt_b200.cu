@@ -1432,6 +1432,55 @@ int tt_model_forward_host(tt_model* m, const float* x, const uint8_t* mask, floa
   return check_cuda(cudaStreamWaitEvent(s, m->ev_out[(n - 1) & 1], 0), "cudaStreamWaitEvent");
 }
 
+struct tt_graph {
+  cudaGraph_t graph = nullptr;
+  cudaGraphExec_t exec = nullptr;
+  int device = -1;
+};
+
+int tt_model_graph_create(tt_model* m, const float* x, const uint8_t* mask, float* out, int batch, int seq,
+                          void* workspace, size_t workspace_bytes, tt_graph** graph) {
+  if (!m || !graph) return fail(TT_ERR_ARG, "null argument");
+  *graph = nullptr;
+  if (m->profiling) return fail(TT_ERR_ARG, "disable profiling before capturing a graph");
+  int dev = -1;
+  if (int rc = check_cuda(cudaGetDevice(&dev), "cudaGetDevice")) return rc;
+  if (dev != m->device)
+    return fail(TT_ERR_ARG, "model was created on device %d but device %d is current", m->device, dev);
+  // Capture on a private stream in relaxed mode: every launch also sets its
+  // kernel's shared-memory attribute, which is not a stream operation.
+  cudaStream_t cs = nullptr;
+  if (int rc = check_cuda(cudaStreamCreateWithFlags(&cs, cudaStreamNonBlocking), "cudaStreamCreate")) return rc;
+  tt_graph* g = new tt_graph();
+  g->device = dev;
+  int rc = check_cuda(cudaStreamBeginCapture(cs, cudaStreamCaptureModeRelaxed), "cudaStreamBeginCapture");
+  if (rc == TT_OK) {
+    const int frc = tt_model_forward(m, x, mask, out, batch, seq, workspace, workspace_bytes, cs);
+    const int erc = check_cuda(cudaStreamEndCapture(cs, &g->graph), "cudaStreamEndCapture");
+    rc = frc != TT_OK ? frc : erc;
+  }
+  if (rc == TT_OK) rc = check_cuda(cudaGraphInstantiate(&g->exec, g->graph, 0), "cudaGraphInstantiate");
+  cudaStreamDestroy(cs);
+  if (rc != TT_OK) {
+    tt_graph_destroy(g);
+    return rc;
+  }
+  *graph = g;
+  return TT_OK;
+}
+
+int tt_graph_launch(tt_graph* g, void* stream) {
+  if (!g || !g->exec) return fail(TT_ERR_ARG, "null graph");
+  return check_cuda(cudaGraphLaunch(g->exec, static_cast<cudaStream_t>(stream)), "cudaGraphLaunch");
+}
+
+void tt_graph_destroy(tt_graph* g) {
+  if (!g) return;
+  if (g->exec) cudaGraphExecDestroy(g->exec);
+  if (g->graph) cudaGraphDestroy(g->graph);
+  delete g;
+}
+
 int tt_model_set_profiling(tt_model* m, int enable) {
   if (!m) return fail(TT_ERR_ARG, "null model");
   m->profiling = enable != 0;

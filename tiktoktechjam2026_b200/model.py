@@ -380,6 +380,66 @@ class B200Transformer(nn.Module):
         return out
 
 
+    def capture_graph(self, x: torch.Tensor, valid_token_mask: Optional[torch.Tensor] = None) -> "GraphedForward":
+        """Captures one forward over ``x`` as a CUDA graph (``tt_model_graph_create``).
+
+        Returns a callable that replays it: write new inputs into
+        ``graphed.x`` (same shape), call ``graphed()``, read ``graphed.out``.
+        The graph owns its workspace and output; the model stays usable for
+        ordinary calls.
+        """
+        if x.dtype != torch.float32 or not x.is_cuda or x.dim() != 3 or x.shape[-1] != self.config.d_model:
+            raise ValueError("capture_graph takes an FP32 CUDA tensor [B, S, d_model]")
+        return GraphedForward(self, x, None if self.assume_all_tokens_valid else valid_token_mask)
+
+
+class GraphedForward:
+    """A captured forward: static input ``x``, static output ``out``, one graph replay per call."""
+
+    def __init__(self, model: B200Transformer, x: torch.Tensor, mask: Optional[torch.Tensor]) -> None:
+        B, S, _ = x.shape
+        self.x = x.contiguous()
+        self.out = torch.empty_like(self.x)
+        self.mask = None
+        mask_ptr = 0
+        if mask is not None:
+            if mask.shape != (B, S):
+                raise ValueError(f"valid_token_mask must have shape {(B, S)}, got {tuple(mask.shape)}")
+            self.mask = mask.to(device=x.device, dtype=torch.bool).contiguous().view(torch.uint8)
+            mask_ptr = self.mask.data_ptr()
+        self.device = x.device
+        self._plan = model._plan(x.device)
+        nbytes = ctypes.c_size_t()
+        _lib.check(_lib.lib().tt_model_workspace_bytes(self._plan.handle, B, S, ctypes.byref(nbytes)))
+        raw = torch.empty(int(nbytes.value) + 1024, dtype=torch.uint8, device=x.device)
+        self._ws = raw
+        ws_ptr = (raw.data_ptr() + 1023) // 1024 * 1024
+        handle = ctypes.c_void_p()
+        with torch.cuda.device(x.device):
+            torch.cuda.current_stream(x.device).synchronize()
+            _lib.check(_lib.lib().tt_model_graph_create(
+                self._plan.handle, self.x.data_ptr(), mask_ptr, self.out.data_ptr(), B, S, ws_ptr,
+                int(nbytes.value), ctypes.byref(handle)))
+        self._handle = handle
+
+    def __call__(self) -> torch.Tensor:
+        with torch.cuda.device(self.device):
+            stream = torch.cuda.current_stream(self.device).cuda_stream
+            _lib.check(_lib.lib().tt_graph_launch(self._handle, stream))
+        return self.out
+
+    def close(self) -> None:
+        if getattr(self, "_handle", None) is not None and self._handle.value:
+            try:
+                _lib.lib().tt_graph_destroy(self._handle)
+            except Exception:  # pragma: no cover - interpreter teardown
+                pass
+            self._handle = ctypes.c_void_p()
+
+    def __del__(self) -> None:  # pragma: no cover
+        self.close()
+
+
 def default_host_chunk(batch: int, seq: int, d_model: int) -> int:
     """Sequences per chunk of the host pipeline: up to 8 chunks of at least 8 MiB of input each."""
     total = batch * seq * d_model * 4
