@@ -50,7 +50,13 @@ struct Ffn2Maps {
 
 template <int D>
 struct Ffn2Layout {
-  static constexpr int FC = 128, KB = 64, NST = 4, SLOT = 32768;
+#ifndef TT_FFN2_NST
+#define TT_FFN2_NST 3
+#endif
+#ifndef TT_FFN2_AHEAD
+#define TT_FFN2_AHEAD 6
+#endif
+  static constexpr int FC = 128, KB = 64, NST = TT_FFN2_NST, SLOT = 32768;
   static constexpr int NKA = D / KB;                 // K-blocks of G1
   static constexpr int A_KBLK = 128 * KB * 2;        // 16 KB
   static constexpr int A_BYTES = NKA * A_KBLK;
@@ -62,7 +68,8 @@ struct Ffn2Layout {
   static constexpr int W2_SLOTS = (FC / KB) / W2_PER_SLOT;
   static constexpr int W2_BOX_ROWS = D < 256 ? D : 256;
   static constexpr int JW = 16;       // columns per epilogue job
-  static constexpr int RING = 3;      // 32 x JW FP32 staging tiles per epilogue warp
+  static constexpr int AHEAD = TT_FFN2_AHEAD;  // epilogue jobs in flight ahead of the one consumed
+  static constexpr int RING = AHEAD + 1;      // 32 x JW FP32 staging tiles per epilogue warp
   static constexpr int TILE = 32 * JW * 4;
   static constexpr int OFF_A = 0;
   static constexpr int OFF_W = OFF_A + A_BYTES;
@@ -81,6 +88,7 @@ struct Ffn2Layout {
   static_assert(NACC2 * D <= TMEM_ACC1, "TMEM budget");
   static_assert(OFF_W % 1024 == 0 && OFF_LN % 1024 == 0 && OFF_F32 % 16 == 0, "alignment");
   static_assert(SMEM_ALLOC <= 232448, "shared memory budget");
+  static_assert(D / JW > AHEAD, "the re-read of an r' chunk must be issued after that chunk's store");
 };
 
 // Warp roles: 0..7 GELU (lane quadrant w & 3, hidden half w >> 2 of each
@@ -330,7 +338,9 @@ __global__ void __launch_bounds__(kFfn2Threads, 1)
     // Job j of a tile: j < nch reads the residual input columns [j*JW, +JW),
     // j >= nch reads back this warp's own r' columns of job j - nch.  Jobs run
     // in one sequence across tiles (number jg = 2 * nch * tile_count + j) and
-    // job jg stages in slot jg % RING, two jobs ahead of the one consumed.
+    // job jg stages in slot jg % RING, AHEAD jobs ahead of the one consumed
+    // (the residual rows were bulk-prefetched into L2 a tile earlier, so the
+    // loads wait on L2 latency; AHEAD covers it).
     auto sw = [](int r, int k) { return r * RB + ((k ^ ((r >> 1) & 3)) << 4); };
     auto issue = [&](int tile, int j, int jg) {
       const int r0 = tile * 128 + ew * 32;
@@ -377,10 +387,10 @@ __global__ void __launch_bounds__(kFfn2Threads, 1)
     bool ok = true;
     int w = blockIdx.x;
     if (w < p.n_items) {
-      issue(w, 0, 0);
-      cp_async_commit();
-      issue(w, 1, 1);
-      cp_async_commit();
+      for (int j = 0; j < L::AHEAD; ++j) {
+        issue(w, j, j);  // 2 * nch >= AHEAD: these all belong to the first tile
+        cp_async_commit();
+      }
     }
     for (; ok && w < p.n_items; w += gridDim.x, ++i) {
       const int ib = i % L::NACC2;
@@ -393,13 +403,13 @@ __global__ void __launch_bounds__(kFfn2Threads, 1)
       // Issue job j + 2 (the next tile's first jobs at the end), then wait for
       // job j; returns job j's staging slot.
       auto advance = [&](int j) -> uint32_t {
-        const int jn = j + 2;
+        const int jn = j + L::AHEAD;
         if (jn < 2 * nch)
           issue(w, jn, jbase + jn);
         else if (wn < p.n_items)
           issue(wn, jn - 2 * nch, jbase + jn);
         cp_async_commit();
-        cp_async_wait<2>();
+        cp_async_wait<L::AHEAD>();
         __syncwarp();
         return ring + ((jbase + j) % L::RING) * L::TILE;
       };
