@@ -209,7 +209,8 @@ int tt_model_forward(tt_model* model, const float* x, const uint8_t* mask, float
 int tt_model_host_workspace_bytes(const tt_model* model, int chunk, int seq, size_t* bytes);
 
 /* tt_model_forward over page-locked HOST buffers x, out ([B, S, D] FP32) and
- * mask ([B, S] bytes or NULL), pipelined by chunks of `chunk` sequences: the
+ * mask ([B, S] bytes or NULL), pipelined by chunks of `chunk` sequences (the
+ * first chunk a quarter of that, to shorten the pipeline's fill): the
  * copy-in of chunk i+1 and the copy-out of chunk i-1 run on the model's own
  * copy streams while chunk i computes on `stream`.  The work starts after the
  * caller's earlier work on `stream`, and `stream` completes only after the

@@ -152,7 +152,7 @@ def test_sequences_independent_of_batch(tt_lib):
     assert torch.equal(full[10:14], part)
 
 
-@pytest.mark.parametrize("chunk", [None, 1, 3, 64])
+@pytest.mark.parametrize("chunk", [None, 1, 3, 4, 8, 64])
 def test_host_pipeline_equals_device_forward(tt_lib, chunk):
     """forward_host (pinned host buffers, copies overlapped by chunks) gives the device path's bits,
     including a ragged last chunk and a chunk larger than the batch."""

@@ -1395,11 +1395,17 @@ int tt_model_forward_host(tt_model* m, const float* x, const uint8_t* mask, floa
   if (int rc = check_cuda(cudaEventRecord(m->ev_entry, s), "cudaEventRecord")) return rc;
   cudaStreamWaitEvent(m->h2d, m->ev_entry, 0);
   cudaStreamWaitEvent(m->d2h, m->ev_entry, 0);
-  const int n = (batch + chunk - 1) / chunk;
+  // The first chunk is a quarter of the others: until its copy-in and its
+  // kernels are done nothing else can overlap, so a small one shortens the
+  // pipeline's fill; after it the copies and the kernels run side by side.
+  const int first = (batch > chunk && chunk >= 4) ? chunk / 4 : chunk;
+  const int n = 1 + (batch - first + chunk - 1) / chunk;
   for (int i = 0; i < n; ++i) {
     const int b = i & 1;
-    const int c0 = i * chunk;
-    const int nb = batch - c0 < chunk ? batch - c0 : chunk;
+    const int c0 = i == 0 ? 0 : first + (i - 1) * chunk;
+    const int want = i == 0 ? first : chunk;
+    const int nb = batch - c0 < want ? batch - c0 : want;
+    if (nb <= 0) break;
     const size_t rows0 = static_cast<size_t>(c0) * seq, rows = static_cast<size_t>(nb) * seq;
     float* xd = reinterpret_cast<float*>(base + h.x[b]);
     float* od = reinterpret_cast<float*>(base + h.out[b]);
