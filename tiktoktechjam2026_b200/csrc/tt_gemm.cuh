@@ -359,6 +359,12 @@ __global__ void __launch_bounds__(gemm_threads(EPI), 1)
 
       if constexpr (EPI == EPI_QKV) {
         const int D = p.d_model, hd = p.head_dim;
+        // head_dim is 16, 32 or 64: heads and features by shift and mask; the
+        // Q/K/V part of a column by one division per item (chunks of 32 never
+        // straddle a part, D % 32 == 0).
+        const int lg_hd = __ffs(hd) - 1;
+        const int which_item = n0 / D;
+        const int within_item = n0 - which_item * D;
         const int bidx = valid ? row / p.seq : 0;
         const int s = valid ? row - bidx * p.seq : 0;
         const int b_w = warp_active ? r0 / p.seq : 0;
@@ -388,8 +394,11 @@ __global__ void __launch_bounds__(gemm_threads(EPI), 1)
             f[4 * e + 2] = __uint_as_float(v[4 * e + 2]) + bb.z;
             f[4 * e + 3] = __uint_as_float(v[4 * e + 3]) + bb.w;
           }
-          const int which = col0 / D;
-          const int within0 = col0 - which * D;
+          int which = which_item, within0 = within_item + c * 32;
+          while (within0 >= D) {
+            within0 -= D;
+            ++which;
+          }
           if (which < 2) {
             // Q / K: a thread's 32 values are consecutive features of its row, in runs of
             // 16 that are each 32 contiguous bytes of [B*H, S, hd].
@@ -398,7 +407,7 @@ __global__ void __launch_bounds__(gemm_threads(EPI), 1)
 #pragma unroll
               for (int gq = 0; gq < 2; ++gq) {
                 const int within = within0 + 16 * gq;
-                const int hh = within / hd, d = within - hh * hd;
+                const int hh = within >> lg_hd, d = within & (hd - 1);
                 uint4* dst = reinterpret_cast<uint4*>(
                     base + ((static_cast<size_t>(bidx) * p.heads + hh) * p.seq + s) * hd + d);
                 uint4 a, bq;
@@ -431,7 +440,7 @@ __global__ void __launch_bounds__(gemm_threads(EPI), 1)
 #pragma unroll 1
             for (int sb = 0; sb < 32 / wbox; ++sb) {
               const int within = within0 + sb * wbox;
-              const int hh = within / hd, d0 = within - hh * hd;
+              const int hh = within >> lg_hd, d0 = within & (hd - 1);
               const size_t bh = static_cast<size_t>(b_w) * p.heads + hh;
               for (int k = 0; k < wbox / 8; ++k) {
                 const int d = k * 8 + (lane >> 2), pc = lane & 3;
@@ -443,7 +452,7 @@ __global__ void __launch_bounds__(gemm_threads(EPI), 1)
 #pragma unroll
             for (int e = 0; e < 32; ++e) {
               const int within = within0 + e;
-              const int hh = within / hd, d = within - hh * hd;
+              const int hh = within >> lg_hd, d = within & (hd - 1);
               p.vt[((static_cast<size_t>(bidx) * p.heads + hh) * hd + d) * p.seq_pad + s] =
                   __float2half_rn(f[e]);
             }
