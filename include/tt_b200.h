@@ -222,6 +222,14 @@ int tt_model_host_workspace_bytes(const tt_model* model, int chunk, int seq, siz
 int tt_model_forward_host(tt_model* model, const float* x, const uint8_t* mask, float* out, int batch,
                           int seq, int chunk, void* workspace, size_t workspace_bytes, void* stream);
 
+/* tt_model_forward_host over an explicit schedule: chunk i holds
+ * chunk_sizes[i] consecutive sequences (every size positive, the sizes adding
+ * up to batch).  The workspace is sized by tt_model_host_workspace_bytes for
+ * the largest chunk.  Same ordering and results as tt_model_forward_host. */
+int tt_model_forward_host_chunks(tt_model* model, const float* x, const uint8_t* mask, float* out, int batch,
+                                 int seq, const int* chunk_sizes, int n_chunks, void* workspace,
+                                 size_t workspace_bytes, void* stream);
+
 /* One forward captured as a CUDA graph: the pointers, shapes and tile
  * configuration of this call are baked in (the caller keeps x, mask, out and
  * the workspace alive and at the same addresses, and writes new inputs into x

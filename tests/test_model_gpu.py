@@ -171,6 +171,40 @@ def test_host_pipeline_equals_device_forward(tt_lib, chunk):
     assert torch.equal(again, ref)
 
 
+@pytest.mark.parametrize("chunks", [[10], [1, 9], [2, 3, 1, 4], [1] * 10, [4, 4, 2]])
+def test_host_pipeline_explicit_schedule(tt_lib, chunks):
+    """forward_host over an explicit chunk schedule (tt_model_forward_host_chunks) gives the device path's bits."""
+    cfg, _ = oracle.CONFIGS["C1"]
+    sd = oracle.seeded_state_dict(cfg)
+    model = build_model(cfg, sd)
+    x, mask = oracle.generate_case(cfg, 12, padding_ratio=0.3)
+    x, mask = x[:10].contiguous(), mask[:10].contiguous()
+    with torch.inference_mode():
+        ref = model(x.to(DEV), mask.to(DEV)).cpu()
+        got = model.forward_host(x.pin_memory(), mask.pin_memory(), chunks=chunks)
+    assert torch.equal(got, ref)
+
+
+def test_host_pipeline_schedule_rejects_bad_sizes(tt_lib):
+    cfg, _ = oracle.CONFIGS["C1"]
+    model = build_model(cfg, oracle.seeded_state_dict(cfg))
+    plan = model._plan(DEV)
+    x = torch.zeros(4, cfg.seq_len, cfg.d_model).pin_memory()
+    out = torch.zeros_like(x).pin_memory()
+    ws, ws_bytes = plan.host_workspace(4, cfg.seq_len)
+    stream = torch.cuda.current_stream(DEV).cuda_stream
+    for sizes in ([1, 2], [2, 0, 2], [4, 1], [-1, 5]):
+        arr = (ctypes.c_int * len(sizes))(*sizes)
+        rc = tt_lib.tt_model_forward_host_chunks(plan.handle, x.data_ptr(), None, out.data_ptr(), 4, cfg.seq_len,
+                                                 arr, len(sizes), ws, ws_bytes, stream)
+        assert rc == _lib.TT_ERR_SHAPE, sizes
+    rc = tt_lib.tt_model_forward_host_chunks(plan.handle, x.data_ptr(), None, out.data_ptr(), 4, cfg.seq_len,
+                                             None, 0, ws, ws_bytes, stream)
+    assert rc == _lib.TT_ERR_ARG
+    with pytest.raises(ValueError):
+        model.forward_host(x, chunks=[3])
+
+
 def test_host_pipeline_with_mask(tt_lib, strict_fp32):
     cfg = oracle.Config(6, 300, 256, 8, 512, 2, True)
     sd = oracle.seeded_state_dict(cfg, 3)

@@ -113,6 +113,11 @@ SIGNATURES = {
         c_int,
         [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_void_p, c_size_t, c_void_p],
     ),
+    "tt_model_forward_host_chunks": (
+        c_int,
+        [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, POINTER(c_int), c_int, c_void_p, c_size_t,
+         c_void_p],
+    ),
     "tt_model_graph_create": (
         c_int,
         [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_void_p, c_size_t, POINTER(c_void_p)],

@@ -1372,12 +1372,13 @@ int tt_model_host_workspace_bytes(const tt_model* m, int chunk, int seq, size_t*
   return TT_OK;
 }
 
-int tt_model_forward_host(tt_model* m, const float* x, const uint8_t* mask, float* out, int batch, int seq,
-                          int chunk, void* workspace, size_t workspace_bytes, void* stream) {
-  if (!m || !x || !out || !workspace) return fail(TT_ERR_ARG, "null argument");
-  if (batch <= 0 || seq <= 0 || chunk <= 0) return fail(TT_ERR_SHAPE, "invalid batch/seq/chunk");
-  if (chunk > batch) chunk = batch;
-  const HostWsLayout h = host_ws_layout(m, chunk, seq);
+namespace {
+
+// The pipeline over an explicit schedule: chunk i holds sizes[i] sequences
+// (all at most `cap`, the chunk the workspace was sized for).
+int forward_host_sched(tt_model* m, const float* x, const uint8_t* mask, float* out, int batch, int seq,
+                       const int* sizes, int n, int cap, void* workspace, size_t workspace_bytes, void* stream) {
+  const HostWsLayout h = host_ws_layout(m, cap, seq);
   if (workspace_bytes < h.total)
     return fail(TT_ERR_WORKSPACE, "workspace %zu < required %zu bytes", workspace_bytes, h.total);
   if (reinterpret_cast<uintptr_t>(workspace) % 1024 != 0)
@@ -1390,22 +1391,15 @@ int tt_model_forward_host(tt_model* m, const float* x, const uint8_t* mask, floa
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   uint8_t* base = static_cast<uint8_t*>(workspace);
   const size_t row_bytes = static_cast<size_t>(m->D) * 4;
-  const size_t model_bytes = ws_layout(m, chunk, seq).total;
+  const size_t model_bytes = ws_layout(m, cap, seq).total;
   // Copies start after the caller's earlier work on the stream (it may still use the workspace).
   if (int rc = check_cuda(cudaEventRecord(m->ev_entry, s), "cudaEventRecord")) return rc;
   cudaStreamWaitEvent(m->h2d, m->ev_entry, 0);
   cudaStreamWaitEvent(m->d2h, m->ev_entry, 0);
-  // The first chunk is a quarter of the others: until its copy-in and its
-  // kernels are done nothing else can overlap, so a small one shortens the
-  // pipeline's fill; after it the copies and the kernels run side by side.
-  const int first = (batch > chunk && chunk >= 4) ? chunk / 4 : chunk;
-  const int n = 1 + (batch - first + chunk - 1) / chunk;
-  for (int i = 0; i < n; ++i) {
+  int c0 = 0;
+  for (int i = 0; i < n; c0 += sizes[i], ++i) {
     const int b = i & 1;
-    const int c0 = i == 0 ? 0 : first + (i - 1) * chunk;
-    const int want = i == 0 ? first : chunk;
-    const int nb = batch - c0 < want ? batch - c0 : want;
-    if (nb <= 0) break;
+    const int nb = sizes[i];
     const size_t rows0 = static_cast<size_t>(c0) * seq, rows = static_cast<size_t>(nb) * seq;
     float* xd = reinterpret_cast<float*>(base + h.x[b]);
     float* od = reinterpret_cast<float*>(base + h.out[b]);
@@ -1436,6 +1430,48 @@ int tt_model_forward_host(tt_model* m, const float* x, const uint8_t* mask, floa
   }
   // The caller's stream completes only after the last copy-out.
   return check_cuda(cudaStreamWaitEvent(s, m->ev_out[(n - 1) & 1], 0), "cudaStreamWaitEvent");
+}
+
+int check_host_args(const tt_model* m, const float* x, const float* out, const void* workspace, int batch,
+                    int seq) {
+  if (!m || !x || !out || !workspace) return fail(TT_ERR_ARG, "null argument");
+  if (batch <= 0 || seq <= 0) return fail(TT_ERR_SHAPE, "invalid batch/seq");
+  return TT_OK;
+}
+
+}  // namespace
+
+int tt_model_forward_host(tt_model* m, const float* x, const uint8_t* mask, float* out, int batch, int seq,
+                          int chunk, void* workspace, size_t workspace_bytes, void* stream) {
+  if (int rc = check_host_args(m, x, out, workspace, batch, seq)) return rc;
+  if (chunk <= 0) return fail(TT_ERR_SHAPE, "invalid chunk %d", chunk);
+  if (chunk > batch) chunk = batch;
+  // The first chunk is a quarter of the others: until its copy-in and its
+  // kernels are done nothing else can overlap, so a small one shortens the
+  // pipeline's fill; after it the copies and the kernels run side by side.
+  std::vector<int> sizes;
+  const int first = (batch > chunk && chunk >= 4) ? chunk / 4 : chunk;
+  sizes.push_back(first);
+  for (int c0 = first; c0 < batch; c0 += chunk) sizes.push_back(batch - c0 < chunk ? batch - c0 : chunk);
+  return forward_host_sched(m, x, mask, out, batch, seq, sizes.data(), static_cast<int>(sizes.size()), chunk,
+                            workspace, workspace_bytes, stream);
+}
+
+int tt_model_forward_host_chunks(tt_model* m, const float* x, const uint8_t* mask, float* out, int batch,
+                                 int seq, const int* chunk_sizes, int n_chunks, void* workspace,
+                                 size_t workspace_bytes, void* stream) {
+  if (int rc = check_host_args(m, x, out, workspace, batch, seq)) return rc;
+  if (!chunk_sizes || n_chunks <= 0) return fail(TT_ERR_ARG, "empty chunk schedule");
+  long long total = 0;
+  int cap = 0;
+  for (int i = 0; i < n_chunks; ++i) {
+    if (chunk_sizes[i] <= 0) return fail(TT_ERR_SHAPE, "chunk %d has %d sequences", i, chunk_sizes[i]);
+    total += chunk_sizes[i];
+    if (chunk_sizes[i] > cap) cap = chunk_sizes[i];
+  }
+  if (total != batch) return fail(TT_ERR_SHAPE, "chunk sizes add up to %lld, batch is %d", total, batch);
+  return forward_host_sched(m, x, mask, out, batch, seq, chunk_sizes, n_chunks, cap, workspace,
+                            workspace_bytes, stream);
 }
 
 struct tt_graph {

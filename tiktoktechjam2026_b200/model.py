@@ -14,7 +14,7 @@ from __future__ import annotations
 import copy
 import ctypes
 from dataclasses import dataclass
-from typing import Dict, Optional
+from typing import Dict, Optional, Sequence
 
 import torch
 import torch.nn as nn
@@ -324,12 +324,15 @@ class B200Transformer(nn.Module):
         *,
         out: Optional[torch.Tensor] = None,
         chunk: Optional[int] = None,
+        chunks: Optional[Sequence[int]] = None,
     ) -> torch.Tensor:
         """``forward`` for host tensors, on the GPU holding the model's parameters.
 
         One ``tt_model_forward_host`` call: the batch is cut into chunks of
         ``chunk`` sequences, and the copy-in of the next chunk and the copy-out
-        of the previous one overlap the current chunk's kernels.  ``x`` (and
+        of the previous one overlap the current chunk's kernels.  ``chunks``
+        gives the schedule explicitly instead (sizes of consecutive chunks,
+        adding up to the batch; ``tt_model_forward_host_chunks``).  ``x`` (and
         ``out``, when given) should be pinned; pageable tensors are staged
         through a pinned copy.  Returns ``out`` (a new pinned FP32 tensor when
         none is given) once the result is in host memory.
@@ -363,19 +366,31 @@ class B200Transformer(nn.Module):
             if not mask8.is_pinned():
                 mask8 = mask8.pin_memory()
             mask_ptr = mask8.data_ptr()
-        if chunk is None:
-            chunk = default_host_chunk(B, S, self.config.d_model)
-        chunk = max(1, min(int(chunk), B))
         plan = self._plan(dev)
-        ws_ptr, ws_bytes = plan.host_workspace(chunk, S)
+        if chunks is not None:
+            sizes = [int(c) for c in chunks]
+            if not sizes or min(sizes) <= 0 or sum(sizes) != B:
+                raise ValueError(f"chunks must be positive sizes adding up to the batch {B}, got {sizes}")
+            ws_ptr, ws_bytes = plan.host_workspace(max(sizes), S)
+            arr = (ctypes.c_int * len(sizes))(*sizes)
+        else:
+            if chunk is None:
+                chunk = default_host_chunk(B, S, self.config.d_model)
+            chunk = max(1, min(int(chunk), B))
+            ws_ptr, ws_bytes = plan.host_workspace(chunk, S)
         with torch.cuda.device(dev):
             stream = torch.cuda.current_stream(dev)
-            _lib.check(
-                _lib.lib().tt_model_forward_host(
+            if chunks is not None:
+                rc = _lib.lib().tt_model_forward_host_chunks(
+                    plan.handle, x.data_ptr(), mask_ptr, out.data_ptr(), B, S, arr, len(sizes), ws_ptr, ws_bytes,
+                    stream.cuda_stream,
+                )
+            else:
+                rc = _lib.lib().tt_model_forward_host(
                     plan.handle, x.data_ptr(), mask_ptr, out.data_ptr(), B, S, chunk, ws_ptr, ws_bytes,
                     stream.cuda_stream,
                 )
-            )
+            _lib.check(rc)
             stream.synchronize()
         return out
 
