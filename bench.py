@@ -53,6 +53,11 @@ WORKLOADS = {
     "C3": (256, 256, 32, 2, 128, 4, True, 0.0),
     "C4": (16, 2048, 512, 8, 2048, 6, True, 0.5),
     "C5": (512, 1024, 256, 8, 1024, 4, True, 0.0),
+    # The reference suite's other cases (analysis_profile_mixed.py:20-26), every token valid.
+    "S6": (10000, 128, 128, 4, 128, 4, True, 0.0),
+    "S10": (64, 128, 128, 2, 128, 4, True, 0.0),
+    "S11": (64, 128, 128, 16, 128, 4, True, 0.0),
+    "S13": (64, 1024, 128, 4, 128, 4, True, 0.0),
 }
 METRIC = "sequences/sec (forward, FP32 in/out)"
 UNIT = "seq/s"
@@ -66,6 +71,8 @@ def kernel_label(kind, cfg):
     """Name of the kernel a kind of launch runs for this shape (the library's dispatch)."""
     hd = cfg["d_model"] // cfg["heads"]
     if kind == "attn":
+        if hd == 8:
+            return "attn_db_fwd_kernel<16> (head_dim 8 stored 16 wide)"
         return f"attn_db_fwd_kernel<{hd}>" if hd in (16, 32) else f"attn_fwd_kernel<{hd}>"
     if kind == "ffn_fused":
         return f"ffn2_kernel<{cfg['d_model']}>" if cfg["d_model"] in (128, 256) else f"ffn_fused_kernel<{cfg['d_model']}>"

@@ -74,10 +74,12 @@ int tt_layernorm_rows(const float* x, const float* gamma, const float* beta, voi
 int tt_mask_kv_end(const uint8_t* mask, int batch, int seq, int* kv_end, void* stream);
 
 /* Packed QKV projection: qkv = normalized[N, D] (FP16) . w_qkv[3D, D]^T (FP16)
- * + b_qkv (FP32), FP32 accumulation, stored FP16 head-major:
- *   q, k : [batch, heads, seq, head_dim]
- *   vt   : [batch, heads, head_dim, seq_pad]   (V transposed; seq_pad >= seq,
- *          seq_pad % 8 == 0; columns >= seq are left untouched)
+ * + b_qkv (FP32), FP32 accumulation, stored FP16 head-major with
+ * hs = max(head_dim, 16) features per head:
+ *   q, k : [batch, heads, seq, hs]      (head_dim 8: features 8..15 written as 0)
+ *   vt   : [batch, heads, hs, seq_pad]   (V transposed; seq_pad >= seq,
+ *          seq_pad % 8 == 0; columns >= seq, and rows >= head_dim, are left
+ *          untouched)
  * Replaces mixed_linear on qkv_proj (mixed_precision/triton_linear.py:221-269,
  * called at mixed_precision/transformer.py:93-143). */
 int tt_qkv_projection(const void* normalized, const void* w_qkv, const float* b_qkv, void* q,
@@ -88,7 +90,10 @@ int tt_qkv_projection(const void* normalized, const void* w_qkv, const float* b_
  * FP16 operands, FP32 softmax statistics and accumulation, FP16 output.
  * key_mask: [batch, seq] bytes (nonzero = valid) or NULL; kv_end must then hold
  * tt_mask_kv_end's output.  With a mask, padded query rows get a zero context
- * (the reference zeroes those rows on the model output).  head_dim in {16, 32, 64}.
+ * (the reference zeroes those rows on the model output).  head_dim in
+ * {8, 16, 32, 64}; q, k and vt have tt_qkv_projection's layout (16 features
+ * per head when head_dim is 8, the extra q/k features zero), ctx has head_dim
+ * per head.
  * Replaces fp16_causal_attention / causal_attention
  * (custom_kernel/triton_attention.py:126-232, 264-390) and the SDPA route
  * (mixed_precision/transformer.py:157-198). */

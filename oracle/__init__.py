@@ -11,6 +11,7 @@ from .reference_fp32 import (  # noqa: F401
     CONFIGS,
     DEFAULT_SEED,
     RTOL,
+    SUITE_CONFIGS,
     TIMING_SEED_OFFSET,
     Comparison,
     Config,

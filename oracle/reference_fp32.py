@@ -60,6 +60,17 @@ CONFIGS: Dict[str, Tuple[Config, float]] = {
     "C5": (Config(512, 1024, 256, 8, 1024, 4, True), 0.0),
 }
 
+# Cases of the reference's wider suite that BASELINE.json does not name
+# (analysis_profile_mixed.py:20-26; run with every token valid, :45).  Case 8
+# (d_model 1024, head_dim 256) is outside this build's shape coverage.
+SUITE_CONFIGS: Dict[str, Tuple[Config, float]] = {
+    "S6": (Config(10000, 128, 128, 4, 128, 4, True), 0.0),
+    "S8": (Config(64, 128, 1024, 4, 1024, 4, True), 0.0),
+    "S10": (Config(64, 128, 128, 2, 128, 4, True), 0.0),
+    "S11": (Config(64, 128, 128, 16, 128, 4, True), 0.0),
+    "S13": (Config(64, 1024, 128, 4, 128, 4, True), 0.0),
+}
+
 DEFAULT_SEED = 1234  # torch_transformer_benchmark.py:871
 TIMING_SEED_OFFSET = 100000  # torch_transformer_benchmark.py:747
 ATOL = 0.002

@@ -37,7 +37,8 @@ def test_layernorm_rows(tt_lib, d, n, out_dtype):
     torch.testing.assert_close(out.float(), ref, rtol=tol, atol=tol)
 
 
-QKV_SHAPES = [(2, 16, 32, 2), (3, 130, 128, 4), (1, 256, 256, 8), (2, 64, 512, 8), (64, 128, 128, 4)]
+QKV_SHAPES = [(2, 16, 32, 2), (3, 130, 128, 4), (1, 256, 256, 8), (2, 64, 512, 8), (64, 128, 128, 4),
+              (2, 128, 128, 16), (1, 70, 64, 8)]
 
 
 @pytest.mark.parametrize("B,S,D,H", QKV_SHAPES)
@@ -47,11 +48,15 @@ def test_qkv_projection(tt_lib, B, S, D, H):
     w = (torch.randn(3 * D, D, generator=g) / math.sqrt(D)).half().to(DEV)
     b = (torch.randn(3 * D, generator=g) * 0.1).to(DEV)
     q, k, vt = ops.qkv_projection(n, w, b, H)
-    ref = (n.float() @ w.float().t() + b).view(B, S, 3, H, D // H).permute(2, 0, 3, 1, 4)
+    hd = D // H
+    ref = (n.float() @ w.float().t() + b).view(B, S, 3, H, hd).permute(2, 0, 3, 1, 4)
+    assert q.shape[-1] == ops.stored_head_dim(hd) and vt.shape[2] == ops.stored_head_dim(hd)
     # FP16 output rounding of |x| < 8 values: 4e-3
-    torch.testing.assert_close(q.float(), ref[0], rtol=2e-3, atol=4e-3)
-    torch.testing.assert_close(k.float(), ref[1], rtol=2e-3, atol=4e-3)
-    torch.testing.assert_close(vt[..., :S].float(), ref[2].transpose(-1, -2), rtol=2e-3, atol=4e-3)
+    torch.testing.assert_close(q[..., :hd].float(), ref[0], rtol=2e-3, atol=4e-3)
+    torch.testing.assert_close(k[..., :hd].float(), ref[1], rtol=2e-3, atol=4e-3)
+    torch.testing.assert_close(vt[:, :, :hd, :S].float(), ref[2].transpose(-1, -2), rtol=2e-3, atol=4e-3)
+    # head_dim 8 is stored 16 wide; the padding features of q and k are exact zeros.
+    assert torch.all(q[..., hd:] == 0) and torch.all(k[..., hd:] == 0)
 
 
 def _attn_ref(q, k, vt, scale, causal, mask):
@@ -69,6 +74,7 @@ def _attn_ref(q, k, vt, scale, causal, mask):
 
 ATTN_SHAPES = [
     (2, 2, 16, 16), (1, 4, 130, 32), (2, 2, 256, 64), (1, 8, 1024, 32), (3, 1, 200, 16), (1, 2, 384, 64),
+    (2, 4, 200, 8), (1, 16, 128, 8),
 ]
 
 
@@ -77,11 +83,17 @@ ATTN_SHAPES = [
 @pytest.mark.parametrize("mask_kind", [None, "prefix", "random"])
 def test_attention(tt_lib, B, H, S, hd, causal, mask_kind):
     g = _gen(B * 1000 + S + hd)
-    q = torch.randn(B, H, S, hd, generator=g).half().to(DEV)
-    k = torch.randn(B, H, S, hd, generator=g).half().to(DEV)
+    hs = ops.stored_head_dim(hd)
+    q = torch.zeros(B, H, S, hs, dtype=torch.float16)
+    k = torch.zeros(B, H, S, hs, dtype=torch.float16)
+    q[..., :hd] = torch.randn(B, H, S, hd, generator=g).half()
+    k[..., :hd] = torch.randn(B, H, S, hd, generator=g).half()
+    q, k = q.to(DEV), k.to(DEV)
     sp = ops.seq_pad_of(S)
-    vt = torch.zeros(B, H, hd, sp, dtype=torch.float16)
-    vt[..., :S] = torch.randn(B, H, hd, S, generator=g).half()
+    vt = torch.zeros(B, H, hs, sp, dtype=torch.float16)
+    vt[:, :, :hd, :S] = torch.randn(B, H, hd, S, generator=g).half()
+    if hs > hd:
+        vt[:, :, hd:, :S] = 7.0  # rows past head_dim feed no stored output
     vt = vt.to(DEV)
     mask = None
     if mask_kind == "prefix":
@@ -91,8 +103,8 @@ def test_attention(tt_lib, B, H, S, hd, causal, mask_kind):
         mask = (torch.rand(B, S, generator=g) > 0.3).to(DEV)
         mask[:, 0] = True
     scale = hd**-0.5
-    out = ops.attention(q, k, vt, scale, causal, mask)
-    ref = _attn_ref(q, k, vt, scale, causal, mask)
+    out = ops.attention(q, k, vt, scale, causal, mask, head_dim=hd)
+    ref = _attn_ref(q[..., :hd], k[..., :hd], vt[:, :, :hd], scale, causal, mask)
     if mask is not None:
         # Padded query rows are defined as zero context.
         ref = ref.masked_fill(~mask[..., None], 0)

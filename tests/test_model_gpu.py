@@ -76,6 +76,38 @@ def test_config_parity_zero_failures(tt_lib, strict_fp32, golden, name):
         assert r.failed == 0, (i, r)
 
 
+SUITE_CHUNK = {"S6": 500, "S10": 64, "S11": 64, "S13": 16}
+
+
+@pytest.mark.parametrize("name", ["S6", "S10", "S11", "S13"])
+def test_suite_case_parity_zero_failures(tt_lib, strict_fp32, name):
+    """The reference suite's cases outside BASELINE.json (analysis_profile_mixed.py:20-26, every token
+    valid): batch 10000, head_dim 64, head_dim 8 (stored 16 wide), seq 1024 at d_model 128."""
+    cfg, pad = oracle.SUITE_CONFIGS[name]
+    sd = oracle.seeded_state_dict(cfg, oracle.DEFAULT_SEED)
+    model = build_model(cfg, sd)
+    model.assume_all_tokens_valid = True
+    x, _ = oracle.generate_case(cfg, oracle.DEFAULT_SEED, pad)
+    with torch.inference_mode():
+        out = model(x.to(DEV))
+        torch.cuda.synchronize()
+        _device_clean()
+        ref = oracle_gpu(sd, cfg, x, None, SUITE_CHUNK[name])
+    res = oracle.compare(ref, out)
+    print(f"{name}: failed={res.failed}/{res.total} max_abs={res.max_abs:.6g} max_rel={res.max_rel:.4g}")
+    assert res.failed == 0, res
+
+
+def test_suite_case8_outside_coverage(tt_lib):
+    """Suite case 8 (d_model 1024, head_dim 256) is refused with TT_ERR_UNSUPPORTED, not run wrongly."""
+    cfg, _ = oracle.SUITE_CONFIGS["S8"]
+    model = build_model(cfg, oracle.seeded_state_dict(cfg, 1))
+    x = torch.zeros(1, cfg.seq_len, cfg.d_model, device=DEV)
+    with torch.inference_mode(), pytest.raises(_lib.TTError) as e:
+        model(x)
+    assert e.value.code == _lib.TT_ERR_UNSUPPORTED
+
+
 @pytest.mark.parametrize("name", ["t_causal_small", "t_causal_mask", "t_full_mask", "t_causal_s130", "t_hd64"])
 def test_tiny_golden_cases(tt_lib, golden, name):
     data, meta = golden
@@ -100,6 +132,8 @@ def test_tiny_golden_cases(tt_lib, golden, name):
         (1, 1, 32, 2, 64, 1, True, None),
         (5, 300, 256, 8, 512, 2, True, "prefix"),
         (2, 256, 512, 8, 1024, 1, True, "prefix"),
+        (3, 130, 64, 8, 128, 2, True, "random"),
+        (2, 96, 128, 16, 256, 1, False, "prefix"),
     ],
 )
 def test_edge_shapes(tt_lib, strict_fp32, B, S, D, H, Fd, L, causal, mask_kind):

@@ -80,3 +80,37 @@ def test_forward_rejects_non_fp32_and_cpu():
         model(torch.zeros(1, 8, 32, dtype=torch.float16))
     with pytest.raises(RuntimeError, match="CUDA"):
         model(torch.zeros(1, 8, 32))
+
+
+class _RowwiseModel(torch.nn.Module):
+    """Stand-in model: each sequence's output depends only on that sequence (and its mask row)."""
+
+    def __init__(self):
+        super().__init__()
+        self.calls = []
+
+    def forward(self, x, mask=None):
+        self.calls.append(x.shape[0])
+        y = x * 2.0 + 1.0
+        if mask is not None:
+            y = y.masked_fill(~mask[..., None], 0.0)
+        return y
+
+
+def test_microbatch_wrapper_matches_whole_batch():
+    """PreallocatedMicrobatchModel (mixed_precision_benchmark.py:13-33): slices of microbatch_size, ragged
+    tail, mask sliced alongside, a batch no larger than one microbatch passed through untouched."""
+    from tiktoktechjam2026_b200 import PreallocatedMicrobatchModel
+
+    g = torch.Generator().manual_seed(3)
+    x = torch.randn(10, 5, 4, generator=g)
+    mask = torch.rand(10, 5, generator=g) > 0.4
+    inner = _RowwiseModel()
+    wrapped = PreallocatedMicrobatchModel(inner, 4)
+    out = wrapped(x, mask)
+    assert inner.calls == [4, 4, 2]
+    assert out.dtype == torch.float32 and torch.equal(out, _RowwiseModel()(x, mask))
+    inner.calls.clear()
+    assert torch.equal(wrapped(x[:4]), x[:4] * 2.0 + 1.0) and inner.calls == [4]
+    with pytest.raises(ValueError):
+        PreallocatedMicrobatchModel(inner, 0)

@@ -41,7 +41,9 @@ struct AttnParams {
   float scale_log2;             // head_dim^-0.5 * log2(e)
   const uint8_t* key_mask;      // [batch, seq], nonzero = valid; nullptr = all valid
   const int* kv_end;            // [batch]: 1 + index of the last valid key (with key_mask)
-  __half* ctx;                  // [batch, seq, heads * HD]
+  __half* ctx;                  // [batch, seq, heads * ctx_hd]
+  int ctx_hd;                   // features per head of ctx: HD, or 8 when head_dim 8
+                                // runs on Q/K/V stored 16 wide (zeros after the 8)
   unsigned int* err;
   unsigned long long timeout_ns;
 };

@@ -127,7 +127,8 @@ __global__ void __launch_bounds__(AttnDbLayout<HD>::THREADS, 1)
                                              ~static_cast<uintptr_t>(1023));
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n_qt = (p.seq + BM - 1) / BM;
-  const int D = p.heads * HD;
+  const int D = p.heads * p.ctx_hd;  // ctx row width (p.ctx_hd = 8 or HD)
+  const int n_out16 = p.ctx_hd / 8;   // 16-byte pieces of a stored ctx row per head
   constexpr int NS = L::NS, NSB = L::NSB;
   const int G2 = NS * static_cast<int>(gridDim.x);  // item stride of one stream
   uint64_t* bars_all = reinterpret_cast<uint64_t*>(smem + L::OFF_BAR);
@@ -346,7 +347,7 @@ __global__ void __launch_bounds__(AttnDbLayout<HD>::THREADS, 1)
           v.y = pack_half2(__uint_as_float(o[8 * i + 2]) * pend_inv, __uint_as_float(o[8 * i + 3]) * pend_inv);
           v.z = pack_half2(__uint_as_float(o[8 * i + 4]) * pend_inv, __uint_as_float(o[8 * i + 5]) * pend_inv);
           v.w = pack_half2(__uint_as_float(o[8 * i + 6]) * pend_inv, __uint_as_float(o[8 * i + 7]) * pend_inv);
-          reinterpret_cast<uint4*>(pend_dst)[i] = v;
+          if (i < n_out16) reinterpret_cast<uint4*>(pend_dst)[i] = v;
         }
       }
       return true;
@@ -355,12 +356,13 @@ __global__ void __launch_bounds__(AttnDbLayout<HD>::THREADS, 1)
     for (int w = NS * static_cast<int>(blockIdx.x) + s; ok && w < n_items; w += G2) {
       const AttnItem item = attn_item(p, w, n_qt);
       const int qi = item.q0 + row;
-      __half* dst_row = p.ctx + (static_cast<size_t>(item.b) * p.seq + qi) * D + item.h * HD;
+      __half* dst_row = p.ctx + (static_cast<size_t>(item.b) * p.seq + qi) * D + item.h * p.ctx_hd;
       const int nt = n_tiles(item);
       if (nt == 0) {
         if (qi < p.seq) {
 #pragma unroll
-          for (int i = 0; i < HD / 8; ++i) reinterpret_cast<uint4*>(dst_row)[i] = make_uint4(0, 0, 0, 0);
+          for (int i = 0; i < HD / 8; ++i)
+            if (i < n_out16) reinterpret_cast<uint4*>(dst_row)[i] = make_uint4(0, 0, 0, 0);
         }
         continue;
       }

@@ -33,6 +33,11 @@ constexpr int kAbiVersion = 1;
 constexpr int kMaxDevices = 64;
 constexpr int kSmemBudget = 225 * 1024;
 
+// Features per head as Q, K and V^T are stored: head_dim 8 is kept 16 wide
+// (features 8..15 of Q and K zero) so that the head_dim-16 attention kernel,
+// whose MMAs need K = 16, runs on it unchanged.
+inline int stored_head_dim(int hd) { return hd < 16 ? 16 : hd; }
+
 thread_local char g_last_error[512] = "";
 std::atomic<unsigned long long> g_launches{0};
 std::atomic<unsigned long long> g_timeout_ns{2000000000ull};
@@ -162,9 +167,11 @@ int encode_epi_tile(CUtensorMap* tm, const void* base, uint64_t rows, uint64_t c
                        base, 2, dims, strides, box);
 }
 
-// Store maps of the QKV epilogue: Q, K [B*H, S, hd] and V^T [B*H, hd, S_pad].
+// Store maps of the QKV epilogue: Q, K [B*H, S, hs] and V^T [B*H, hs, S_pad]
+// (hs = stored_head_dim(hd)).
 int encode_qkv_store_maps(CUtensorMap* tq, CUtensorMap* tk, CUtensorMap* tv, const void* q,
-                          const void* k, const void* vt, int bh, int seq, int hd, int seq_pad) {
+                          const void* k, const void* vt, int bh, int seq, int hd_real, int seq_pad) {
+  const int hd = stored_head_dim(hd_real);
   const uint32_t w = static_cast<uint32_t>(hd < 32 ? hd : 32);
   {
     const uint64_t dims[3] = {static_cast<uint64_t>(hd), static_cast<uint64_t>(seq),
@@ -257,8 +264,8 @@ int check_model_shape(int d_model, int heads, int ffn) {
   if (d_model <= 0 || heads <= 0 || ffn <= 0 || d_model % heads != 0)
     return fail(TT_ERR_SHAPE, "invalid (d_model=%d, heads=%d, ffn=%d)", d_model, heads, ffn);
   const int hd = d_model / heads;
-  if (hd != 16 && hd != 32 && hd != 64)
-    return fail(TT_ERR_UNSUPPORTED, "head_dim %d not in {16, 32, 64}", hd);
+  if (hd != 8 && hd != 16 && hd != 32 && hd != 64)
+    return fail(TT_ERR_UNSUPPORTED, "head_dim %d not in {8, 16, 32, 64}", hd);
   if (d_model % 32 != 0 || d_model > 512 || (d_model > 256 && d_model != 512))
     return fail(TT_ERR_UNSUPPORTED, "d_model %d must be a multiple of 32, <= 256, or 512", d_model);
   if (ffn % 32 != 0) return fail(TT_ERR_UNSUPPORTED, "ffn %d must be a multiple of 32", ffn);
@@ -439,9 +446,11 @@ int check_ln_width(int d) {
   return TT_OK;
 }
 
-// Q/K/V^T tensor maps for attention over a [B*H, S, hd] / [B*H, hd, S_pad] layout.
+// Q/K/V^T tensor maps for attention over a [B*H, S, hs] / [B*H, hs, S_pad]
+// layout (hs = stored_head_dim(hd)).
 int encode_attention_maps(CUtensorMap* tq, CUtensorMap* tk, CUtensorMap* tv, const void* q,
-                          const void* k, const void* vt, int bh, int seq, int hd, int seq_pad) {
+                          const void* k, const void* vt, int bh, int seq, int hd_real, int seq_pad) {
+  const int hd = stored_head_dim(hd_real);
   {
     const uint64_t dims[3] = {static_cast<uint64_t>(hd), static_cast<uint64_t>(seq),
                               static_cast<uint64_t>(bh)};
@@ -471,11 +480,13 @@ int launch_attention(const CUtensorMap& tq, const CUtensorMap& tk, const CUtenso
   if (items > 0x7fffffffLL) return fail(TT_ERR_SHAPE, "batch*heads*query tiles too large");
   const int n_items = static_cast<int>(items);
   const unsigned grid = static_cast<unsigned>(n_items < sm_count ? n_items : sm_count);
-  if (hd == 16 || hd == 32) {
+  if (ap.ctx_hd != hd) return fail(TT_ERR_ARG, "ctx head width %d != head_dim %d", ap.ctx_hd, hd);
+  if (hd == 8 || hd == 16 || hd == 32) {
     // Two streams per CTA, 64-key tiles, double-buffered scores and probabilities.
-    auto kern = hd == 16 ? (exp16 ? attn_db_fwd_kernel<16, true> : attn_db_fwd_kernel<16, false>)
+    // head_dim 8 runs the head_dim-16 kernel on its zero-padded Q/K/V.
+    auto kern = hd <= 16 ? (exp16 ? attn_db_fwd_kernel<16, true> : attn_db_fwd_kernel<16, false>)
                          : (exp16 ? attn_db_fwd_kernel<32, true> : attn_db_fwd_kernel<32, false>);
-    const int smem = hd == 16 ? AttnDbLayout<16>::SMEM_ALLOC : AttnDbLayout<32>::SMEM_ALLOC;
+    const int smem = hd <= 16 ? AttnDbLayout<16>::SMEM_ALLOC : AttnDbLayout<32>::SMEM_ALLOC;
     if (int rc = prepare_kernel(kern, smem)) return rc;
     // The kernel splits its registers with setmaxnreg; that split is only sound
     // when each thread is launched with exactly the planned register count.
@@ -493,7 +504,7 @@ int launch_attention(const CUtensorMap& tq, const CUtensorMap& tk, const CUtenso
     if (int rc = prepare_kernel(kern, AttnLayout<64>::SMEM_ALLOC)) return rc;
     kern<<<grid, 192, AttnLayout<64>::SMEM_ALLOC, stream>>>(tq, tk, tv, ap, n_items);
   } else {
-    return fail(TT_ERR_UNSUPPORTED, "head_dim %d not in {16, 32, 64}", hd);
+    return fail(TT_ERR_UNSUPPORTED, "head_dim %d not in {8, 16, 32, 64}", hd);
   }
   return after_launch("attention");
 }
@@ -602,7 +613,7 @@ size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 WsLayout ws_layout(const tt_model* m, int batch, int seq) {
   WsLayout w;
   const size_t N = static_cast<size_t>(batch) * seq;
-  const int hd = m->D / m->H;
+  const int hs = stored_head_dim(m->D / m->H);
   w.seq_pad = (seq + 7) / 8 * 8;
   size_t off = 0;
   auto take = [&](size_t bytes) {
@@ -612,9 +623,9 @@ WsLayout ws_layout(const tt_model* m, int batch, int seq) {
   };
   w.resid = take(N * m->D * 4);
   w.norm = take(N * m->D * 2);
-  w.q = take(N * m->D * 2);
-  w.k = take(N * m->D * 2);
-  w.vt = take(static_cast<size_t>(batch) * m->H * hd * w.seq_pad * 2);
+  w.q = take(N * m->H * hs * 2);
+  w.k = take(N * m->H * hs * 2);
+  w.vt = take(static_cast<size_t>(batch) * m->H * hs * w.seq_pad * 2);
   w.ctx = take(N * m->D * 2);
   Route r;
   const bool fused = choose_route(m->D, m->H, seq, m->F, &r) == TT_OK && r.ffn_fused;
@@ -761,7 +772,8 @@ int bind_workspace(tt_model* m, int batch, int seq, void* ws, cudaStream_t strea
   // must hold finite values because masked probabilities (0) multiply them.
   if (w.seq_pad != seq)
     if (int rc = check_cuda(cudaMemsetAsync(base + w.vt, 0,
-                                            static_cast<size_t>(batch) * m->H * hd * w.seq_pad * 2,
+                                            static_cast<size_t>(batch) * m->H * stored_head_dim(hd) *
+                                                w.seq_pad * 2,
                                             stream),
                             "cudaMemsetAsync"))
       return rc;
@@ -902,6 +914,7 @@ int tt_causal_attention(const void* q, const void* k, const void* vt, const uint
   ap.key_mask = key_mask;
   ap.kv_end = kv_end;
   ap.ctx = static_cast<__half*>(ctx);
+  ap.ctx_hd = head_dim;
   ap.err = ds->err;
   ap.timeout_ns = g_timeout_ns.load();
   return launch_attention(tq, tk, tv, ap, head_dim, false, ds->sm_count, static_cast<cudaStream_t>(stream));
@@ -945,6 +958,7 @@ int tt_causal_attention_masked_noalloc(const void* q, const void* k, const void*
   ap.key_mask = key_mask;
   ap.kv_end = key_mask ? kv_end : nullptr;
   ap.ctx = static_cast<__half*>(ctx);
+  ap.ctx_hd = head_dim;
   ap.err = ds->err;
   ap.timeout_ns = g_timeout_ns.load();
   return launch_attention(tq, tk, tv, ap, head_dim, false, ds->sm_count, s);
@@ -1199,6 +1213,7 @@ int tt_model_forward(tt_model* m, const float* x, const uint8_t* mask, float* ou
   ap.key_mask = mask;
   ap.kv_end = mask ? kv_end : nullptr;
   ap.ctx = ctx;
+  ap.ctx_hd = hd;
   ap.err = ds->err;
   ap.timeout_ns = g_timeout_ns.load();
 

@@ -16,7 +16,8 @@
 //               MMAs of item i+1 overlap the epilogue of item i
 //   warps 0..3  epilogue: warp e owns rows 32e..32e+31 of the tile, one row
 //               per thread (TMEM lane = row), in 32-column chunks:
-//   EPI_QKV       + bias, FP16, to Q/K [B*H, S, hd] and V^T [B*H, hd, S_pad]
+//   EPI_QKV       + bias, FP16, to Q/K [B*H, S, hs] and V^T [B*H, hs, S_pad]
+//                 (hs = max(hd, 16); head_dim 8 is stored with 8 zero features)
 //   EPI_RESID_LN  + bias + FP32 residual -> residual out (FP32), then a
 //                 two-pass FP32 LayerNorm of the row (the row is kept in
 //                 TMEM between passes) -> FP16 or FP32, optionally zeroing
@@ -399,9 +400,52 @@ __global__ void __launch_bounds__(gemm_threads(EPI), 1)
             within0 -= D;
             ++which;
           }
-          if (which < 2) {
-            // Q / K: a thread's 32 values are consecutive features of its row, in runs of
-            // 16 that are each 32 contiguous bytes of [B*H, S, hd].
+          if (which < 2 && p.tma_out && hd >= 32) {
+            // Q / K: the warp's 32 rows of these 32 features are 64-byte pieces of
+            // consecutive rows of [B*H, S, hd] (the slab lies within one sequence:
+            // S % 32 == 0).  Stage them row-major (16-byte piece k of row r at
+            // r * 64 + ((k ^ ((r >> 1) & 3)) << 4), conflict-free both ways), then
+            // write 8 rows per instruction, 4 lanes per 64-byte piece.
+            if (!warp_active) continue;
+            const uint32_t slot = ring.base;
+            __syncwarp();
+#pragma unroll
+            for (int k = 0; k < 4; ++k)
+              st_shared_v4(slot + lane * 64 + ((k ^ ((lane >> 1) & 3)) << 4), pack_half2(f[8 * k], f[8 * k + 1]),
+                           pack_half2(f[8 * k + 2], f[8 * k + 3]), pack_half2(f[8 * k + 4], f[8 * k + 5]),
+                           pack_half2(f[8 * k + 6], f[8 * k + 7]));
+            __syncwarp();
+            const int hh = within0 >> lg_hd, d0 = within0 & (hd - 1);
+            __half* blk = (which == 0 ? p.q : p.k) +
+                          ((static_cast<size_t>(b_w) * p.heads + hh) * p.seq + s0) * hd + d0;
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+              const int rr = 8 * k + (lane >> 2), pc = lane & 3;
+              const uint4 v4 = ld_shared_v4(slot + rr * 64 + ((pc ^ ((rr >> 1) & 3)) << 4));
+              *reinterpret_cast<uint4*>(blk + static_cast<size_t>(rr) * hd + pc * 8) = v4;
+            }
+          } else if (which < 2 && hd == 8) {
+            // Q / K with head_dim 8, stored 16 wide: each of the chunk's 4 heads is
+            // the row's 8 features and 8 zeros (32 contiguous bytes of [B*H, S, 16]).
+            if (valid) {
+              __half* base = which == 0 ? p.q : p.k;
+#pragma unroll
+              for (int j = 0; j < 4; ++j) {
+                const int hh = (within0 >> 3) + j;
+                uint4* dst = reinterpret_cast<uint4*>(
+                    base + ((static_cast<size_t>(bidx) * p.heads + hh) * p.seq + s) * 16);
+                uint4 a;
+                a.x = pack_half2(f[8 * j + 0], f[8 * j + 1]);
+                a.y = pack_half2(f[8 * j + 2], f[8 * j + 3]);
+                a.z = pack_half2(f[8 * j + 4], f[8 * j + 5]);
+                a.w = pack_half2(f[8 * j + 6], f[8 * j + 7]);
+                dst[0] = a;
+                dst[1] = make_uint4(0, 0, 0, 0);
+              }
+            }
+          } else if (which < 2) {
+            // Q / K, rows not staged: a thread's 32 values are consecutive features of
+            // its row, in runs of 16 that are each 32 contiguous bytes of [B*H, S, hd].
             if (valid) {
               __half* base = which == 0 ? p.q : p.k;
 #pragma unroll
@@ -423,7 +467,7 @@ __global__ void __launch_bounds__(gemm_threads(EPI), 1)
                 dst[1] = bq;
               }
             }
-          } else if (p.tma_out) {
+          } else if (p.tma_out && hd >= 16) {
             // V^T: transpose the 32 rows through this warp's staging tile, then write
             // [wbox features x 32 tokens] as 64-byte rows of [B*H, hd, S_pad] with
             // coalesced 16-byte stores (the slab lies within one sequence: S % 32 == 0).
@@ -449,11 +493,14 @@ __global__ void __launch_bounds__(gemm_threads(EPI), 1)
               }
             }
           } else if (valid) {
+            // V^T one element at a time ([B*H, hs, S_pad], hs = 16 for head_dim 8:
+            // rows 8..15 of a head are never read into any stored output).
+            const int hs = hd < 16 ? 16 : hd;
 #pragma unroll
             for (int e = 0; e < 32; ++e) {
               const int within = within0 + e;
               const int hh = within >> lg_hd, d = within & (hd - 1);
-              p.vt[((static_cast<size_t>(bidx) * p.heads + hh) * hd + d) * p.seq_pad + s] =
+              p.vt[((static_cast<size_t>(bidx) * p.heads + hh) * hs + d) * p.seq_pad + s] =
                   __float2half_rn(f[e]);
             }
           }

@@ -487,3 +487,32 @@ def copy_mixed_model_weights(baseline: nn.Module, mixed: nn.Module) -> None:
         else:
             mapped[key] = source[key]
     mixed.load_state_dict(mapped, strict=True)
+
+
+class PreallocatedMicrobatchModel(nn.Module):
+    """Runs ``model`` over microbatches of ``microbatch_size`` sequences into one preallocated output.
+
+    Same contract as the reference runner's wrapper (mixed_precision_benchmark.py:13-33),
+    which it applies automatically to batches of 4096 or more (:79-84): a batch no
+    larger than one microbatch goes straight to ``model``; otherwise every slice of
+    ``x`` (and of the mask) runs separately and is copied into an FP32 output shaped
+    like ``x``.  A B200Transformer needs no microbatching for memory (its whole batch
+    runs as one call); the wrapper is here so that runners which apply it keep working.
+    """
+
+    def __init__(self, model: nn.Module, microbatch_size: int) -> None:
+        super().__init__()
+        if microbatch_size <= 0:
+            raise ValueError("microbatch_size must be positive")
+        self.model = model
+        self.microbatch_size = microbatch_size
+
+    def forward(self, x: torch.Tensor, valid_token_mask: Optional[torch.Tensor] = None) -> torch.Tensor:
+        if x.shape[0] <= self.microbatch_size:
+            return self.model(x, valid_token_mask)
+        output = torch.empty_like(x, dtype=torch.float32)
+        for start in range(0, x.shape[0], self.microbatch_size):
+            end = min(start + self.microbatch_size, x.shape[0])
+            mask_slice = None if valid_token_mask is None else valid_token_mask[start:end]
+            output[start:end].copy_(self.model(x[start:end], mask_slice))
+        return output

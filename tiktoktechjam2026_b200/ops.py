@@ -30,6 +30,11 @@ def _cuda(t: torch.Tensor, name: str) -> None:
     _need(t.is_cuda and t.is_contiguous(), f"{name} must be a contiguous CUDA tensor")
 
 
+def stored_head_dim(head_dim: int) -> int:
+    """Features per head of the q/k/v^T buffers: head_dim 8 is stored 16 wide."""
+    return max(head_dim, 16)
+
+
 def seq_pad_of(seq: int) -> int:
     """Row length of the V^T buffer: seq rounded up to a multiple of 8."""
     return (seq + 7) // 8 * 8
@@ -53,15 +58,18 @@ def layernorm_rows(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor, ep
 
 def qkv_projection(normalized: torch.Tensor, w_qkv: torch.Tensor, b_qkv: torch.Tensor, heads: int
                    ) -> Tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
-    """normalized [B, S, D] FP16 -> q, k [B, H, S, hd] FP16 and v^T [B, H, hd, S_pad] FP16."""
+    """normalized [B, S, D] FP16 -> q, k [B, H, S, hs] FP16 and v^T [B, H, hs, S_pad] FP16.
+
+    hs = max(D // heads, 16): head_dim 8 is stored 16 wide (q/k features 8..15 zero).
+    """
     _cuda(normalized, "normalized")
     _need(normalized.dtype == torch.float16 and w_qkv.dtype == torch.float16, "FP16 operands required")
     B, S, D = normalized.shape
-    hd = D // heads
+    hs = stored_head_dim(D // heads)
     sp = seq_pad_of(S)
-    q = torch.empty(B, heads, S, hd, dtype=torch.float16, device=normalized.device)
+    q = torch.empty(B, heads, S, hs, dtype=torch.float16, device=normalized.device)
     k = torch.empty_like(q)
-    vt = torch.zeros(B, heads, hd, sp, dtype=torch.float16, device=normalized.device)
+    vt = torch.zeros(B, heads, hs, sp, dtype=torch.float16, device=normalized.device)
     b32 = b_qkv.float().contiguous()
     with torch.cuda.device(normalized.device):
         check(lib().tt_qkv_projection(normalized.data_ptr(), w_qkv.contiguous().data_ptr(), b32.data_ptr(),
@@ -71,12 +79,17 @@ def qkv_projection(normalized: torch.Tensor, w_qkv: torch.Tensor, b_qkv: torch.T
 
 
 def attention(q: torch.Tensor, k: torch.Tensor, vt: torch.Tensor, scale: float, causal: bool = True,
-              key_mask: Optional[torch.Tensor] = None) -> torch.Tensor:
-    """q, k [B, H, S, hd], vt [B, H, hd, S_pad] FP16 -> context [B, S, H*hd] FP16."""
+              key_mask: Optional[torch.Tensor] = None, head_dim: Optional[int] = None) -> torch.Tensor:
+    """q, k [B, H, S, hs], vt [B, H, hs, S_pad] FP16 -> context [B, S, H*hd] FP16.
+
+    hd = head_dim (default hs); head_dim 8 takes qkv_projection's 16-wide layout.
+    """
     for t, n in ((q, "q"), (k, "k"), (vt, "vt")):
         _cuda(t, n)
         _need(t.dtype == torch.float16, f"{n} must be FP16")
-    B, H, S, hd = q.shape
+    B, H, S, hs = q.shape
+    hd = hs if head_dim is None else int(head_dim)
+    _need(stored_head_dim(hd) == hs, f"head_dim {hd} is stored {stored_head_dim(hd)} wide, got {hs}")
     sp = vt.shape[-1]
     ctx = torch.empty(B, S, H * hd, dtype=torch.float16, device=q.device)
     mask_ptr = 0
