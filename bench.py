@@ -5,9 +5,10 @@
 
 Workload: BASELINE configuration C5 by default (batch 512, seq 1024,
 d_model 256, 8 heads, ffn 1024, 4 layers, causal), the configuration the
-metric's 1/2/4/8-GPU clause is quoted on; the batch is sharded across the N
-ranks (one process per GPU, launched by torchrun for N > 1) with no
-collective in the data path.  A step is one forward of this rank's shard.
+metric's 1/2/4/8-GPU clause is quoted on.  Weak scaling: each of the N ranks
+(one process per GPU, launched by torchrun for N > 1) runs that whole batch as
+its shard of a global batch of N times as many sequences, with no collective
+in the data path.  A step is one forward of this rank's shard.
 
   value  device-resident inputs; per step: L2 flush (256 MiB write, untimed),
          CUDA events around the forward; max over ranks of the summed step
@@ -93,7 +94,7 @@ def parse_args():
     ap.add_argument("--graph", action="store_true",
                     help="time replays of one captured CUDA graph of the forward (small workloads)")
     ap.add_argument("--batch", type=int, default=None,
-                    help="override the workload's global batch (smaller profiling cases)")
+                    help="override the workload's batch per GPU (smaller profiling cases)")
     return ap.parse_args()
 
 
@@ -269,7 +270,7 @@ def run_reference(args, cfg, padding_ratio, workload_name):
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000.0 * total / len(times),
-        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
         "config": {"workload": workload_name, "sample_per_step": per_step, **cfg},
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port",
                          "sample": f"{per_step} sequences per step of the {workload_name} workload, FP32 oracle "
@@ -294,7 +295,6 @@ def main() -> int:
 
     from tiktoktechjam2026_b200 import B200Transformer, TransformerConfig, _lib
     from tiktoktechjam2026_b200.model import default_host_chunk
-    from tiktoktechjam2026_b200.sharding import shard_bounds
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -321,15 +321,18 @@ def main() -> int:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return float(t.item())
 
-    s0, s1 = shard_bounds(B, world, rank)
-    nb = s1 - s0
+    # Weak scaling: every rank runs the workload's whole batch as its shard of a
+    # global batch of B * world sequences (rank r holds sequences [r B, (r+1) B),
+    # drawn from seed SEED + r; rank 0's shard is the single-GPU input).
+    nb = B
+    global_batch = B * world
     torch.manual_seed(1234)
     model = B200Transformer(TransformerConfig(nb, S, D, H, F, L, causal)).to(dev).eval()
     model.convert_projections_to_fp16()
     model.assume_all_tokens_valid = pad <= 0
-    x_full, mask_full = make_inputs(cfg, pad, SEED)
-    x_host = x_full[s0:s1].contiguous().pin_memory()
-    mask_host = None if mask_full is None else mask_full[s0:s1].contiguous().pin_memory()
+    x_full, mask_full = make_inputs(cfg, pad, SEED + rank)
+    x_host = x_full.pin_memory()
+    mask_host = None if mask_full is None else mask_full.pin_memory()
     del x_full, mask_full
     out_host = torch.empty_like(x_host).pin_memory()
     x_dev = x_host.to(dev)
@@ -427,24 +430,25 @@ def main() -> int:
 
     if rank == 0:
         ms_per_step = total_ms / args.steps
-        value = B * 1000.0 / ms_per_step
-        e2e_value = B * 1000.0 / (e2e_ms / args.steps)
+        value = global_batch * 1000.0 / ms_per_step
+        e2e_value = global_batch * 1000.0 / (e2e_ms / args.steps)
         line = {
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "strong",
+            "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "f16 tensor-core operands, f32 accumulate/softmax/LayerNorm/residual",
             "data": "synthetic (x ~ N(0,1) FP32 from the reference's timing seed; seeded default-init weights)",
             "config": {"workload": f"{workload_name}: batch {B}, seq {S}, d_model {D}, heads {H}, ffn {F}, "
                                    f"layers {L}, causal{', key padding' if pad > 0 else ''}",
-                       "global_batch": B, "per_gpu_batch": nb, "seq_len": S, "d_model": D, "heads": H, "ffn": F,
-                       "layers": L, "parallelism": f"batch-sharded x{world}, no collective in the data path",
+                       "global_batch": global_batch, "per_gpu_batch": nb, "seq_len": S, "d_model": D, "heads": H,
+                       "ffn": F, "layers": L,
+                       "parallelism": f"batch-sharded x{world} ({nb} sequences per GPU), no collective in the data path",
                        "l2": "flushed between timed steps (256 MiB write, untimed)",
                        "launch": "one CUDA graph replay per step" if args.graph else "eager (one host call per step)"},
             "e2e": {"value": e2e_value, "unit": UNIT, "ms_per_step": e2e_ms / args.steps, "chunk": chunk,
                     "path": "model.forward_host -> tt_model_forward_host (pinned host in/out, copies overlapped "
                             "with compute by chunks)",
-                    "h2d_bytes_per_step": x_host.numel() * 4 + (0 if mask_host is None else mask_host.numel()),
-                    "d2h_bytes_per_step": out_host.numel() * 4},
+                    "h2d_bytes_per_step": world * (x_host.numel() * 4 + (0 if mask_host is None else mask_host.numel())),
+                    "d2h_bytes_per_step": world * out_host.numel() * 4},
             "gpu_launches": int(launches),
             "roofline": roof,
             "kernel_ms_per_step": {k: v[0] / args.steps for k, v in prof.items() if v[1] > 0},
