@@ -11,7 +11,7 @@ import pytest
 import torch
 import torch.nn.functional as F
 
-from tiktoktechjam2026_b200 import ops
+from tiktoktechjam2026_b200 import _lib, ops
 
 pytestmark = pytest.mark.gpu
 DEV = "cuda:0"
@@ -57,6 +57,21 @@ def test_qkv_projection(tt_lib, B, S, D, H):
     torch.testing.assert_close(vt[:, :, :hd, :S].float(), ref[2].transpose(-1, -2), rtol=2e-3, atol=4e-3)
     # head_dim 8 is stored 16 wide; the padding features of q and k are exact zeros.
     assert torch.all(q[..., hd:] == 0) and torch.all(k[..., hd:] == 0)
+
+
+def test_qkv_projection_rejects_misaligned_outputs(tt_lib):
+    """The epilogue stores 16-byte pieces: q/k/vt that are not 16-byte aligned are refused, not written."""
+    B, S, D, H = 1, 64, 128, 4
+    n = torch.zeros(B, S, D, dtype=torch.float16, device=DEV)
+    w = torch.zeros(3 * D, D, dtype=torch.float16, device=DEV)
+    b = torch.zeros(3 * D, device=DEV)
+    buf = torch.zeros(4 * B * S * D, dtype=torch.float16, device=DEV)
+    base = buf.data_ptr()
+    q, k, vt = base + 2, base + 2 * B * S * D + 256, base + 4 * B * S * D + 512
+    rc = tt_lib.tt_qkv_projection(n.data_ptr(), w.data_ptr(), b.data_ptr(), q, k, vt, B, S, D, H, S,
+                                  torch.cuda.current_stream(DEV).cuda_stream)
+    assert rc == _lib.TT_ERR_ALIGN
+    assert torch.all(buf == 0)
 
 
 def _attn_ref(q, k, vt, scale, causal, mask):

@@ -167,31 +167,6 @@ int encode_epi_tile(CUtensorMap* tm, const void* base, uint64_t rows, uint64_t c
                        base, 2, dims, strides, box);
 }
 
-// Store maps of the QKV epilogue: Q, K [B*H, S, hs] and V^T [B*H, hs, S_pad]
-// (hs = stored_head_dim(hd)).
-int encode_qkv_store_maps(CUtensorMap* tq, CUtensorMap* tk, CUtensorMap* tv, const void* q,
-                          const void* k, const void* vt, int bh, int seq, int hd_real, int seq_pad) {
-  const int hd = stored_head_dim(hd_real);
-  const uint32_t w = static_cast<uint32_t>(hd < 32 ? hd : 32);
-  {
-    const uint64_t dims[3] = {static_cast<uint64_t>(hd), static_cast<uint64_t>(seq),
-                              static_cast<uint64_t>(bh)};
-    const uint64_t strides[2] = {static_cast<uint64_t>(hd) * 2, static_cast<uint64_t>(hd) * seq * 2};
-    const uint32_t box[3] = {w, 32, 1};
-    if (int rc = encode_f16(tq, q, 3, dims, strides, box)) return rc;
-    if (int rc = encode_f16(tk, k, 3, dims, strides, box)) return rc;
-  }
-  {
-    const uint64_t dims[3] = {static_cast<uint64_t>(seq_pad), static_cast<uint64_t>(hd),
-                              static_cast<uint64_t>(bh)};
-    const uint64_t strides[2] = {static_cast<uint64_t>(seq_pad) * 2,
-                                 static_cast<uint64_t>(seq_pad) * hd * 2};
-    const uint32_t box[3] = {32, w, 1};
-    if (int rc = encode_f16(tv, vt, 3, dims, strides, box)) return rc;
-  }
-  return TT_OK;
-}
-
 template <typename K>
 int prepare_kernel(K kernel, int smem_bytes) {
   return check_cuda(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -584,7 +559,7 @@ struct tt_model {
   // Operand loads (box {KSW, 128}) and attention loads.
   CUtensorMap tm_norm{}, tm_ctx{}, tm_hidden{}, tm_q{}, tm_k{}, tm_vt{};
   // Epilogue tiles (box 32 x 32): QKV stores, residual (FP32), normalized and hidden (FP16).
-  CUtensorMap tm_q_st{}, tm_k_st{}, tm_vt_st{}, tm_resid{}, tm_norm_st{}, tm_hidden_st{};
+  CUtensorMap tm_resid{}, tm_norm_st{}, tm_hidden_st{};
   CUtensorMap tm_norm32{};  // normalized activations as the fused FFN's A operand (box {32, 128})
   CUtensorMap tm_norm3{};   // the same as whole 128-row K-block tiles (ffn2_kernel)
   // Profiling.
@@ -760,10 +735,6 @@ int bind_workspace(tt_model* m, int batch, int seq, void* ws, cudaStream_t strea
   if (int rc = encode_attention_maps(&m->tm_q, &m->tm_k, &m->tm_vt, base + w.q, base + w.k,
                                      base + w.vt, batch * m->H, seq, hd, w.seq_pad))
     return rc;
-  if (seq % 32 == 0)
-    if (int rc = encode_qkv_store_maps(&m->tm_q_st, &m->tm_k_st, &m->tm_vt_st, base + w.q, base + w.k,
-                                       base + w.vt, batch * m->H, seq, hd, w.seq_pad))
-      return rc;
   if (int rc = encode_epi_tile(&m->tm_resid, base + w.resid, N, m->D, true)) return rc;
   if (int rc = encode_epi_tile(&m->tm_norm_st, base + w.norm, N, m->D, false)) return rc;
   if (!m->route.ffn_fused)
@@ -869,10 +840,10 @@ int tt_qkv_projection(const void* normalized, const void* w_qkv, const float* b_
   if (int rc = encode_matrix(&maps.a, normalized, N, d_model, ksw, 128)) return rc;
   if (int rc = encode_matrix(&maps.w, w_qkv, 3 * d_model, d_model, ksw, bn)) return rc;
   const bool tma_out = seq % 32 == 0;
-  if (tma_out)
-    if (int rc = encode_qkv_store_maps(&maps.out0, &maps.out1, &maps.out2, q, k, vt, batch * heads, seq,
-                                       hd, seq_pad))
-      return rc;
+  // The epilogue writes Q, K and V^T in 16-byte pieces.
+  if (reinterpret_cast<uintptr_t>(q) % 16 || reinterpret_cast<uintptr_t>(k) % 16 ||
+      reinterpret_cast<uintptr_t>(vt) % 16)
+    return fail(TT_ERR_ALIGN, "q, k and vt must be 16-byte aligned");
   GemmParams p = base_params(ds);
   p.M = static_cast<int>(N);
   p.N_total = 3 * d_model;
@@ -1242,9 +1213,6 @@ int tt_model_forward(tt_model* m, const float* x, const uint8_t* mask, float* ou
       p.d_model = D;
       maps.a = m->tm_norm;
       maps.w = m->tm_wqkv[l];
-      maps.out0 = m->tm_q_st;
-      maps.out1 = m->tm_k_st;
-      maps.out2 = m->tm_vt_st;
       if (int rc = record_begin(m, s, &ev)) return rc;
       if (int rc = launch_gemm(m->ksw_qkv, EPI_QKV, maps, p, ds->sm_count, s)) return rc;
       if (int rc = record_end(m, s, TT_KERNEL_QKV, ev)) return rc;

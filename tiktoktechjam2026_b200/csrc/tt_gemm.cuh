@@ -8,25 +8,31 @@
 // generic configurations (mixed_precision/transformer.py:138-139, 669-677).
 //
 // Persistent kernel.  A work item is (128-row M tile, `bn`-column split);
-// CTA c takes items c, c + gridDim.x, ...  Roles:
-//   warp 4      TMA producer: (A, W) K-blocks through an `nst`-deep ring that
-//               runs continuously across items
-//   warp 5      TMEM allocator and single-thread tcgen05.mma issuer; the FP32
+// CTA c takes items c, c + gridDim.x, ...  Warps (NEPI = 4 for EPI_RESID_LN,
+// 8 otherwise):
+//   warps 0..NEPI-1  epilogue: warp e reads TMEM lane quadrant e % 4 (rows
+//               32(e%4)..+31 of the tile, one row per thread); with 8 warps
+//               the two warps of a quadrant split its 32-column chunks
+//   warp NEPI   first TMA producer; warps NEPI+2.. further producers: (A, W)
+//               K-blocks through an `nst`-deep ring that runs continuously
+//               across items, slot st always filled by producer
+//               st % kGemmProducers
+//   warp NEPI+1 TMEM allocator and single-thread tcgen05.mma issuer; the FP32
 //               accumulator is double buffered in TMEM (bn <= 256), so the
 //               MMAs of item i+1 overlap the epilogue of item i
-//   warps 0..3  epilogue: warp e owns rows 32e..32e+31 of the tile, one row
-//               per thread (TMEM lane = row), in 32-column chunks:
+// Epilogues, in 32-column chunks:
 //   EPI_QKV       + bias, FP16, to Q/K [B*H, S, hs] and V^T [B*H, hs, S_pad]
-//                 (hs = max(hd, 16); head_dim 8 is stored with 8 zero features)
+//                 (hs = max(hd, 16); head_dim 8 is stored with 8 zero
+//                 features); rows staged through shared memory and written
+//                 with coalesced 16-byte stores (one value per store when S is
+//                 not a multiple of 32)
 //   EPI_RESID_LN  + bias + FP32 residual -> residual out (FP32), then a
 //                 two-pass FP32 LayerNorm of the row (the row is kept in
 //                 TMEM between passes) -> FP16 or FP32, optionally zeroing
-//                 rows whose mask byte is 0
-//   EPI_GELU      + bias, exact-erf GELU in FP32, FP16 out
-// Epilogue inputs (the residual) arrive by TMA into a per-warp ring of
-// [32 rows x 32 col] tiles; outputs are staged in swizzled shared tiles and
-// written by TMA bulk stores, so HBM sees whole lines in both directions.
-// When S is not a multiple of 32 the QKV epilogue falls back to direct stores.
+//                 rows whose mask byte is 0; the residual arrives by TMA into
+//                 a per-warp ring of [32 rows x 32 col] tiles and the outputs
+//                 leave by TMA bulk stores from swizzled shared tiles
+//   EPI_GELU      + bias, exact-erf GELU in FP32, FP16 out (TMA bulk stores)
 #pragma once
 
 #include "tt_ptx.cuh"
@@ -46,7 +52,7 @@ struct GemmParams {
   int n_splits;  // N_total / bn
   int nst;       // pipeline depth
   int n_items;   // ceil(M / 128) * n_splits
-  int tma_out;   // QKV only: 1 = TMA stores (requires seq % 32 == 0)
+  int tma_out;   // QKV only: 1 = rows staged for coalesced stores (requires seq % 32 == 0)
   const float* bias;  // [N_total]
   // EPI_QKV
   __half* q;
@@ -64,14 +70,13 @@ struct GemmParams {
 };
 
 // Tensor maps of one GEMM launch.  `a`, `w`: operands (box {KSW, 128} and
-// {KSW, min(bn, 256)}).  Outputs/inputs of the epilogue, box 32 x 32:
-//   EPI_QKV       out0 = Q, out1 = K   [B*H, S, hd],   box {min(hd,32), 32, 1}
-//                 out2 = V^T [B*H, hd, S_pad],          box {32, min(hd,32), 1}
+// {KSW, min(bn, 256)}).  Outputs/inputs of the epilogue, box 32 x 32 (EPI_QKV
+// uses none: it stores through GemmParams' pointers):
 //   EPI_RESID_LN  out0 = residual out (FP32), out1 = normalized (FP16/FP32),
 //                 res  = residual in (FP32)
 //   EPI_GELU      out0 = activation (FP16)
 struct GemmMaps {
-  CUtensorMap a, w, out0, out1, out2, res;
+  CUtensorMap a, w, out0, out1, res;
 };
 
 __host__ __device__ inline int gemm_stage_bytes(int ksw, int bn) { return (128 + bn) * ksw * 2; }
