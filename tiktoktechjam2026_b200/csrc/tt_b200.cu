@@ -367,10 +367,16 @@ int encode_kblocks(CUtensorMap* tm, const void* base, uint64_t rows, uint64_t co
   return encode_f16(tm, base, 3, dims, strides, box);
 }
 
+// W1 of the fused FFN: one 32 KB ring slot is FC rows x W1_PER_SLOT K-blocks.
+int encode_ffn2_w1(CUtensorMap* tm, const void* w1, int D, int F) {
+  if (D == 256) return encode_kblocks(tm, w1, F, D, Ffn2Layout<256>::FC, Ffn2Layout<256>::W1_PER_SLOT);
+  return encode_kblocks(tm, w1, F, D, Ffn2Layout<128>::FC, Ffn2Layout<128>::W1_PER_SLOT);
+}
+
 int encode_ffn2_maps(Ffn2Maps* maps, const void* a, const void* w1, const void* w2, uint64_t rows, int D, int F) {
   memset(maps, 0, sizeof(*maps));
   if (int rc = encode_kblocks(&maps->a, a, rows, D, 128, D / 64)) return rc;
-  if (int rc = encode_kblocks(&maps->w1, w1, F, D, 128, 2)) return rc;
+  if (int rc = encode_ffn2_w1(&maps->w1, w1, D, F)) return rc;
   return encode_matrix(&maps->w2, w2, D, F, 64, D < 256 ? D : 256);
 }
 
@@ -708,7 +714,7 @@ int bind_workspace(tt_model* m, int batch, int seq, void* ws, cudaStream_t strea
         // The TMEM-hidden kernel (d_model 128/256) reads 64-wide K-blocks, the other one 32-wide.
         const bool f2 = ffn2_route(m->D, m->F);
         if (f2) {
-          if (int rc = encode_kblocks(&m->tm_w1f[l], w.w_ffn_in, m->F, m->D, 128, 2)) return rc;
+          if (int rc = encode_ffn2_w1(&m->tm_w1f[l], w.w_ffn_in, m->D, m->F)) return rc;
         } else if (int rc = encode_matrix(&m->tm_w1f[l], w.w_ffn_in, m->F, m->D, 32, 128)) {
           return rc;
         }

@@ -10,28 +10,30 @@
 // (mixed_precision/transformer.py:669-695), for F a multiple of 128.
 //
 // Persistent kernel over 128-row tiles; the hidden dimension runs in chunks
-// of FC = 128 units.  Per chunk c (buffer b = c & 1):
-//   G1(c)  acc1[b] (TMEM, 128 x 128 FP32) = A . W1[c]^T
+// of FC = 128 units (NACC1 = 256 / FC accumulator buffers).  Per chunk c
+// (buffer b = c % NACC1):
+//   G1(c)  acc1[b] (TMEM, 128 x FC FP32) = A . W1[c]^T
 //   GELU   8 warps: acc1[b] + b1 -> GELU -> FP16 pairs written back into the
 //          first half of each warp's own columns of acc1[b]: H(c) stays in
 //          TMEM and is the A operand of G2 (tcgen05.mma with A in TMEM)
 //   G2(c)  acc2 (TMEM, 128 x D FP32) += H(c) . W2[:, c]^T
-// issued in the order G1(0) G1(1) G2(0) G1(2) G2(1) ...; acc1[b] is rewritten
-// by G1(c+2) only after G2(c) has read H(c) (the tensor core executes one
-// thread's MMAs in issue order).  With H out of shared memory the weight ring
-// holds 4 x 32 KB (each slot one 32 KB TMA copy or two 16 KB copies): one
-// chunk's W1 and W2 blocks, so the next chunk's W1 streams in while G2 waits
-// for the GELU warps.
+// issued as G1(c) then G2(c - LAG) (LAG = 1: G1(0) G1(1) G2(0) G1(2) G2(1)
+// ...); acc1[b] is rewritten by G1(c + NACC1) only after G2(c) has read H(c)
+// (the tensor core executes one thread's MMAs in issue order; LAG < NACC1).
+// With H out of shared memory the weight ring holds NST = 3 slots of 32 KB,
+// each one TMA copy (W1: FC rows x the K-blocks that fill 32 KB, as a 3-D
+// K-block view; W2: 64 hidden units x D rows).
 //
 // Epilogue (4 warps, one row per thread): one TMEM pass computes
-// r' = acc2 + b2 + r (the residual rows prefetched by cp.async two 16-column
-// tiles ahead), accumulates shifted FP32 sums for the LayerNorm statistics and
-// writes r' with coalesced stores; acc2 is released right after that pass, so
-// the next tile's G2 starts while the second pass re-reads the warp's own r'
-// rows (L2 hits) and writes the normalized rows.  d_model 128 double-buffers
-// acc2 in TMEM.  Warp 12 loads A and the even ring slots, warp 14 the odd
-// ones (more producers: warps 14, 15, ... share the slots round-robin); warp
-// 13 allocates TMEM and issues the MMAs.
+// r' = acc2 + b2 + r (the residual rows bulk-prefetched into L2 a tile ahead,
+// then staged by cp.async AHEAD = 6 16-column jobs ahead), accumulates
+// shifted FP32 sums for the LayerNorm statistics and writes r' with coalesced
+// stores; acc2 is released right after that pass, so the next tile's G2
+// starts while the second pass re-reads the warp's own r' rows (L2 hits) and
+// writes the normalized rows.  d_model 128 double-buffers acc2 in TMEM.
+// Warp 12 loads A and the even ring slots, warp 14 the odd ones (more
+// producers: warps 14, 15, ... own slots st % producers); warp 13 allocates
+// TMEM and issues the MMAs.
 #pragma once
 
 #include "tt_ffn.cuh"
@@ -56,7 +58,16 @@ struct Ffn2Layout {
 #ifndef TT_FFN2_AHEAD
 #define TT_FFN2_AHEAD 6
 #endif
-  static constexpr int FC = 128, KB = 64, NST = TT_FFN2_NST, SLOT = 32768;
+#ifndef TT_FFN2_FC256
+#define TT_FFN2_FC256 128
+#endif
+#ifndef TT_FFN2_LAG256
+#define TT_FFN2_LAG256 1
+#endif
+  // Hidden units per chunk (d_model 256 may take 64), TMEM buffers of the
+  // chunk accumulator (columns 256..511), and how many chunks G2 trails G1.
+  static constexpr int FC = D == 256 ? TT_FFN2_FC256 : 128, KB = 64, NST = TT_FFN2_NST, SLOT = 32768;
+  static constexpr int NACC1 = 256 / FC, LAG = D == 256 ? TT_FFN2_LAG256 : 1;
   static constexpr int NKA = D / KB;                 // K-blocks of G1
   static constexpr int A_KBLK = 128 * KB * 2;        // 16 KB
   static constexpr int A_BYTES = NKA * A_KBLK;
@@ -76,12 +87,12 @@ struct Ffn2Layout {
   static constexpr int OFF_LN = OFF_W + NST * SLOT;
   static constexpr int OFF_F32 = OFF_LN + 4 * RING * TILE;  // b2, gamma, beta
   static constexpr int OFF_BAR = OFF_F32 + 3 * D * 4;
-  // a_full a_empty w_full[NST] w_empty[NST] acc1_full[2] h_full[2] acc2_full[2] acc2_empty[2] done
-  static constexpr int NBAR = 2 + 2 * NST + 8 + 1;
+  // a_full a_empty w_full[NST] w_empty[NST] acc1_full[NACC1] h_full[NACC1] acc2_full[2] acc2_empty[2] done
+  static constexpr int NBAR = 2 + 2 * NST + 2 * NACC1 + 4 + 1;
   static constexpr int OFF_MISC = OFF_BAR + NBAR * 8;
   static constexpr int SMEM_ALLOC = OFF_MISC + 16 + 1024;
   static constexpr int NACC2 = D <= 128 ? 2 : 1;  // acc2 buffers (TMEM columns [j * D, (j + 1) * D))
-  static constexpr int TMEM_ACC1 = 256;           // acc1 buffer b at columns 256 + 128 b
+  static constexpr int TMEM_ACC1 = 256;           // acc1 buffer b at columns 256 + FC b
   static_assert(D == 128 || D == 256, "this kernel covers d_model 128 and 256");
   static_assert(W1_SLOTS >= 1 && W2_SLOTS >= 1 && W1_PER_SLOT * W1_KBLK == SLOT && W2_PER_SLOT * W2_KBLK == SLOT,
                 "slot shapes");
@@ -89,6 +100,8 @@ struct Ffn2Layout {
   static_assert(OFF_W % 1024 == 0 && OFF_LN % 1024 == 0 && OFF_F32 % 16 == 0, "alignment");
   static_assert(SMEM_ALLOC <= 232448, "shared memory budget");
   static_assert(D / JW > AHEAD, "the re-read of an r' chunk must be issued after that chunk's store");
+  static_assert((FC == 64 || FC == 128) && LAG >= 1 && LAG < NACC1,
+                "G1(c) rewrites the buffer of H(c - NACC1), which G2 must have read: LAG < NACC1");
 };
 
 // Warp roles: 0..7 GELU (lane quadrant w & 3, hidden half w >> 2 of each
@@ -118,8 +131,8 @@ __global__ void __launch_bounds__(kFfn2Threads, 1)
   uint64_t* w_full = bars + 2;
   uint64_t* w_empty = w_full + NST;
   uint64_t* acc1_full = w_empty + NST;
-  uint64_t* h_full = acc1_full + 2;
-  uint64_t* acc2_full = h_full + 2;
+  uint64_t* h_full = acc1_full + L::NACC1;
+  uint64_t* acc2_full = h_full + L::NACC1;
   uint64_t* acc2_empty = acc2_full + 2;
   uint64_t* done = acc2_empty + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::OFF_MISC);
@@ -134,9 +147,11 @@ __global__ void __launch_bounds__(kFfn2Threads, 1)
       mbar_init(&w_full[i], 1);
       mbar_init(&w_empty[i], 1);
     }
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < L::NACC1; ++i) {
       mbar_init(&acc1_full[i], 1);
       mbar_init(&h_full[i], 8);
+    }
+    for (int i = 0; i < 2; ++i) {
       mbar_init(&acc2_full[i], 1);
       mbar_init(&acc2_empty[i], 4);
     }
@@ -203,11 +218,11 @@ __global__ void __launch_bounds__(kFfn2Threads, 1)
                              static_cast<uint32_t>(rows) * D * 4u);
           }
         }
-        for (int step = 0; ok && step <= nchunk; ++step) {
+        for (int step = 0; ok && step < nchunk + L::LAG; ++step) {
           if (step < nchunk)
             for (int s = 0; ok && s < L::W1_SLOTS; ++s) ok = slot_load(false, step, s);
-          if (step >= 1)
-            for (int s = 0; ok && s < L::W2_SLOTS; ++s) ok = slot_load(true, step - 1, s);
+          if (step >= L::LAG)
+            for (int s = 0; ok && s < L::W2_SLOTS; ++s) ok = slot_load(true, step - L::LAG, s);
         }
       }
       if (pidx == 0 && i > 0) wait_drain(a_full, (i - 1) & 1, kDrainLimitNs);
@@ -227,11 +242,11 @@ __global__ void __launch_bounds__(kFfn2Threads, 1)
         const int ib = i % L::NACC2;
         const uint32_t tacc2 = tmem_base + ib * D;
         if (!(ok = wait_phase(a_full, i & 1, wd, 0x611))) break;
-        for (int step = 0; ok && step <= nchunk; ++step) {
+        for (int step = 0; ok && step < nchunk + L::LAG; ++step) {
           if (step < nchunk) {
-            // G1(step) -> acc1[c & 1].  Its previous contents, H(c - 2), were
-            // read by G2(c - 2), issued before this MMA.
-            const int c = cg + step, ab = c & 1;
+            // G1(step) -> acc1[c % NACC1].  Its previous contents, H(c - NACC1),
+            // were read by G2(c - NACC1), issued before this MMA (LAG < NACC1).
+            const int c = cg + step, ab = c % L::NACC1;
             const uint32_t tacc1 = tmem_base + L::TMEM_ACC1 + ab * FC;
             for (int s = 0; ok && s < L::W1_SLOTS; ++s, ++g) {
               const int st = g % NST;
@@ -253,12 +268,12 @@ __global__ void __launch_bounds__(kFfn2Threads, 1)
             umma_commit(&acc1_full[ab]);
             if (step == nchunk - 1) umma_commit(a_empty);
           }
-          if (step >= 1) {
-            // G2(step - 1): acc2 += H(c) . W2[:, chunk c]^T with H(c) in TMEM.
-            const int c = cg + step - 1, hb = c & 1;
+          if (step >= L::LAG) {
+            // G2(step - LAG): acc2 += H(c) . W2[:, chunk c]^T with H(c) in TMEM.
+            const int c = cg + step - L::LAG, hb = c % L::NACC1;
             const uint32_t th = tmem_base + L::TMEM_ACC1 + hb * FC;
-            if (step == 1 && !(ok = wait_phase(&acc2_empty[ib], ((i / L::NACC2) & 1) ^ 1, wd, 0x613))) break;
-            if (!(ok = wait_phase(&h_full[hb], (c >> 1) & 1, wd, 0x614))) break;
+            if (step == L::LAG && !(ok = wait_phase(&acc2_empty[ib], ((i / L::NACC2) & 1) ^ 1, wd, 0x613))) break;
+            if (!(ok = wait_phase(&h_full[hb], (c / L::NACC1) & 1, wd, 0x614))) break;
             tc_fence_after();
             for (int s = 0; ok && s < L::W2_SLOTS; ++s, ++g) {
               const int st = g % NST;
@@ -269,15 +284,18 @@ __global__ void __launch_bounds__(kFfn2Threads, 1)
                 const int hk = s * L::W2_PER_SLOT + q;  // 64-unit hidden block of the chunk
 #pragma unroll
                 for (int kk = 0; kk < L::KB / 16; ++kk) {
-                  // Hidden units hk*64 + 16kk .. +15 sit in columns hk*64 + 8kk .. +7 (packed pairs).
+                  // Hidden units 16u .. 16u+15 of the chunk (u = 4hk + kk) were packed by GELU
+                  // warp u / (FC/32) into columns (u % (FC/32)) * 8 .. +7 of its FC/2 columns.
+                  const int u = hk * 4 + kk;
+                  const uint32_t ta = th + (u / (FC / 32)) * (FC / 2) + (u % (FC / 32)) * 8;
                   const uint64_t db = umma_sdesc(sW + st * L::SLOT + q * L::W2_KBLK + kk * 32, 1024, kSw128);
-                  umma_f16_ts(tacc2, th + hk * 64 + kk * 8, db, idesc2, (step > 1 || hk > 0 || kk > 0) ? 1u : 0u);
+                  umma_f16_ts(tacc2, ta, db, idesc2, (step > L::LAG || hk > 0 || kk > 0) ? 1u : 0u);
                 }
               }
               umma_commit(&w_empty[st]);
             }
             if (!ok) break;
-            if (step == nchunk) umma_commit(&acc2_full[ib]);
+            if (step == nchunk + L::LAG - 1) umma_commit(&acc2_full[ib]);
           }
         }
         cg += nchunk;
@@ -288,24 +306,25 @@ __global__ void __launch_bounds__(kFfn2Threads, 1)
   } else if (warp < 8) {
     // ------------------------------------------------------------ GELU warps
     const int gq = warp & 3, gh = warp >> 2;
-    const uint32_t tbase = tmem_base + (static_cast<uint32_t>(gq * 32) << 16) + L::TMEM_ACC1 + gh * 64;
+    constexpr int GW = FC / 2;  // accumulator columns (hidden units) per GELU warp and chunk
+    const uint32_t tbase = tmem_base + (static_cast<uint32_t>(gq * 32) << 16) + L::TMEM_ACC1 + gh * GW;
     int cg = 0;
     bool ok = true;
     for (int w = blockIdx.x; ok && w < p.n_items; w += gridDim.x) {
       for (int cc = 0; cc < nchunk; ++cc) {
-        const int c = cg + cc, ab = c & 1;
-        if (!(ok = warp_wait_phase(&acc1_full[ab], (c >> 1) & 1, wd, 0x621))) break;
+        const int c = cg + cc, ab = c % L::NACC1;
+        if (!(ok = warp_wait_phase(&acc1_full[ab], (c / L::NACC1) & 1, wd, 0x621))) break;
         tc_fence_after();
-        uint32_t v[2][32];
+        uint32_t v[GW / 32][32];
         const uint32_t tsrc = tbase + ab * FC;
-        tmem_ld_x32(tsrc, v[0]);
-        tmem_ld_x32(tsrc + 32, v[1]);
-        tmem_ld_wait_tied(v[0]);
-        tmem_ld_wait_tied(v[1]);
-        const float4* b4 = reinterpret_cast<const float4*>(p.b1 + cc * FC + gh * 64);
-        uint32_t pk[32];
 #pragma unroll
-        for (int e = 0; e < 16; ++e) {
+        for (int h = 0; h < GW / 32; ++h) tmem_ld_x32(tsrc + 32 * h, v[h]);
+#pragma unroll
+        for (int h = 0; h < GW / 32; ++h) tmem_ld_wait_tied(v[h]);
+        const float4* b4 = reinterpret_cast<const float4*>(p.b1 + cc * FC + gh * GW);
+        uint32_t pk[GW / 2];
+#pragma unroll
+        for (int e = 0; e < GW / 4; ++e) {
           const float4 bb = __ldg(b4 + e);  // the same address in every lane: one broadcast load
           const uint32_t* x = &v[e >> 3][(e & 7) * 4];
           const uint64_t h01 = gelu_erf_pair(
@@ -315,8 +334,12 @@ __global__ void __launch_bounds__(kFfn2Threads, 1)
           pk[2 * e] = pack_half2(f2_lo(h01), f2_hi(h01));
           pk[2 * e + 1] = pack_half2(f2_lo(h23), f2_hi(h23));
         }
-        // H (64 hidden units = 32 packed columns) over the first half of this warp's columns.
-        tmem_st_x32(tsrc, pk);
+        // H (GW hidden units = GW/2 packed columns) over the first half of this warp's columns.
+        if constexpr (GW == 64) {
+          tmem_st_x32(tsrc, pk);
+        } else {
+          tmem_st_x16(tsrc, pk);
+        }
         tmem_st_wait();
         tc_fence_before();
         __syncwarp();
