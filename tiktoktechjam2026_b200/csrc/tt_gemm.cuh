@@ -26,9 +26,10 @@
 //                 features); rows staged through shared memory and written
 //                 with coalesced 16-byte stores (one value per store when S is
 //                 not a multiple of 32)
-//   EPI_RESID_LN  + bias + FP32 residual -> residual out (FP32), then a
-//                 two-pass FP32 LayerNorm of the row (the row is kept in
-//                 TMEM between passes) -> FP16 or FP32, optionally zeroing
+//   EPI_RESID_LN  + bias + FP32 residual -> residual out (FP32) and FP32
+//                 shifted sums for the LayerNorm statistics in one TMEM pass
+//                 (the row is written back into TMEM), then the normalized row
+//                 in a second pass -> FP16 or FP32, optionally zeroing
 //                 rows whose mask byte is 0; the residual arrives by TMA into
 //                 a per-warp ring of [32 rows x 32 col] tiles and the outputs
 //                 leave by TMA bulk stores from swizzled shared tiles
@@ -546,12 +547,23 @@ __global__ void __launch_bounds__(gemm_threads(EPI), 1)
         }
       } else {
         // EPI_RESID_LN: bn == N_total == d_model (the whole row lives in TMEM).
+        // Pass 1 (two chunks per TMEM wait): r' = acc + bias + residual, written
+        // back into TMEM and out to HBM, with FP32 sums of r' - shift (shift =
+        // the row's first r') for the mean and variance; pass 2 normalizes.
         const int D = bn;
-        float sum = 0.f;
-        for (int c = 0; c < nch; ++c) {
-          uint32_t v[32];
+        float shift = 0.f, s1 = 0.f, s2 = 0.f;
+        for (int cb = 0; cb < nch; cb += 2) {
+          uint32_t vv[2][32];
           __syncwarp();
-          tmem_ld_x32_sync(taddr + c * 32, v);
+          tmem_ld_x32(taddr + cb * 32, vv[0]);
+          if (cb + 1 < nch) tmem_ld_x32(taddr + (cb + 1) * 32, vv[1]);
+          tmem_ld_wait_tied(vv[0]);
+          tmem_ld_wait_tied(vv[1]);
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {
+          const int c = cb + u;
+          if (c >= nch) break;
+          const uint32_t (&v)[32] = vv[u];
           float res[32];
           const int q = res_g + c;
           if (warp_active) {
@@ -578,8 +590,13 @@ __global__ void __launch_bounds__(gemm_threads(EPI), 1)
             rr[e] = __uint_as_float(v[e]) + s_bias[c * 32 + e] + res[e];
             out[e] = __float_as_uint(rr[e]);
           }
+          if (c == 0) shift = rr[0];
 #pragma unroll
-          for (int e = 0; e < 32; e += 4) sum += (rr[e] + rr[e + 1]) + (rr[e + 2] + rr[e + 3]);
+          for (int e = 0; e < 32; ++e) {
+            const float d = rr[e] - shift;
+            s1 += d;
+            s2 = fmaf(d, d, s2);
+          }
           __syncwarp();
           tmem_st_x32(taddr + c * 32, out);
           if (warp_active) {
@@ -592,30 +609,15 @@ __global__ void __launch_bounds__(gemm_threads(EPI), 1)
             }
           }
         }
+          if (!ok) break;
+        }
         if (!ok) break;
         if (warp_active) res_g += nch;
         tmem_st_wait();
-        const float mean = sum / static_cast<float>(D);
-        float sq = 0.f;
-        for (int cb = 0; cb < nch; cb += 4) {
-          uint32_t vv[4][32];
-          __syncwarp();
-#pragma unroll
-          for (int u = 0; u < 4; ++u)
-            if (cb + u < nch) tmem_ld_x32(taddr + (cb + u) * 32, vv[u]);
-#pragma unroll
-          for (int u = 0; u < 4; ++u) tmem_ld_wait_tied(vv[u]);
-#pragma unroll
-          for (int u = 0; u < 4; ++u) {
-            if (cb + u >= nch) break;
-#pragma unroll
-            for (int e = 0; e < 32; ++e) {
-              const float d = __uint_as_float(vv[u][e]) - mean;
-              sq = fmaf(d, d, sq);
-            }
-          }
-        }
-        const float rstd = rsqrtf(sq / static_cast<float>(D) + p.eps);
+        const float inv_d = 1.f / static_cast<float>(D);
+        const float m1 = s1 * inv_d;
+        const float mean = shift + m1;
+        const float rstd = rsqrtf(fmaxf(s2 * inv_d - m1 * m1, 0.f) + p.eps);
         const bool zero_row = valid && p.row_mask != nullptr && p.row_mask[row] == 0;
         for (int cb = 0; cb < nch; cb += 2) {
           uint32_t vv[2][32];
