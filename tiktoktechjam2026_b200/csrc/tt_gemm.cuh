@@ -337,7 +337,8 @@ __global__ void __launch_bounds__(gemm_threads(EPI), 1)
     const uint32_t res_base = smem_u32(epi) + warp * (kRes + kOutRing) * kEpiTile;
     OutRing ring{res_base + kRes * kEpiTile, 0};
     uint64_t* my_res_full = res_full + warp * kResRing;
-    int res_g = 0;  // residual tiles this warp has requested and consumed
+    int res_g = 0;         // residual tiles this warp has requested and consumed
+    bool res_pre = false;  // this item's first residual tiles already went out
     int i = 0;
     bool ok = true;
     for (int w = blockIdx.x; ok && w < p.n_items; w += gridDim.x, ++i) {
@@ -348,9 +349,10 @@ __global__ void __launch_bounds__(gemm_threads(EPI), 1)
       const bool valid = row < p.M;
       const bool warp_active = r0 < p.M;
       const int nch = bn / 32;
-      // Residual tiles of this item: the first kResRing go out now.
+      // Residual tiles of this item: the first kResRing go out now, unless the
+      // previous item sent them during its normalization pass.
       if constexpr (EPI == EPI_RESID_LN) {
-        if (lane == 0 && warp_active) {
+        if (lane == 0 && warp_active && !res_pre) {
           for (int c = 0; c < nch && c < kResRing; ++c) {
             const int q = res_g + c;
             mbar_arrive_expect_tx(&my_res_full[q % kResRing], kEpiTile);
@@ -613,6 +615,24 @@ __global__ void __launch_bounds__(gemm_threads(EPI), 1)
         }
         if (!ok) break;
         if (warp_active) res_g += nch;
+        // The ring is free until the next item: send that item's first residual
+        // tiles now, so that they land while this item is normalized.
+        res_pre = false;
+        if (const int wn = w + static_cast<int>(gridDim.x); wn < p.n_items) {
+          const int r0n = (wn / p.n_splits) * 128 + eq * 32;
+          if (r0n < p.M) {
+            if (lane == 0) {
+              fence_proxy_async_smem();
+              for (int c = 0; c < nch && c < kResRing; ++c) {
+                const int q = res_g + c;
+                mbar_arrive_expect_tx(&my_res_full[q % kResRing], kEpiTile);
+                tma_load_2d_u32(res_base + (q % kResRing) * kEpiTile, &maps.res, &my_res_full[q % kResRing],
+                                (wn % p.n_splits) * bn + 32 * c, r0n);
+              }
+            }
+            res_pre = true;
+          }
+        }
         tmem_st_wait();
         const float inv_d = 1.f / static_cast<float>(D);
         const float m1 = s1 * inv_d;
