@@ -322,7 +322,7 @@ __global__ void __launch_bounds__(kFfnThreads, 1)
     const int ew = warp - 8;  // TMEM lane quadrant
     const uint32_t lane_base = static_cast<uint32_t>(ew * 32) << 16;
     const uint32_t taddr = tmem_base + lane_base;
-    OutRing ring{smem_u32(smem + L::OFF_EPI) + ew * 2 * kEpiTile, 0};
+    OutRing<2> ring{smem_u32(smem + L::OFF_EPI) + ew * 2 * kEpiTile, 0};
     constexpr int nch = D / 32;
     int i = 0;
     bool ok = true;
