@@ -8,8 +8,7 @@
 // generic configurations (mixed_precision/transformer.py:138-139, 669-677).
 //
 // Persistent kernel.  A work item is (128-row M tile, `bn`-column split);
-// CTA c takes items c, c + gridDim.x, ...  Warps (NEPI = 4 for EPI_RESID_LN,
-// 8 otherwise):
+// CTA c takes items c, c + gridDim.x, ...  Warps (NEPI = 8):
 //   warps 0..NEPI-1  epilogue: warp e reads TMEM lane quadrant e % 4 (rows
 //               32(e%4)..+31 of the tile, one row per thread); with 8 warps
 //               the two warps of a quadrant split its 32-column chunks
@@ -28,8 +27,10 @@
 //                 not a multiple of 32)
 //   EPI_RESID_LN  + bias + FP32 residual -> residual out (FP32) and FP32
 //                 shifted sums for the LayerNorm statistics in one TMEM pass
-//                 (the row is written back into TMEM), then the normalized row
-//                 in a second pass -> FP16 or FP32, optionally zeroing
+//                 (the row is written back into TMEM); the quadrant's two
+//                 warps swap (mean, M2) of their column halves through shared
+//                 memory; then the normalized row in a second pass -> FP16 or
+//                 FP32, optionally zeroing
 //                 rows whose mask byte is 0; the residual arrives by TMA into
 //                 a per-warp ring of [32 rows x 32 col] tiles and the outputs
 //                 leave by TMA bulk stores from swizzled shared tiles
@@ -43,7 +44,19 @@ namespace tt {
 enum GemmEpilogue : int { EPI_QKV = 0, EPI_RESID_LN = 1, EPI_GELU = 2 };
 
 constexpr int kGemmMaxStages = 8;
-constexpr int kResRing = 3;   // residual tiles in flight per epilogue warp (EPI_RESID_LN)
+// EPI_RESID_LN with TT_LN_SPLIT (the default): two epilogue warps per TMEM
+// lane quadrant, each on half of the row's columns, the row statistics
+// combined through shared memory (C5 out-proj 1.27 -> 1.08 ms per forward
+// against one warp per quadrant).
+#ifndef TT_LN_SPLIT
+#define TT_LN_SPLIT 1
+#endif
+#ifndef TT_LN_SPLIT_RES
+#define TT_LN_SPLIT_RES 2
+#endif
+constexpr bool kLnSplit = TT_LN_SPLIT != 0;
+// Residual tiles in flight per epilogue warp (EPI_RESID_LN).
+constexpr int kResRing = kLnSplit ? TT_LN_SPLIT_RES : 3;
 constexpr int kEpiTile = 4096;  // one [32 x 32] FP32 tile
 
 struct GemmParams {
@@ -87,10 +100,10 @@ __host__ __device__ inline int gemm_acc_stride(int bn) {
 }
 __host__ __device__ inline int gemm_n_acc(int bn) { return bn <= 256 ? 2 : 1; }
 __host__ __device__ inline int gemm_tmem_cols(int bn) { return gemm_n_acc(bn) * gemm_acc_stride(bn); }
-// Epilogue warps: the LayerNorm epilogue keeps a whole row per thread (4 warps,
-// one per TMEM lane quadrant); the others pair two warps on each quadrant and
-// split its columns, so every SM sub-partition has two epilogue warps.
-__host__ __device__ constexpr int gemm_epi_warps(int epi) { return epi == EPI_RESID_LN ? 4 : 8; }
+// Epilogue warps: two on each TMEM lane quadrant, splitting its columns, so
+// every SM sub-partition has two epilogue warps (the LayerNorm epilogue keeps
+// a whole row per thread, 4 warps, when built without TT_LN_SPLIT).
+__host__ __device__ constexpr int gemm_epi_warps(int epi) { return epi == EPI_RESID_LN && !kLnSplit ? 4 : 8; }
 // Warps: epilogue warps, then the first TMA producer, the MMA issuer and
 // kGemmProducers - 1 more producers.  Ring slot st is always filled by
 // producer st % kGemmProducers: one producer per slot keeps the parity-based
@@ -114,8 +127,9 @@ __host__ __device__ inline int gemm_smem_bytes(int ksw, int bn, int nst, int epi
   int off = nst * gemm_stage_bytes(ksw, bn);
   off += gemm_epi_bytes(epi);
   off += (n_total + 2 * bn) * 4;
-  off += (2 * kGemmMaxStages + 5 + 4 * kResRing + 1) * 8;
+  off += (2 * kGemmMaxStages + 5 + 8 * kResRing + 4 + 1) * 8;
   off += 16;
+  off += 2 * 4 * 2 * 2 * 32 * 4;  // row-statistics exchange of the split LayerNorm epilogue
   return off + 1024;
 }
 
@@ -228,10 +242,13 @@ __global__ void __launch_bounds__(gemm_threads(EPI), 1)
   uint64_t* empty = full + kGemmMaxStages;
   uint64_t* acc_full = empty + kGemmMaxStages;
   uint64_t* acc_empty = acc_full + 2;
-  uint64_t* res_full = acc_empty + 2;  // [4 warps][kResRing]
-  uint64_t* done = res_full + 4 * kResRing;
+  uint64_t* res_full = acc_empty + 2;  // [epilogue warp][kResRing]
+  uint64_t* xbar = res_full + 8 * kResRing;  // [lane quadrant]: statistics exchange (split LN)
+  uint64_t* done = xbar + 4;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  // [item parity][quadrant][column half][mean, M2][lane]
+  float* xch = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(done + 1) + 16);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nk = p.K / KSW;
@@ -248,7 +265,8 @@ __global__ void __launch_bounds__(gemm_threads(EPI), 1)
       mbar_init(&acc_full[i], 1);
       mbar_init(&acc_empty[i], NEPI);
     }
-    for (int i = 0; i < 4 * kResRing; ++i) mbar_init(&res_full[i], 1);
+    for (int i = 0; i < NEPI * kResRing; ++i) mbar_init(&res_full[i], 1);
+    for (int i = 0; i < 4; ++i) mbar_init(&xbar[i], 2);
     mbar_init(done, 1);
     *abort_flag = 0;
     fence_mbar_init();
@@ -354,15 +372,19 @@ __global__ void __launch_bounds__(gemm_threads(EPI), 1)
       const bool valid = row < p.M;
       const bool warp_active = r0 < p.M;
       const int nch = bn / 32;
+      // EPI_RESID_LN: this warp's 32-column chunks [c_lo, c_hi) (half of them
+      // with the split epilogue, where the pair of a quadrant shares a row).
+      const int c_lo = NSTEP == 2 ? ehalf * nch / 2 : 0;
+      const int c_hi = NSTEP == 2 ? (ehalf + 1) * nch / 2 : nch;
       // Residual tiles of this item: the first kResRing go out now, unless the
       // previous item sent them during its normalization pass.
       if constexpr (EPI == EPI_RESID_LN) {
         if (lane == 0 && warp_active && !res_pre) {
-          for (int c = 0; c < nch && c < kResRing; ++c) {
-            const int q = res_g + c;
+          for (int k = 0; c_lo + k < c_hi && k < kResRing; ++k) {
+            const int q = res_g + k;
             mbar_arrive_expect_tx(&my_res_full[q % kResRing], kEpiTile);
             tma_load_2d_u32(res_base + (q % kResRing) * kEpiTile, &maps.res, &my_res_full[q % kResRing],
-                            n0 + 32 * c, r0);
+                            n0 + 32 * (c_lo + k), r0);
           }
         }
       }
@@ -559,27 +581,27 @@ __global__ void __launch_bounds__(gemm_threads(EPI), 1)
         // the row's first r') for the mean and variance; pass 2 normalizes.
         const int D = bn;
         float shift = 0.f, s1 = 0.f, s2 = 0.f;
-        for (int cb = 0; cb < nch; cb += 2) {
+        for (int cb = c_lo; cb < c_hi; cb += 2) {
           uint32_t vv[2][32];
           __syncwarp();
           tmem_ld_x32(taddr + cb * 32, vv[0]);
-          if (cb + 1 < nch) tmem_ld_x32(taddr + (cb + 1) * 32, vv[1]);
+          if (cb + 1 < c_hi) tmem_ld_x32(taddr + (cb + 1) * 32, vv[1]);
           tmem_ld_wait_tied(vv[0]);
           tmem_ld_wait_tied(vv[1]);
 #pragma unroll
         for (int u = 0; u < 2; ++u) {
           const int c = cb + u;
-          if (c >= nch) break;
+          if (c >= c_hi) break;
           const uint32_t (&v)[32] = vv[u];
           float res[32];
-          const int q = res_g + c;
+          const int q = res_g + (c - c_lo);
           if (warp_active) {
             if (!(ok = warp_wait_phase(&my_res_full[q % kResRing], (q / kResRing) & 1, wd, 0x405)))
               break;
             load_row_f32(res_base + (q % kResRing) * kEpiTile, r, res);
             __syncwarp();
             // The slot is read; refill it with the tile kResRing chunks ahead.
-            if (lane == 0 && c + kResRing < nch) {
+            if (lane == 0 && c + kResRing < c_hi) {
               fence_proxy_async_smem();
               const int q2 = q + kResRing;
               mbar_arrive_expect_tx(&my_res_full[q2 % kResRing], kEpiTile);
@@ -597,7 +619,7 @@ __global__ void __launch_bounds__(gemm_threads(EPI), 1)
             rr[e] = __uint_as_float(v[e]) + s_bias[c * 32 + e] + res[e];
             out[e] = __float_as_uint(rr[e]);
           }
-          if (c == 0) shift = rr[0];
+          if (c == c_lo) shift = rr[0];
 #pragma unroll
           for (int e = 0; e < 32; ++e) {
             const float d = rr[e] - shift;
@@ -619,7 +641,7 @@ __global__ void __launch_bounds__(gemm_threads(EPI), 1)
           if (!ok) break;
         }
         if (!ok) break;
-        if (warp_active) res_g += nch;
+        if (warp_active) res_g += c_hi - c_lo;
         // The ring is free until the next item: send that item's first residual
         // tiles now, so that they land while this item is normalized.
         res_pre = false;
@@ -628,34 +650,71 @@ __global__ void __launch_bounds__(gemm_threads(EPI), 1)
           if (r0n < p.M) {
             if (lane == 0) {
               fence_proxy_async_smem();
-              for (int c = 0; c < nch && c < kResRing; ++c) {
-                const int q = res_g + c;
+              for (int k = 0; c_lo + k < c_hi && k < kResRing; ++k) {
+                const int q = res_g + k;
                 mbar_arrive_expect_tx(&my_res_full[q % kResRing], kEpiTile);
                 tma_load_2d_u32(res_base + (q % kResRing) * kEpiTile, &maps.res, &my_res_full[q % kResRing],
-                                (wn % p.n_splits) * bn + 32 * c, r0n);
+                                (wn % p.n_splits) * bn + 32 * (c_lo + k), r0n);
               }
             }
             res_pre = true;
           }
         }
         tmem_st_wait();
-        const float inv_d = 1.f / static_cast<float>(D);
-        const float m1 = s1 * inv_d;
-        const float mean = shift + m1;
-        const float rstd = rsqrtf(fmaxf(s2 * inv_d - m1 * m1, 0.f) + p.eps);
+        // Row statistics: this warp's columns give (count, mean, M2) from the
+        // shifted sums; with the split epilogue the two warps of the quadrant
+        // swap theirs through shared memory and both combine them in column
+        // order (half 0, then half 1), so that they normalize with identical
+        // values.
+        float mean, rstd;
+        {
+          const int n_mine = 32 * (c_hi - c_lo);
+          float mean_a = 0.f, m2_a = 0.f;
+          if (n_mine > 0) {
+            const float inv = 1.f / static_cast<float>(n_mine);
+            mean_a = shift + s1 * inv;
+            m2_a = fmaxf(s2 - s1 * s1 * inv, 0.f);
+          }
+          int n_a = n_mine, n_b = 0;
+          float mean_b = 0.f, m2_b = 0.f;
+          if constexpr (NSTEP == 2) {
+            float* xs = xch + ((i & 1) * 4 + eq) * 128;  // [half][mean, M2][lane]
+            xs[ehalf * 64 + lane] = mean_a;
+            xs[ehalf * 64 + 32 + lane] = m2_a;
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&xbar[eq]);
+            // Slot (i & 1) is rewritten at item i + 2, after both warps have
+            // passed item i + 1's exchange, so the partner's values stay put.
+            if (!(ok = warp_wait_phase(&xbar[eq], i & 1, wd, 0x406))) break;
+            const int oh = ehalf ^ 1;
+            const float mean_o = xs[oh * 64 + lane], m2_o = xs[oh * 64 + 32 + lane];
+            const int n_o = 32 * ((oh + 1) * nch / 2 - oh * nch / 2);
+            if (ehalf == 0) {
+              mean_b = mean_o, m2_b = m2_o, n_b = n_o;
+            } else {
+              mean_b = mean_a, m2_b = m2_a, n_b = n_mine;
+              mean_a = mean_o, m2_a = m2_o, n_a = n_o;
+            }
+          }
+          const float fb = static_cast<float>(n_b) / static_cast<float>(n_a + n_b);
+          const float delta = mean_b - mean_a;
+          mean = fmaf(delta, fb, mean_a);
+          const float m2 = m2_a + m2_b + delta * delta * static_cast<float>(n_a) * fb;
+          rstd = rsqrtf(fmaxf(m2 / static_cast<float>(D), 0.f) + p.eps);
+        }
         const bool zero_row = valid && p.row_mask != nullptr && p.row_mask[row] == 0;
-        for (int cb = 0; cb < nch; cb += 2) {
+        for (int cb = c_lo; cb < c_hi; cb += 2) {
           uint32_t vv[2][32];
           __syncwarp();
           tmem_ld_x32(taddr + cb * 32, vv[0]);
-          if (cb + 1 < nch) tmem_ld_x32(taddr + (cb + 1) * 32, vv[1]);
+          if (cb + 1 < c_hi) tmem_ld_x32(taddr + (cb + 1) * 32, vv[1]);
           tmem_ld_wait_tied(vv[0]);
           tmem_ld_wait_tied(vv[1]);
           if (!warp_active) continue;
 #pragma unroll
         for (int u = 0; u < 2; ++u) {
           const int c = cb + u;
-          if (c >= nch) break;
+          if (c >= c_hi) break;
           const uint32_t (&v)[32] = vv[u];
           float y[32];
 #pragma unroll
