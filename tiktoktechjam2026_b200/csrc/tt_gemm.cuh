@@ -223,6 +223,7 @@ __global__ void __launch_bounds__(gemm_threads(EPI), 1)
     gemm_kernel(const __grid_constant__ GemmMaps maps, const GemmParams p) {
   constexpr int NEPI = gemm_epi_warps(EPI);  // epilogue warps 0..NEPI-1
   constexpr int NSTEP = NEPI / 4;            // warps sharing one TMEM lane quadrant
+  static_assert(NEPI == 4 || NEPI == 8, "residual barriers and the statistics exchange assume 4 or 8 epilogue warps");
   constexpr int W_PROD = NEPI, W_MMA = NEPI + 1;  // further producers: warps NEPI + 2 ...
   constexpr int A_BYTES = 128 * KSW * 2;
   constexpr uint32_t kSw = swizzle_kind_for_bytes(KSW * 2);
