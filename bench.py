@@ -2,22 +2,32 @@
 """Benchmark of the B200 forward pass (one JSON line on rank 0).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--config C5] [--impl b200|reference]
+                    [--scaling strong|weak]
 
 Workload: BASELINE configuration C5 by default (batch 512, seq 1024,
 d_model 256, 8 heads, ffn 1024, 4 layers, causal), the configuration the
-metric's 1/2/4/8-GPU clause is quoted on.  Weak scaling: each of the N ranks
-(one process per GPU, launched by torchrun for N > 1) runs that whole batch as
-its shard of a global batch of N times as many sequences, with no collective
-in the data path.  A step is one forward of this rank's shard.
+metric's 1/2/4/8-GPU clause is quoted on.  One process per GPU (torchrun for
+N > 1).  Strong scaling (default): the one batch of 512 sequences is split
+into contiguous slices (sharding.shard_bounds, 64 per GPU at N = 8), every
+rank runs its slice, and every slice's FP32 output is pushed into one gather
+buffer on GPU 0 (tt_model_forward_gather: NVLink copies on the copy engines,
+each overlapped with the next step's compute).  A step is one forward of this
+rank's slice plus its push.
 
   value  device-resident inputs; per step: L2 flush (256 MiB write, untimed),
-         CUDA events around the forward; max over ranks of the summed step
-         times; sequences/s of the whole job.
+         CUDA events around the forward and its push; after the last step the
+         wait for the last push is timed too; max over ranks of the summed
+         times; sequences/s of the whole batch.  compute_only (no push),
+         latency_ms (one step with its push waited for) and weak (every rank a
+         whole batch of its own, nothing gathered) are reported beside it, and
+         gather_check says whether rank 0's gathered batch equals, bit for bit,
+         its own 1-GPU forward of the whole batch.
   e2e    same metric through the public model call with host buffers
          (model.forward_host -> tt_model_forward_host): every step copies the
-         input shard from pinned host memory and the FP32 output back to pinned
-         host memory inside the timed region, the copies overlapped with the
-         kernels by batch chunks.
+         input slice from pinned host memory and the FP32 output back to host
+         memory inside the timed region, the copies overlapped with the
+         kernels by batch chunks; with N > 1 every rank writes its slice into
+         one page-locked host buffer shared with rank 0's process.
   roofline  the dominant kernel's algorithmic FLOPs (or bytes) per launch over
          its mean event-timed duration inside the timed region, against the
          measured peak in MEASURED_PEAKS.json.
@@ -94,7 +104,10 @@ def parse_args():
     ap.add_argument("--graph", action="store_true",
                     help="time replays of one captured CUDA graph of the forward (small workloads)")
     ap.add_argument("--batch", type=int, default=None,
-                    help="override the workload's batch per GPU (smaller profiling cases)")
+                    help="override the workload's batch (smaller profiling cases)")
+    ap.add_argument("--scaling", default="strong", choices=("strong", "weak"),
+                    help="strong: the workload's batch split across the GPUs and gathered to GPU 0 (default); "
+                         "weak: every GPU runs a whole batch of its own")
     return ap.parse_args()
 
 
@@ -281,6 +294,75 @@ def run_reference(args, cfg, padding_ratio, workload_name):
     return 0
 
 
+class SharedHostOutput:
+    """The whole batch's FP32 output in host memory shared by every rank's process.
+
+    Rank 0 creates a file under /dev/shm; every rank maps it and page-locks its
+    own slice (cudaHostRegister), so each GPU copies its slice of the output
+    over its own PCIe link straight into memory rank 0 reads: the gather to
+    rank 0's host needs no further copy.  Falls back to a private pinned
+    buffer per rank when no shared file can be made (then ``shared`` is False).
+    """
+
+    def __init__(self, shape, s0, s1, rank, world, barrier):
+        import tempfile
+
+        self.shared = False
+        self.path = None
+        self._registered = None
+        numel = 1
+        for d in shape:
+            numel *= d
+        row = numel // shape[0]
+        path = [None]
+        if rank == 0:
+            try:
+                fd, p = tempfile.mkstemp(prefix="tt_b200_out_", dir="/dev/shm")
+                os.close(fd)
+                os.truncate(p, numel * 4)
+                path[0] = p
+            except OSError:
+                path[0] = None
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.broadcast_object_list(path, src=0)
+        barrier()
+        self.path = path[0]
+        if self.path is not None:
+            try:
+                full = torch.from_file(self.path, shared=True, size=numel, dtype=torch.float32).view(*shape)
+                part = full[s0:s1]
+                rc = torch.cuda.cudart().cudaHostRegister(part.data_ptr(), part.numel() * 4, 0)
+                if int(rc) == 0:
+                    self.full, self.part, self.shared = full, part, True
+                    self._registered = part.data_ptr()
+            except Exception:
+                self.shared = False
+        if not self.shared:
+            self.full = None
+            self.part = torch.empty((s1 - s0,) + tuple(shape[1:]), dtype=torch.float32).pin_memory()
+        ok = torch.tensor([1.0 if self.shared else 0.0])
+        if world > 1:
+            import torch.distributed as dist
+
+            t = ok.cuda()
+            dist.all_reduce(t, op=dist.ReduceOp.MIN)
+            ok = t.cpu()
+        self.all_shared = bool(ok.item() > 0.5)
+
+    def close(self, rank, barrier):
+        if self._registered is not None:
+            torch.cuda.cudart().cudaHostUnregister(self._registered)
+            self._registered = None
+        barrier()
+        if rank == 0 and self.path is not None:
+            try:
+                os.unlink(self.path)
+            except OSError:
+                pass
+
+
 def main() -> int:
     args = parse_args()
     B, S, D, H, F, L, causal, pad = WORKLOADS[args.config]
@@ -295,6 +377,7 @@ def main() -> int:
 
     from tiktoktechjam2026_b200 import B200Transformer, TransformerConfig, _lib
     from tiktoktechjam2026_b200.model import default_host_chunk
+    from tiktoktechjam2026_b200.sharding import PeerGatherBuffer, shard_bounds
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -321,28 +404,70 @@ def main() -> int:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return float(t.item())
 
-    # Weak scaling: every rank runs the workload's whole batch as its shard of a
-    # global batch of B * world sequences (rank r holds sequences [r B, (r+1) B),
-    # drawn from seed SEED + r; rank 0's shard is the single-GPU input).
-    nb = B
-    global_batch = B * world
+    strong = args.scaling == "strong"
+    # Strong scaling (default): the workload's one batch of B sequences is split
+    # into contiguous slices (shard_bounds), rank r runs sequences [s0, s1), and
+    # every slice's FP32 output is pushed into one gather buffer on GPU 0 inside
+    # the timed region.  Weak scaling: every rank runs a whole batch of B of its
+    # own (seed SEED + r), nothing is gathered.
+    if strong:
+        s0, s1 = shard_bounds(B, world, rank)
+        global_batch = B
+    else:
+        s0, s1 = 0, B
+        global_batch = B * world
+    nb = s1 - s0
     torch.manual_seed(1234)
     model = B200Transformer(TransformerConfig(nb, S, D, H, F, L, causal)).to(dev).eval()
     model.convert_projections_to_fp16()
     model.assume_all_tokens_valid = pad <= 0
-    x_full, mask_full = make_inputs(cfg, pad, SEED + rank)
-    x_host = x_full.pin_memory()
-    mask_host = None if mask_full is None else mask_full.pin_memory()
+    x_full, mask_full = make_inputs(cfg, pad, SEED if strong else SEED + rank)
+    x_host = x_full[s0:s1].contiguous().pin_memory()
+    mask_host = None if mask_full is None else mask_full[s0:s1].contiguous().pin_memory()
+    x_all = x_full if (strong and world > 1 and rank == 0) else None  # for rank 0's 1-GPU check
+    mask_all = mask_full if x_all is not None else None
     del x_full, mask_full
-    out_host = torch.empty_like(x_host).pin_memory()
     x_dev = x_host.to(dev)
     mask_dev = None if mask_host is None else mask_host.to(dev)
     flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)
     stream = torch.cuda.current_stream(dev)
+    gather = None
+    outs = [torch.empty_like(x_dev) for _ in range(2)]
+    if strong and world > 1:
+        gather = PeerGatherBuffer(B, (S, D), rank, world, dev, slots=2)
+        if rank == 0:
+            outs = [gather.local_view(k)[s0:s1] for k in range(2)]
+
+    def step(i):
+        """One forward of this rank's slice; with a gather, its output pushed to GPU 0."""
+        if gather is None:
+            model.forward_gather(x_dev, mask_dev, outs[i % 2], 0)
+        else:
+            model.forward_gather(x_dev, mask_dev, outs[i % 2], gather.dst(i % 2) if rank != 0 else 0)
+
+    def timed_steps(fn, n, tail=None):
+        """Per-step CUDA-event times with the L2 flushed (untimed) before each step,
+        plus the time `tail` adds after the last step; summed, in ms."""
+        st = [torch.cuda.Event(enable_timing=True) for _ in range(n + 1)]
+        en = [torch.cuda.Event(enable_timing=True) for _ in range(n + 1)]
+        barrier()
+        for i in range(n):
+            flush.zero_()
+            st[i].record(stream)
+            fn(i)
+            en[i].record(stream)
+        st[n].record(stream)
+        if tail is not None:
+            tail()
+        en[n].record(stream)
+        barrier()
+        return [a.elapsed_time(b) for a, b in zip(st, en)]
 
     with torch.inference_mode():
-        for _ in range(max(3, args.warmup)):
-            model(x_dev, mask_dev)
+        for i in range(max(3, args.warmup)):
+            step(i)
+        if gather is not None:
+            model.gather_wait(dev)
         barrier()
 
         # ---------------- value: device-resident inputs ----------------
@@ -350,7 +475,7 @@ def main() -> int:
         # the per-kernel breakdown then comes from a separate profiled eager pass.
         graphed = None
         kernels_per_forward = 0
-        if args.graph:
+        if args.graph and gather is None:
             l0 = _lib.lib().tt_launch_count()
             model(x_dev, mask_dev)
             kernels_per_forward = _lib.lib().tt_launch_count() - l0
@@ -361,24 +486,15 @@ def main() -> int:
         else:
             model.set_profiling(True, dev)
             model.profile_collect(dev)
-        starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-        ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
         sampler = ClockSampler() if rank == 0 else None
         if sampler:
             sampler.start()
         launches0 = _lib.lib().tt_launch_count()
-        barrier()
-        for i in range(args.steps):
-            flush.zero_()
-            starts[i].record(stream)
-            if graphed is not None:
-                graphed()
-            else:
-                model(x_dev, mask_dev)
-            ends[i].record(stream)
-        barrier()
+        if graphed is not None:
+            step_ms = timed_steps(lambda i: graphed(), args.steps)
+        else:
+            step_ms = timed_steps(step, args.steps, (lambda: model.gather_wait(dev)) if gather is not None else None)
         launches = _lib.lib().tt_launch_count() - launches0 + kernels_per_forward * args.steps
-        step_ms = [a.elapsed_time(b) for a, b in zip(starts, ends)]
         if graphed is not None:
             model.set_profiling(True, dev)
             model.profile_collect(dev)
@@ -389,11 +505,52 @@ def main() -> int:
         prof = model.profile_collect(dev)
         model.set_profiling(False, dev)
         total_ms = max_over_ranks(sum(step_ms))
+        gather_tail_ms = max_over_ranks(step_ms[-1])
+
+        extra = {}
+        if gather is not None:
+            # Compute alone (no push), and one step's latency with the push exposed.
+            comp = timed_steps(lambda i: model.forward_gather(x_dev, mask_dev, outs[i % 2], 0), args.steps)
+            extra["compute_only"] = {"value": global_batch * 1000.0 / (max_over_ranks(sum(comp)) / args.steps),
+                                     "ms_per_step": max_over_ranks(sum(comp)) / args.steps,
+                                     "what": "the same steps without the push to GPU 0"}
+            lat = []
+            for i in range(args.steps):
+                t = timed_steps(lambda j: (step(i), model.gather_wait(dev)), 1)
+                lat.append(max_over_ranks(sum(t)))
+            extra["latency_ms"] = {"median": statistics.median(lat), "max": max(lat),
+                                   "what": "one step alone: slice forward, then its push to GPU 0 waited for"}
+            # Rank 0 checks the gathered batch against its own 1-GPU forward of the whole batch.
+            barrier()
+            if rank == 0:
+                full_model = model
+                ref = full_model(x_all.to(dev), None if mask_all is None else mask_all.to(dev))
+                torch.cuda.synchronize(dev)
+                got = gather.local_view((args.steps - 1) % 2)
+                extra["gather_check"] = {
+                    "sequences": B, "bitwise_equal_to_1gpu_forward": bool(torch.equal(got, ref)),
+                    "max_abs_diff": float((got - ref).abs().max().item())}
+                del ref
+            barrier()
+            # Weak scaling for comparison: every rank runs a whole batch of its own.
+            xw, mw = make_inputs(cfg, pad, SEED + rank)
+            xw = xw.to(dev)
+            mw = None if mw is None else mw.to(dev)
+            ow = torch.empty_like(xw)
+            model(xw, mw)
+            weak = timed_steps(lambda i: model.forward_gather(xw, mw, ow, 0), args.steps)
+            extra["weak"] = {"value": B * world * 1000.0 / (max_over_ranks(sum(weak)) / args.steps),
+                             "ms_per_step": max_over_ranks(sum(weak)) / args.steps, "global_batch": B * world,
+                             "what": f"each rank runs a whole batch of {B} of its own; nothing gathered"}
+            del xw, mw, ow
 
         # ---------------- e2e: host buffers through the public call ----------------
         # model.forward_host = one tt_model_forward_host call: pinned host input in,
-        # pinned host output back, copies pipelined with the kernels by chunks.
+        # pinned host output back, copies pipelined with the kernels by chunks.  With
+        # several ranks each writes its slice into one host buffer shared with rank 0.
         chunk = args.chunk or default_host_chunk(nb, S, D)
+        host_out = SharedHostOutput((B, S, D), s0, s1, rank, world, barrier) if strong and world > 1 else None
+        out_host = host_out.part if host_out is not None else torch.empty_like(x_host).pin_memory()
         for _ in range(2):
             model.forward_host(x_host, mask_host, out=out_host, chunk=chunk)
         barrier()
@@ -407,6 +564,15 @@ def main() -> int:
         barrier()
         clocks = sampler.stop(list(range(world))) if sampler else None
         e2e_ms = max_over_ranks(e_start.elapsed_time(e_end))
+        if host_out is not None:
+            if rank == 0 and host_out.all_shared:
+                ref = model(x_all.to(dev), None if mask_all is None else mask_all.to(dev)).cpu()
+                extra["e2e_gather_check"] = {"sequences": B,
+                                             "bitwise_equal_to_1gpu_forward": bool(torch.equal(host_out.full, ref))}
+                del ref
+            extra["e2e_gather"] = ("one host buffer shared by all ranks (/dev/shm, page-locked per slice)"
+                                   if host_out.all_shared else "per-rank pinned buffers (no shared host memory)")
+            host_out.close(rank, barrier)
 
     # ---------------- roofline of the dominant kernel ----------------
     hbm_peak, tc_peak, peak_src = load_peaks()
@@ -421,7 +587,7 @@ def main() -> int:
     else:
         roof = {"bound": "hbm", "achieved": nbytes / per_launch_s / 1e9, "peak": hbm_peak, "unit": "GB/s"}
     roof["frac"] = roof["achieved"] / roof["peak"]
-    roof["traffic"] = load_traffic(workload_name, nb, kind)
+    roof["traffic"] = load_traffic(args.config if args.batch is None else workload_name, nb, kind)
     roof["kernel"] = kernel_label(kind, cfg)
     roof["mean_launch_us"] = per_launch_s * 1e6
     roof["algorithmic_per_launch"] = {"flops": flops, "bytes": nbytes}
@@ -432,32 +598,50 @@ def main() -> int:
         ms_per_step = total_ms / args.steps
         value = global_batch * 1000.0 / ms_per_step
         e2e_value = global_batch * 1000.0 / (e2e_ms / args.steps)
+        if strong:
+            par = (f"batch split x{world}: {nb} sequences on GPU 0 (shard_bounds), FP32 outputs pushed into one "
+                   f"gather buffer on GPU 0 over NVLink (copy engines, overlapped with the next step)"
+                   if world > 1 else "one GPU, whole batch")
+        else:
+            par = f"weak scaling x{world}: {nb} sequences per GPU, no collective in the data path"
         line = {
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
+            "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True,
+            "scaling": "strong" if strong else "weak",
             "vs_baseline": None, "dtype": "f16 tensor-core operands, f32 accumulate/softmax/LayerNorm/residual",
             "data": "synthetic (x ~ N(0,1) FP32 from the reference's timing seed; seeded default-init weights)",
             "config": {"workload": f"{workload_name}: batch {B}, seq {S}, d_model {D}, heads {H}, ffn {F}, "
                                    f"layers {L}, causal{', key padding' if pad > 0 else ''}",
                        "global_batch": global_batch, "per_gpu_batch": nb, "seq_len": S, "d_model": D, "heads": H,
-                       "ffn": F, "layers": L,
-                       "parallelism": f"batch-sharded x{world} ({nb} sequences per GPU), no collective in the data path",
+                       "ffn": F, "layers": L, "parallelism": par,
                        "l2": "flushed between timed steps (256 MiB write, untimed)",
-                       "launch": "one CUDA graph replay per step" if args.graph else "eager (one host call per step)"},
+                       "launch": "one CUDA graph replay per step" if graphed is not None else
+                                 "eager (one host call per step)"},
             "e2e": {"value": e2e_value, "unit": UNIT, "ms_per_step": e2e_ms / args.steps, "chunk": chunk,
                     "path": "model.forward_host -> tt_model_forward_host (pinned host in/out, copies overlapped "
-                            "with compute by chunks)",
-                    "h2d_bytes_per_step": world * (x_host.numel() * 4 + (0 if mask_host is None else mask_host.numel())),
-                    "d2h_bytes_per_step": world * out_host.numel() * 4},
+                            "with compute by chunks)" + ("; each rank's slice of one shared host output" if
+                                                         strong and world > 1 else ""),
+                    "h2d_bytes_per_step": (world if not strong else 1) * (
+                        B * S * D * 4 + (0 if mask_host is None else B * S)),
+                    "d2h_bytes_per_step": (world if not strong else 1) * B * S * D * 4},
             "gpu_launches": int(launches),
             "roofline": roof,
             "kernel_ms_per_step": {k: v[0] / args.steps for k, v in prof.items() if v[1] > 0},
             "clocks": clocks,
         }
+        if gather is not None:
+            line["gather"] = {"bytes_into_gpu0_per_step": (B - nb) * S * D * 4,
+                              "tail_ms": gather_tail_ms,
+                              "what": "each step's push overlaps the next step's compute; tail_ms is the wait "
+                                      "for the last push after the last step, inside the timed total"}
+        line.update(extra)
         if world == 1 and not args.no_cpu_baseline:
             v, cores, sample = cpu_baseline(cfg, pad, args.cpu_sample_seconds)
             line["cpu_baseline"] = {"value": v, "unit": UNIT, "cores": cores, "kind": "port", "sample": sample}
         print(json.dumps(line), flush=True)
+    if gather is not None:
+        barrier()
+        gather.close()
     if world > 1:
         dist.destroy_process_group()
     return 0

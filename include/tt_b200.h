@@ -7,8 +7,9 @@
  *     where a comment says "host".  FP16 tensors are passed as void*.
  *   - Every compute entry point takes the CUDA stream to launch on (as void*,
  *     a cudaStream_t; NULL = legacy default stream), launches asynchronously
- *     and returns a status code.  No entry point allocates device memory, and
- *     none traps or exits: failures are status codes, plus a device error word
+ *     and returns a status code.  No compute entry point allocates device
+ *     memory (tt_workspace_alloc/free are the only ones that do), and none
+ *     traps or exits: failures are status codes, plus a device error word
  *     that bounded in-kernel waits set on timeout (see tt_device_error).
  *   - Kernels run on the calling thread's current CUDA device.
  *
@@ -58,6 +59,13 @@ unsigned long long tt_launch_count(void);
  * designed (synchronizes the stream; clears the error word afterwards). */
 int tt_watchdog_selftest(unsigned long long timeout_ns, void* stream);
 
+/* Self-test of the polynomial exponential that evaluates part of the attention
+ * softmax's probabilities on the FP32 pipe instead of the MUFU unit:
+ * y32[i] = 2^x[i] from the polynomial (FP32) and y16[i] the same rounded to
+ * FP16 (bits), for n (even) inputs in [-125, 64).  A test probe; it has no
+ * counterpart in the reference, whose Triton kernels call exp2 only. */
+int tt_selftest_exp2_fma(const float* x, float* y32, uint16_t* y16, int n, void* stream);
+
 /* ---- single ops ----------------------------------------------------------- */
 
 /* out[r, :] = LayerNorm(x[r, :]) * gamma + beta over d features, FP32 math,
@@ -90,7 +98,9 @@ int tt_qkv_projection(const void* normalized, const void* w_qkv, const float* b_
  * FP16 operands, FP32 softmax statistics and accumulation, FP16 output.
  * key_mask: [batch, seq] bytes (nonzero = valid) or NULL; kv_end must then hold
  * tt_mask_kv_end's output.  With a mask, padded query rows get a zero context
- * (the reference zeroes those rows on the model output).  head_dim in
+ * (the reference zeroes those rows on the model output).  vt's padding columns
+ * [seq, seq_pad) must hold finite values (zeros, say): they are multiplied by
+ * zero probabilities, and 0 * Inf or 0 * NaN would reach ctx.  head_dim in
  * {8, 16, 32, 64}; q, k and vt have tt_qkv_projection's layout (16 features
  * per head when head_dim is 8, the extra q/k features zero), ctx has head_dim
  * per head.
@@ -198,12 +208,23 @@ typedef struct tt_model tt_model;
 int tt_model_create(const tt_model_desc* desc, tt_model** out);
 void tt_model_destroy(tt_model* model);
 
+/* Device memory for a workspace on the current device (cudaMalloc: 256-byte
+ * aligned or better), outside any allocator of the caller's framework, e.g.
+ * so that a CUDA-graph capture by that framework never sees it as a pool
+ * allocation.  The only entry points that allocate or free device memory; no
+ * compute entry point calls them.  tt_workspace_free(NULL) is a no-op.
+ * No counterpart in the reference, which allocates through PyTorch. */
+int tt_workspace_alloc(size_t bytes, void** ptr);
+int tt_workspace_free(void* ptr);
+
 /* Workspace bytes tt_model_forward needs for (batch, seq). */
 int tt_model_workspace_bytes(const tt_model* model, int batch, int seq, size_t* bytes);
 
 /* out[B, S, D] (FP32) = the model applied to x[B, S, D] (FP32).  mask: [B, S]
  * bytes (nonzero = valid token) or NULL; with a mask, padded output rows are
- * exactly zero.  x and out must not overlap the workspace.
+ * exactly zero.  x and out must not overlap the workspace.  The workspace
+ * needs no initialisation and may be used for anything between calls: every
+ * forward writes what it later reads (including the V^T padding columns). 
  * Replaces MixedPrecisionTransformer.forward (mixed_precision/transformer.py:480-699). */
 int tt_model_forward(tt_model* model, const float* x, const uint8_t* mask, float* out, int batch,
                      int seq, void* workspace, size_t workspace_bytes, void* stream);
@@ -234,6 +255,46 @@ int tt_model_forward_host(tt_model* model, const float* x, const uint8_t* mask, 
 int tt_model_forward_host_chunks(tt_model* model, const float* x, const uint8_t* mask, float* out, int batch,
                                  int seq, const int* chunk_sizes, int n_chunks, void* workspace,
                                  size_t workspace_bytes, void* stream);
+
+/* ---- batch sharding across the GPUs of one node ---------------------------
+ * Sequences are independent, so a batch splits into contiguous slices, one per
+ * GPU (one process per GPU), with no exchange during compute; the only
+ * communication is the final gather of the FP32 outputs into one buffer on the
+ * first GPU, over NVLink.  These generalise the reference's batch slicing into
+ * a preallocated output (PreallocatedMicrobatchModel,
+ * mixed_precision_benchmark.py:13-33 and :79-84; MicrobatchModel,
+ * torch_transformer_benchmark.py:808-833), which runs its slices one after the
+ * other on one GPU; the reference itself has no multi-GPU code. */
+
+#define TT_PEER_HANDLE_BYTES 64
+
+/* Exports device memory of the current device to other processes: writes a
+ * TT_PEER_HANDLE_BYTES handle (host) of the allocation that contains dev_ptr
+ * and dev_ptr's byte offset inside it. */
+int tt_peer_export(const void* dev_ptr, void* handle, size_t* offset);
+
+/* Maps memory exported by another process (tt_peer_export's handle and
+ * offset) into this process with peer access from the current device, and
+ * returns its address.  Not for a handle this process exported itself. */
+int tt_peer_open(const void* handle, size_t offset, void** dev_ptr);
+
+/* Unmaps an address tt_peer_open returned (the same offset). */
+int tt_peer_close(void* dev_ptr, size_t offset);
+
+/* tt_model_forward of this GPU's batch slice into `out` (local), then a copy
+ * of the finished slice into gather_dst (typically another GPU's gather
+ * buffer from tt_peer_open) on the model's own copy stream, so the copy
+ * crosses NVLink on the copy engines while later work on `stream` computes.
+ * The copy reads `out`: a later forward of this model waits for it before its
+ * last layer writes `out` again, so calls may follow one another on `stream`
+ * without a bubble.  gather_dst NULL or equal to out: a plain forward (the
+ * GPU that holds the gather buffer writes its slice there directly).  The
+ * destination holds the slice once tt_model_gather_wait's stream reaches it. */
+int tt_model_forward_gather(tt_model* model, const float* x, const uint8_t* mask, float* out, float* gather_dst,
+                            int batch, int seq, void* workspace, size_t workspace_bytes, void* stream);
+
+/* Makes `stream` wait until every gather copy this model has issued is done. */
+int tt_model_gather_wait(tt_model* model, void* stream);
 
 /* One forward captured as a CUDA graph: the pointers, shapes and tile
  * configuration of this call are baked in (the caller keeps x, mask, out and

@@ -32,7 +32,7 @@ def test_ctypes_signatures_cover_header(tt_lib):
 
 
 def test_abi_version_and_error_string(tt_lib):
-    assert tt_lib.tt_abi_version() == 1
+    assert tt_lib.tt_abi_version() == 2
     assert isinstance(_lib.last_error(), str)
 
 

@@ -143,8 +143,9 @@ def test_attention_fully_padded_tile_is_zero(tt_lib):
     torch.testing.assert_close(out[1, :300].float(), ref[1, :300], rtol=5e-3, atol=5e-3)
 
 
+# d_model 96, 160 and 224 split their rows unevenly between the two epilogue warps of a lane quadrant.
 LIN_LN_SHAPES = [(1000, 128, 128), (300, 32, 32), (513, 256, 256), (257, 512, 512), (200, 2048, 512),
-                 (129, 1024, 256), (4096, 128, 128)]
+                 (129, 1024, 256), (4096, 128, 128), (300, 96, 96), (257, 160, 160), (129, 224, 224)]
 
 
 @pytest.mark.parametrize("N,K,D", LIN_LN_SHAPES)
@@ -229,3 +230,26 @@ def test_gelu_matches_exact_erf(tt_lib):
     ref = F.gelu(x.half().float(), approximate="none")
     # out is FP16: within FP16 rounding of the exact value
     torch.testing.assert_close(out.float(), ref, rtol=1e-3, atol=1e-6)
+
+
+def test_exp2_polynomial_matches_exp2(tt_lib):
+    """The softmax's FMA-pipe exponential against exact 2^x: relative error <= 2.7e-6 (the fit's bound)
+    plus FP32 rounding of the result, over [-125, 64); its FP16 form within one FP16 unit in the last
+    place of the exact value (x < 15.99, below FP16's largest finite value 65504 = 2^15.9993)."""
+    g = _gen(77)
+    x = torch.cat([torch.linspace(-125.0, 63.99, 1 << 21), (torch.rand(1 << 20, generator=g) * 188.99 - 125.0),
+                   torch.tensor([-125.0, -0.5, 0.5, -0.49999997, 0.49999997, 0.0, -1.0, 1.0, 7.9999995, 8.0])])
+    x = x[: x.numel() // 2 * 2].contiguous().to(DEV)
+    y32 = torch.empty_like(x)
+    y16 = torch.empty(x.numel(), dtype=torch.float16, device=DEV)
+    rc = tt_lib.tt_selftest_exp2_fma(x.data_ptr(), y32.data_ptr(), y16.data_ptr(), x.numel(),
+                                     torch.cuda.current_stream(DEV).cuda_stream)
+    assert rc == _lib.TT_OK, _lib.last_error()
+    exact = torch.exp2(x.double())
+    rel = ((y32.double() - exact).abs() / exact).max().item()
+    assert rel <= 2.7e-6 + 2 ** -23, rel
+    sel = x < 15.99
+    e = exact[sel]
+    ulp = torch.exp2(torch.floor(torch.log2(e)) - 10).clamp_min(2.0 ** -24)
+    err16 = (y16[sel].double() - e).abs()
+    assert bool(torch.all(err16 <= ulp)), float((err16 / ulp).max())

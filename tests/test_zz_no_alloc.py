@@ -1,4 +1,4 @@
-"""The allocation-free masked attention entry point agrees with the allocating path.
+"""The allocation-free masked attention entry point agrees with the allocating path and with FP32 math.
 
 tt_causal_attention_masked_noalloc serves callers that cannot allocate device
 memory (CUDA-graph capture in progress, device memory owned by an external
@@ -7,8 +7,10 @@ in a static array inside the library.  This test calls it through the C ABI
 twice in a row, with different masks so the second call must overwrite what
 the first left in the shared array, and compares each result with
 tt_mask_kv_end + tt_causal_attention on the same inputs, within the attention
-tests' tolerance.  The file sorts last so a failing run stops only after every
-other test has run; it also passes on its own in a fresh process.
+tests' tolerance.  A second test runs it at head_dim 16, 32 and 64, causal and
+not, twice in a row with different masks, against plain PyTorch FP32 attention
+on the same FP16 operands.  The file sorts last so a failing run stops only
+after every other test has run; it also passes on its own in a fresh process.
 """
 
 import ctypes
@@ -73,3 +75,41 @@ def test_noalloc_rejects_batch_beyond_static_limit(tt_lib):
                                                        torch.cuda.current_stream(DEV).cuda_stream)
     assert rc == _lib.TT_ERR_SHAPE
     assert "65536" in _lib.last_error()
+
+
+def _fp32_attention(q, k, vt, scale, causal, mask):
+    """softmax(q k^T * scale + masks) v in FP32 from the FP16 operands; padded query rows are zero."""
+    B, H, S, hd = q.shape
+    v = vt[..., :S].transpose(-1, -2).float()
+    s = (q.float() @ k.float().transpose(-1, -2)) * scale
+    if causal:
+        s = s.masked_fill(torch.ones(S, S, dtype=torch.bool, device=q.device).triu(1), float("-inf"))
+    s = s.masked_fill(~mask[:, None, None, :], float("-inf"))
+    p = torch.nan_to_num(torch.softmax(s, dim=-1), nan=0.0)
+    ctx = (p @ v).transpose(1, 2).reshape(B, S, H * hd)
+    return ctx.masked_fill(~mask[..., None], 0)
+
+
+@pytest.mark.parametrize("hd", [16, 32, 64])
+@pytest.mark.parametrize("causal", [True, False])
+def test_noalloc_matches_fp32_attention(tt_lib, hd, causal):
+    B, H, S = 5, 2, 200
+    g = torch.Generator().manual_seed(hd * 10 + int(causal))
+    q = torch.randn(B, H, S, hd, generator=g).half().to(DEV)
+    k = torch.randn(B, H, S, hd, generator=g).half().to(DEV)
+    sp = ops.seq_pad_of(S)
+    vt = torch.zeros(B, H, hd, sp, dtype=torch.float16)
+    vt[..., :S] = torch.randn(B, H, hd, S, generator=g).half()
+    vt = vt.to(DEV)
+    scale = hd**-0.5
+    ctx = torch.empty(B, S, H * hd, dtype=torch.float16, device=DEV)
+    for lengths in (torch.tensor([200, 1, 77, 128, 199]), torch.tensor([64, 200, 3, 150, 129])):
+        mask = (torch.arange(S)[None, :] < lengths[:, None]).to(DEV)
+        m8 = mask.contiguous().view(torch.uint8)
+        _lib.check(_lib.lib().tt_causal_attention_masked_noalloc(
+            q.data_ptr(), k.data_ptr(), vt.data_ptr(), m8.data_ptr(), ctx.data_ptr(), B, S, H, hd, sp, scale,
+            int(causal), torch.cuda.current_stream(DEV).cuda_stream))
+        torch.cuda.synchronize()
+        ref = _fp32_attention(q, k, vt, scale, causal, mask)
+        # P is rounded to FP16 before P.V; |ctx| <= max|v| < 5
+        torch.testing.assert_close(ctx.float(), ref, rtol=5e-3, atol=5e-3)

@@ -23,6 +23,8 @@ TT_ERR_TIMEOUT = 5
 TT_ERR_ARG = 6
 TT_ERR_WORKSPACE = 7
 
+TT_PEER_HANDLE_BYTES = 64
+
 KERNEL_KINDS = ["ln0", "mask", "qkv", "attn", "out_ln", "ffn_in", "ffn_out_ln", "ffn_fused"]
 
 
@@ -73,6 +75,7 @@ SIGNATURES = {
     "tt_set_wait_timeout_ns": (None, [c_ulonglong]),
     "tt_launch_count": (c_ulonglong, []),
     "tt_watchdog_selftest": (c_int, [c_ulonglong, c_void_p]),
+    "tt_selftest_exp2_fma": (c_int, [c_void_p, c_void_p, c_void_p, c_int, c_void_p]),
     "tt_layernorm_rows": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int, c_float, c_int, c_void_p]),
     "tt_mask_kv_end": (c_int, [c_void_p, c_int, c_int, c_void_p, c_void_p]),
     "tt_qkv_projection": (
@@ -103,6 +106,8 @@ SIGNATURES = {
     "tt_route_describe": (c_int, [c_int, c_int, c_int, c_int, c_char_p, c_int]),
     "tt_model_create": (c_int, [POINTER(ModelDesc), POINTER(c_void_p)]),
     "tt_model_destroy": (None, [c_void_p]),
+    "tt_workspace_alloc": (c_int, [c_size_t, POINTER(c_void_p)]),
+    "tt_workspace_free": (c_int, [c_void_p]),
     "tt_model_workspace_bytes": (c_int, [c_void_p, c_int, c_int, POINTER(c_size_t)]),
     "tt_model_forward": (
         c_int,
@@ -122,6 +127,14 @@ SIGNATURES = {
         c_int,
         [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_void_p, c_size_t, POINTER(c_void_p)],
     ),
+    "tt_peer_export": (c_int, [c_void_p, c_void_p, POINTER(c_size_t)]),
+    "tt_peer_open": (c_int, [c_void_p, c_size_t, POINTER(c_void_p)]),
+    "tt_peer_close": (c_int, [c_void_p, c_size_t]),
+    "tt_model_forward_gather": (
+        c_int,
+        [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_void_p, c_size_t, c_void_p],
+    ),
+    "tt_model_gather_wait": (c_int, [c_void_p, c_void_p]),
     "tt_graph_launch": (c_int, [c_void_p, c_void_p]),
     "tt_graph_destroy": (None, [c_void_p]),
     "tt_model_set_profiling": (c_int, [c_void_p, c_int]),

@@ -105,20 +105,12 @@ __device__ __forceinline__ AttnItem attn_item(const AttnParams& p, int w, int n_
 }
 
 // Eight probabilities of one row, packed as four FP16 pairs.
-template <bool EXP16>
 __device__ __forceinline__ void probs8(const float* x, float sl2, float m_use, uint32_t (&pk)[4]) {
 #pragma unroll
   for (int e = 0; e < 4; ++e) {
     const float a = fmaf(x[2 * e], sl2, -m_use);
     const float c = fmaf(x[2 * e + 1], sl2, -m_use);
-    if constexpr (EXP16) {
-      uint32_t h2, r;
-      asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(h2) : "f"(c), "f"(a));
-      asm("ex2.approx.f16x2 %0, %1;" : "=r"(r) : "r"(h2));
-      pk[e] = r;
-    } else {
-      pk[e] = pack_half2(ex2_approx(a), ex2_approx(c));
-    }
+    pk[e] = pack_half2(ex2_approx(a), ex2_approx(c));
   }
 }
 
@@ -128,7 +120,7 @@ __device__ __forceinline__ float max3(float a, float b, float c) {
   return m;
 }
 
-template <int HD, bool EXP16>
+template <int HD>
 __global__ void __launch_bounds__(192, 1)
     attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                     const __grid_constant__ CUtensorMap tmV, const AttnParams p, int n_items) {
@@ -414,7 +406,7 @@ __global__ void __launch_bounds__(192, 1)
 #pragma unroll
         for (int ch = 0; ch < BN / 8; ++ch) {
           uint32_t pk[4];
-          probs8<EXP16>(&x[ch * 8], sl2, m_use, pk);
+          probs8(&x[ch * 8], sl2, m_use, pk);
           const uint32_t addr = prow + (ch >> 3) * (BM * 128) + (((ch & 7) ^ (row & 7)) << 4);
           st_shared_v4(addr, pk[0], pk[1], pk[2], pk[3]);
         }

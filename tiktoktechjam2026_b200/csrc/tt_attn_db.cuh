@@ -6,19 +6,17 @@
 // score) bounds the kernel, so the layout keeps the softmax warps from ever
 // waiting on the tensor core:
 //
-//  * one CTA per SM runs NS independent pipelines ("streams", 2 by default),
-//    each on a 128-query tile of its own work item, with 4 softmax warps (one
-//    per TMEM lane quadrant, a whole row per thread), its own TMA producer warp
-//    (4 NS + s) and its own MMA-issuer warp (5 NS + s); idle warps complete
-//    the last warpgroup (setmaxnreg acts on whole warpgroups);
-//  * key tiles are 64 wide; each stream has NSB score buffers S in TMEM (1 with
-//    3 streams, 2 with 2 streams); the softmax writes the FP16 probabilities P
-//    back over the first 32 columns of the S buffer it has just read (one
-//    tcgen05.st, no shared memory and no proxy fence), and P.V reads them as a
-//    TMEM A operand.  S_{t+NSB} is issued right after P.V of tile t into the
-//    same buffer: one thread's MMAs execute in issue order, so P_t is read
-//    before it is overwritten.  With one buffer the softmax of a stream waits
-//    for its next S after publishing P; the other streams' warps fill that gap.
+//  * one CTA per SM runs two independent pipelines ("streams"), each on a
+//    128-query tile of its own work item, with 4 softmax warps (one per TMEM
+//    lane quadrant, a whole row per thread), its own TMA producer warp (8 + s)
+//    and its own MMA-issuer warp (10 + s); idle warps complete the last
+//    warpgroup (setmaxnreg acts on whole warpgroups);
+//  * key tiles are 64 wide; each stream has two score buffers S in TMEM; the
+//    softmax writes the FP16 probabilities P back over the first 32 columns of
+//    the S buffer it has just read (one tcgen05.st, no shared memory and no
+//    proxy fence), and P.V reads them as a TMEM A operand.  S_{t+2} is issued
+//    right after P.V of tile t into the same buffer: one thread's MMAs execute
+//    in issue order, so P_t is read before it is overwritten.
 //
 // Per stream and key tile t (buffer b = t % NSB):
 //   S_b = Q K_t^T           TMEM, 64 FP32 columns
@@ -43,17 +41,12 @@
 
 namespace tt {
 
-// Streams per CTA (3: one S buffer each; 2: two S buffers each).
-#ifndef TT_DB_STREAMS
-#define TT_DB_STREAMS 2
-#endif
-
 template <int HD>
 struct AttnDbLayout {
-  static constexpr int NS = TT_DB_STREAMS;         // independent pipelines per CTA
-  static constexpr int NSB = NS == 3 ? 1 : 2;      // S (and P) buffers per stream
+  static constexpr int NS = 2;   // independent pipelines per CTA
+  static constexpr int NSB = 2;  // S (and P) buffers per stream
   static constexpr int BM = 128, BN = 64;
-  static constexpr int NST = NS == 3 ? (HD == 16 ? 6 : 4) : (HD == 16 ? 8 : 6);
+  static constexpr int NST = HD == 16 ? 8 : 6;
   static constexpr int Q_BYTES = BM * HD * 2;
   static constexpr int K_BYTES = BN * HD * 2;
   static constexpr int V_BYTES = HD * 128;  // V^T block: HD rows of 64 keys (128 bytes)
@@ -88,8 +81,8 @@ struct AttnDbLayout {
   // The launcher refuses to start the kernel unless it was built with exactly
   // REGS_LAUNCH registers per thread (a split above the launch total would make
   // setmaxnreg.inc wait forever).
-  static constexpr int REGS_LAUNCH = NS == 3 ? 96 : 168;
-  static constexpr int REGS_SOFTMAX = NS == 3 ? 128 : 216, REGS_OTHER = NS == 3 ? 48 : 56;
+  static constexpr int REGS_LAUNCH = 168;
+  static constexpr int REGS_SOFTMAX = 216, REGS_OTHER = 56;
   static_assert(NWARPS % 4 == 0, "whole warpgroups");
   static_assert(128 * NS * REGS_SOFTMAX + 32 * (NWARPS - 4 * NS) * REGS_OTHER <= THREADS * REGS_LAUNCH,
                 "register split");
@@ -105,18 +98,14 @@ struct AttnDbLayout {
 #define TT_DB_EXP_FMA_OF8 2
 #endif
 constexpr int kDbExpFmaOf8 = TT_DB_EXP_FMA_OF8;
-
-// The reference maximum moves when a tile's maximum exceeds it by more than
-// this (log2 units): FP32 exponentials tolerate 2^8; with packed-FP16
-// exponentials a smaller bound keeps the FP16 input x = s - m, whose rounding
-// error grows with |x|, accurate for the largest probabilities.
-#ifndef TT_DB_LAZY_F16
-#define TT_DB_LAZY_F16 2.0f
+#ifndef TT_ATTN_SKIP_MASKED
+#define TT_ATTN_SKIP_MASKED 0
+#endif
+#ifndef TT_ATTN_SCALAR_X
+#define TT_ATTN_SCALAR_X 0
 #endif
 
-// EXP16: probabilities from ex2.approx.f16x2 on FP16-rounded x (two per MUFU
-// operation, already packed for the P tile); otherwise FP32 exponentials.
-template <int HD, bool EXP16>
+template <int HD>
 __global__ void __launch_bounds__(AttnDbLayout<HD>::THREADS, 1)
     attn_db_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                        const __grid_constant__ CUtensorMap tmV, const AttnParams p, int n_items) {
@@ -391,6 +380,23 @@ __global__ void __launch_bounds__(AttnDbLayout<HD>::THREADS, 1)
 
         if (!(ok = warp_wait_phase(&b[L::B_SF + bb], (t / NSB) & 1, wd, 0x331))) break;
         tc_fence_after();
+#if TT_ATTN_SKIP_MASKED
+        // No row of this warp sees a key of this tile (above the causal diagonal,
+        // or past the sequence's last valid key): its probabilities are all zero.
+        if (__all_sync(0xffffffffu, k0 >= row_lim)) {
+          uint32_t zero[16];
+#pragma unroll
+          for (int e = 0; e < 16; ++e) zero[e] = 0u;
+          tmem_st_x16(tS + bb * BN, zero);
+          tmem_st_x16(tS + bb * BN + 16, zero);
+          tmem_st_wait();
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&b[L::B_PF + bb]);
+          if (j == 0 && pend && !(ok = finish_item())) break;
+          continue;
+        }
+#endif
         uint32_t sc[2][32];
         tmem_ld_x32(tS + bb * BN, sc[0]);
         tmem_ld_x32(tS + bb * BN + 32, sc[1]);
@@ -424,7 +430,8 @@ __global__ void __launch_bounds__(AttnDbLayout<HD>::THREADS, 1)
         // maximum without a rescale.
         float m_new = m_run;
         bool resc = false;
-        constexpr float kLazy = EXP16 ? TT_DB_LAZY_F16 : 8.0f;
+        // FP32 exponentials of x <= 8 keep P <= 2^8, well inside FP16.
+        constexpr float kLazy = 8.0f;
         if (m_tile > m_run + kLazy) {
           resc = (m_run != -INFINITY);
           m_new = m_tile;
@@ -458,19 +465,21 @@ __global__ void __launch_bounds__(AttnDbLayout<HD>::THREADS, 1)
           uint32_t pk[16];
 #pragma unroll
           for (int e = 0; e < 16; ++e) {
-            const uint64_t xx =
-                ffma2(f2_pack(__uint_as_float(sc[g][2 * e]), __uint_as_float(sc[g][2 * e + 1])), sl2x2, negm);
-            if constexpr (EXP16) {
-              uint32_t h2;
-              asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(h2) : "f"(f2_hi(xx)), "f"(f2_lo(xx)));
-              asm("ex2.approx.f16x2 %0, %1;" : "=r"(pk[e]) : "r"(h2));
-            } else {
-              uint64_t pp;
-              if ((e & 7) < kDbExpFmaOf8)
-                pp = exp2_pair_fma(xx);
-              else
-                pp = f2_pack(ex2_approx(f2_lo(xx)), ex2_approx(f2_hi(xx)));
+            if ((e & 7) < kDbExpFmaOf8) {
+              const uint64_t xx =
+                  ffma2(f2_pack(__uint_as_float(sc[g][2 * e]), __uint_as_float(sc[g][2 * e + 1])), sl2x2, negm);
+              const uint64_t pp = exp2_pair_fma(xx);
               pk[e] = pack_half2(f2_lo(pp), f2_hi(pp));
+            } else {
+#if TT_ATTN_SCALAR_X
+              const float x0 = fmaf(__uint_as_float(sc[g][2 * e]), sl2, -m_use);
+              const float x1 = fmaf(__uint_as_float(sc[g][2 * e + 1]), sl2, -m_use);
+              pk[e] = pack_half2(ex2_approx(x0), ex2_approx(x1));
+#else
+              const uint64_t xx =
+                  ffma2(f2_pack(__uint_as_float(sc[g][2 * e]), __uint_as_float(sc[g][2 * e + 1])), sl2x2, negm);
+              pk[e] = pack_half2(ex2_approx(f2_lo(xx)), ex2_approx(f2_hi(xx)));
+#endif
             }
           }
           tmem_st_x16(tS + bb * BN + 16 * g, pk);

@@ -29,7 +29,7 @@ __device__ unsigned int g_err_word;
 
 namespace {
 
-constexpr int kAbiVersion = 1;
+constexpr int kAbiVersion = 2;
 constexpr int kMaxDevices = 64;
 constexpr int kSmemBudget = 225 * 1024;
 
@@ -167,11 +167,46 @@ int encode_epi_tile(CUtensorMap* tm, const void* base, uint64_t rows, uint64_t c
                        base, 2, dims, strides, box);
 }
 
+// Per (kernel, device): the dynamic shared memory the kernel was opened up to
+// and its register count.  Each is queried or set once, so a launch is only a
+// launch (nothing else happens on the driver while a stream is captured).
+struct KernelInfo {
+  const void* fn;
+  int dev, smem, regs;
+};
+std::mutex g_kinfo_mu;
+std::vector<KernelInfo> g_kinfo;
+
+int kernel_info(const void* fn, int smem_bytes, KernelInfo* out) {
+  int dev = 0;
+  if (int rc = check_cuda(cudaGetDevice(&dev), "cudaGetDevice")) return rc;
+  std::lock_guard<std::mutex> lock(g_kinfo_mu);
+  for (KernelInfo& k : g_kinfo) {
+    if (k.fn == fn && k.dev == dev) {
+      if (k.smem < smem_bytes) {
+        if (int rc = check_cuda(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes),
+                                "cudaFuncSetAttribute"))
+          return rc;
+        k.smem = smem_bytes;
+      }
+      *out = k;
+      return TT_OK;
+    }
+  }
+  if (int rc = check_cuda(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes),
+                          "cudaFuncSetAttribute"))
+    return rc;
+  cudaFuncAttributes fa;
+  if (int rc = check_cuda(cudaFuncGetAttributes(&fa, fn), "cudaFuncGetAttributes")) return rc;
+  g_kinfo.push_back({fn, dev, smem_bytes, fa.numRegs});
+  *out = g_kinfo.back();
+  return TT_OK;
+}
+
 template <typename K>
 int prepare_kernel(K kernel, int smem_bytes) {
-  return check_cuda(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         smem_bytes),
-                    "cudaFuncSetAttribute");
+  KernelInfo ki;
+  return kernel_info(reinterpret_cast<const void*>(kernel), smem_bytes, &ki);
 }
 
 int after_launch(const char* what) {
@@ -191,7 +226,6 @@ struct Route {
   int out_nst;
   int ffn_in_bn, ffn_in_nst;
   int ffn_out_nst;
-  int attn_exp16;  // 1: probabilities from packed-FP16 exp2, 0: FP32 exp2
   int ffn_fused;   // 1: one fused FFN kernel (d_model in {32, 64, 128, 256}); 0: split route
 };
 
@@ -202,15 +236,15 @@ struct RouteEntry {
 
 const RouteEntry kRouteTable[] = {
     // C1  B64 S128  D128 H4 F128
-    {128, 4, 128, 128, {"d128-h4-s128", 128, 2, 2, 128, 2, 2, 0, 1}},
+    {128, 4, 128, 128, {"d128-h4-s128", 128, 2, 2, 128, 2, 2, 1}},
     // C2  B64 S1024 D128 H4 F128
-    {128, 4, 1024, 128, {"d128-h4-s1024", 128, 2, 2, 128, 2, 2, 0, 1}},
+    {128, 4, 1024, 128, {"d128-h4-s1024", 128, 2, 2, 128, 2, 2, 1}},
     // C3  B256 S256 D32 H2 F128
-    {32, 2, 256, 128, {"d32-h2-s256", 96, 1, 1, 128, 1, 4, 0, 1}},
+    {32, 2, 256, 128, {"d32-h2-s256", 96, 1, 1, 128, 1, 4, 1}},
     // C4  B16 S2048 D512 H8 F2048 (+ key padding)
-    {512, 8, 2048, 2048, {"d512-h8-s2048", 256, 4, 2, 256, 4, 2, 0, 0}},
+    {512, 8, 2048, 2048, {"d512-h8-s2048", 256, 4, 2, 256, 4, 2, 0}},
     // C5  B512 S1024 D256 H8 F1024
-    {256, 8, 1024, 1024, {"d256-h8-s1024", 256, 2, 2, 256, 2, 3, 0, 1}},
+    {256, 8, 1024, 1024, {"d256-h8-s1024", 256, 2, 2, 256, 2, 3, 1}},
 };
 
 int largest_bn_dividing(int n, int cap) {
@@ -252,9 +286,6 @@ int choose_route(int d_model, int heads, int seq, int ffn, Route* out) {
   for (const RouteEntry& e : kRouteTable) {
     if (e.d_model == d_model && e.heads == heads && e.seq == seq && e.ffn == ffn) {
       *out = e.route;
-#ifdef TT_FORCE_ATTN_EXP16
-      out->attn_exp16 = TT_FORCE_ATTN_EXP16;  // build-time override of the table's exponential choice
-#endif
       return TT_OK;
     }
   }
@@ -266,7 +297,6 @@ int choose_route(int d_model, int heads, int seq, int ffn, Route* out) {
   r.ffn_in_bn = largest_bn_dividing(ffn, 256);
   r.ffn_in_nst = 4;
   r.ffn_out_nst = 4;
-  r.attn_exp16 = 0;
   r.ffn_fused = ffn_fusable(d_model, ffn) ? 1 : 0;
   if (r.qkv_bn == 0 || r.ffn_in_bn == 0)
     return fail(TT_ERR_UNSUPPORTED, "no column split for d_model=%d ffn=%d", d_model, ffn);
@@ -455,7 +485,7 @@ int encode_attention_maps(CUtensorMap* tq, CUtensorMap* tk, CUtensorMap* tv, con
 }
 
 int launch_attention(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
-                     const AttnParams& ap, int hd, bool exp16, int sm_count, cudaStream_t stream) {
+                     const AttnParams& ap, int hd, int sm_count, cudaStream_t stream) {
   const long long n_qt = (ap.seq + 127) / 128;
   const long long items = static_cast<long long>(ap.batch) * ap.heads * n_qt;
   if (items > 0x7fffffffLL) return fail(TT_ERR_SHAPE, "batch*heads*query tiles too large");
@@ -465,23 +495,21 @@ int launch_attention(const CUtensorMap& tq, const CUtensorMap& tk, const CUtenso
   if (hd == 8 || hd == 16 || hd == 32) {
     // Two streams per CTA, 64-key tiles, double-buffered scores and probabilities.
     // head_dim 8 runs the head_dim-16 kernel on its zero-padded Q/K/V.
-    auto kern = hd <= 16 ? (exp16 ? attn_db_fwd_kernel<16, true> : attn_db_fwd_kernel<16, false>)
-                         : (exp16 ? attn_db_fwd_kernel<32, true> : attn_db_fwd_kernel<32, false>);
+    auto kern = hd <= 16 ? attn_db_fwd_kernel<16> : attn_db_fwd_kernel<32>;
     const int smem = hd <= 16 ? AttnDbLayout<16>::SMEM_ALLOC : AttnDbLayout<32>::SMEM_ALLOC;
-    if (int rc = prepare_kernel(kern, smem)) return rc;
+    KernelInfo ki;
+    if (int rc = kernel_info(reinterpret_cast<const void*>(kern), smem, &ki)) return rc;
     // The kernel splits its registers with setmaxnreg; that split is only sound
     // when each thread is launched with exactly the planned register count.
-    cudaFuncAttributes fa;
-    if (int rc = check_cuda(cudaFuncGetAttributes(&fa, kern), "cudaFuncGetAttributes")) return rc;
-    if (fa.numRegs != AttnDbLayout<32>::REGS_LAUNCH)
+    if (ki.regs != AttnDbLayout<32>::REGS_LAUNCH)
       return fail(TT_ERR_UNSUPPORTED, "attention kernel built with %d registers per thread, expected %d",
-                  fa.numRegs, AttnDbLayout<32>::REGS_LAUNCH);
+                  ki.regs, AttnDbLayout<32>::REGS_LAUNCH);
     const int ctas = (n_items + AttnDbLayout<32>::NS - 1) / AttnDbLayout<32>::NS;
     const unsigned grid2 = static_cast<unsigned>(ctas < sm_count ? ctas : sm_count);
     kern<<<grid2, AttnDbLayout<32>::THREADS, smem, stream>>>(tq, tk, tv, ap, n_items);
     (void)grid;
   } else if (hd == 64) {
-    auto kern = exp16 ? attn_fwd_kernel<64, true> : attn_fwd_kernel<64, false>;
+    auto kern = attn_fwd_kernel<64>;
     if (int rc = prepare_kernel(kern, AttnLayout<64>::SMEM_ALLOC)) return rc;
     kern<<<grid, 192, AttnLayout<64>::SMEM_ALLOC, stream>>>(tq, tk, tv, ap, n_items);
   } else {
@@ -579,7 +607,13 @@ struct tt_model {
   // Host-buffer pipeline (tt_model_forward_host): one copy stream per
   // direction and per-buffer events, created on first use.
   cudaStream_t h2d = nullptr, d2h = nullptr;
-  cudaEvent_t ev_entry = nullptr, ev_in[2] = {}, ev_comp[2] = {}, ev_out[2] = {};
+  cudaEvent_t ev_entry = nullptr, ev_in[2] = {}, ev_comp[2] = {}, ev_out[2] = {}, ev_join[2] = {};
+  // Batch-shard gather (tt_model_forward_gather): the copy stream that pushes
+  // a finished shard to its destination, the event after each forward, and
+  // the event after the latest push (gather_pending: one was issued).
+  cudaStream_t gather = nullptr;
+  cudaEvent_t ev_fwd_done = nullptr, ev_gathered = nullptr;
+  bool gather_pending = false;
 };
 
 namespace {
@@ -655,7 +689,16 @@ int ensure_copy_streams(tt_model* m) {
   if (int rc = check_cuda(cudaStreamCreateWithFlags(&m->d2h, cudaStreamNonBlocking), "cudaStreamCreate"))
     return rc;
   for (cudaEvent_t* e : {&m->ev_entry, &m->ev_in[0], &m->ev_in[1], &m->ev_comp[0], &m->ev_comp[1],
-                         &m->ev_out[0], &m->ev_out[1]})
+                         &m->ev_out[0], &m->ev_out[1], &m->ev_join[0], &m->ev_join[1]})
+    if (int rc = check_cuda(cudaEventCreateWithFlags(e, cudaEventDisableTiming), "cudaEventCreate")) return rc;
+  return TT_OK;
+}
+
+int ensure_gather_stream(tt_model* m) {
+  if (m->gather) return TT_OK;
+  if (int rc = check_cuda(cudaStreamCreateWithFlags(&m->gather, cudaStreamNonBlocking), "cudaStreamCreate"))
+    return rc;
+  for (cudaEvent_t* e : {&m->ev_fwd_done, &m->ev_gathered})
     if (int rc = check_cuda(cudaEventCreateWithFlags(e, cudaEventDisableTiming), "cudaEventCreate")) return rc;
   return TT_OK;
 }
@@ -685,7 +728,7 @@ int record_end(tt_model* m, cudaStream_t s, int kind, cudaEvent_t start) {
   return check_cuda(cudaEventRecord(end, s), "cudaEventRecord");
 }
 
-int bind_workspace(tt_model* m, int batch, int seq, void* ws, cudaStream_t stream) {
+int bind_workspace(tt_model* m, int batch, int seq, void* ws) {
   if (m->route_seq != seq) {
     if (int rc = choose_route(m->D, m->H, seq, m->F, &m->route)) return rc;
     m->route_seq = seq;
@@ -745,15 +788,6 @@ int bind_workspace(tt_model* m, int batch, int seq, void* ws, cudaStream_t strea
   if (int rc = encode_epi_tile(&m->tm_norm_st, base + w.norm, N, m->D, false)) return rc;
   if (!m->route.ffn_fused)
     if (int rc = encode_epi_tile(&m->tm_hidden_st, base + w.hidden, N, m->F, false)) return rc;
-  // V^T columns in [seq, seq_pad) are never written by the projection; they
-  // must hold finite values because masked probabilities (0) multiply them.
-  if (w.seq_pad != seq)
-    if (int rc = check_cuda(cudaMemsetAsync(base + w.vt, 0,
-                                            static_cast<size_t>(batch) * m->H * stored_head_dim(hd) *
-                                                w.seq_pad * 2,
-                                            stream),
-                            "cudaMemsetAsync"))
-      return rc;
   m->bound_ws = ws;
   m->bound_batch = batch;
   m->bound_seq = seq;
@@ -806,6 +840,18 @@ int tt_watchdog_selftest(unsigned long long timeout_ns, void* stream) {
   if ((w & kDevErrTimeout) && (w & 0xffffu) == 0x7e57u)
     return fail(TT_ERR_TIMEOUT, "watchdog fired as designed (word 0x%x)", w);
   return fail(TT_ERR_LAUNCH, "watchdog did not fire (word 0x%x)", w);
+}
+
+int tt_selftest_exp2_fma(const float* x, float* y32, uint16_t* y16, int n, void* stream) {
+  DeviceState* ds;
+  if (int rc = current_device_state(&ds)) return rc;
+  if (!x || !y32 || !y16 || n < 0 || n % 2 != 0) return fail(TT_ERR_ARG, "invalid argument");
+  if (reinterpret_cast<uintptr_t>(y16) % 4 != 0) return fail(TT_ERR_ALIGN, "y16 must be 4-byte aligned");
+  const int pairs = n / 2;
+  if (pairs == 0) return TT_OK;
+  exp2_fma_probe_kernel<<<(pairs + 255) / 256, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      x, y32, reinterpret_cast<uint32_t*>(y16), pairs);
+  return after_launch("exp2 probe");
 }
 
 int tt_layernorm_rows(const float* x, const float* gamma, const float* beta, void* out,
@@ -894,7 +940,7 @@ int tt_causal_attention(const void* q, const void* k, const void* vt, const uint
   ap.ctx_hd = head_dim;
   ap.err = ds->err;
   ap.timeout_ns = g_timeout_ns.load();
-  return launch_attention(tq, tk, tv, ap, head_dim, false, ds->sm_count, static_cast<cudaStream_t>(stream));
+  return launch_attention(tq, tk, tv, ap, head_dim, ds->sm_count, static_cast<cudaStream_t>(stream));
 }
 
 int tt_causal_attention_masked_noalloc(const void* q, const void* k, const void* vt,
@@ -938,7 +984,7 @@ int tt_causal_attention_masked_noalloc(const void* q, const void* k, const void*
   ap.ctx_hd = head_dim;
   ap.err = ds->err;
   ap.timeout_ns = g_timeout_ns.load();
-  return launch_attention(tq, tk, tv, ap, head_dim, false, ds->sm_count, s);
+  return launch_attention(tq, tk, tv, ap, head_dim, ds->sm_count, s);
 }
 
 int tt_linear_residual_layernorm(const void* a, const void* w, const float* bias,
@@ -1071,9 +1117,8 @@ int tt_route_describe(int d_model, int heads, int seq, int ffn, char* buf, int b
   if (buf && buflen > 0)
     snprintf(buf, buflen,
              "route=%s qkv_bn=%d qkv_nst=%d out_nst=%d ffn_in_bn=%d ffn_in_nst=%d "
-             "ffn_out_nst=%d attn_tile=128x128 attn_exp=%s",
-             r.name, r.qkv_bn, r.qkv_nst, r.out_nst, r.ffn_in_bn, r.ffn_in_nst, r.ffn_out_nst,
-             r.attn_exp16 ? "f16x2" : "f32");
+             "ffn_out_nst=%d",
+             r.name, r.qkv_bn, r.qkv_nst, r.out_nst, r.ffn_in_bn, r.ffn_in_nst, r.ffn_out_nst);
   if (buf && buflen > 0 && r.ffn_fused) {
     const size_t len = strlen(buf);
     snprintf(buf + len, buflen - len > 0 ? buflen - len : 0, " ffn=fused(chunk=128)");
@@ -1120,10 +1165,24 @@ void tt_model_destroy(tt_model* m) {
   for (auto e : m->pool) cudaEventDestroy(e);
   if (m->h2d) cudaStreamDestroy(m->h2d);
   if (m->d2h) cudaStreamDestroy(m->d2h);
+  if (m->gather) cudaStreamDestroy(m->gather);
   for (cudaEvent_t e : {m->ev_entry, m->ev_in[0], m->ev_in[1], m->ev_comp[0], m->ev_comp[1], m->ev_out[0],
-                        m->ev_out[1]})
+                        m->ev_out[1], m->ev_join[0], m->ev_join[1], m->ev_fwd_done, m->ev_gathered})
     if (e) cudaEventDestroy(e);
   delete m;
+}
+
+int tt_workspace_alloc(size_t bytes, void** ptr) {
+  if (!ptr || bytes == 0) return fail(TT_ERR_ARG, "invalid argument");
+  *ptr = nullptr;
+  DeviceState* ds;
+  if (int rc = current_device_state(&ds)) return rc;
+  return check_cuda(cudaMalloc(ptr, bytes), "cudaMalloc(workspace)");
+}
+
+int tt_workspace_free(void* ptr) {
+  if (!ptr) return TT_OK;
+  return check_cuda(cudaFree(ptr), "cudaFree(workspace)");
 }
 
 int tt_model_workspace_bytes(const tt_model* m, int batch, int seq, size_t* bytes) {
@@ -1133,8 +1192,16 @@ int tt_model_workspace_bytes(const tt_model* m, int batch, int seq, size_t* byte
   return TT_OK;
 }
 
-int tt_model_forward(tt_model* m, const float* x, const uint8_t* mask, float* out, int batch,
-                     int seq, void* workspace, size_t workspace_bytes, void* stream) {
+}  // extern "C"
+
+namespace {
+
+// The whole-model forward.  out_guard, when not null, is an event the stream
+// waits on before the first kernel that writes `out` (the last layer's FFN):
+// the batch-shard gather uses it so that a forward can start while the push of
+// the previous forward's output (which reads `out`) is still in flight.
+int model_forward(tt_model* m, const float* x, const uint8_t* mask, float* out, int batch, int seq,
+                  void* workspace, size_t workspace_bytes, cudaStream_t s, cudaEvent_t out_guard) {
   if (!m || !x || !out || !workspace) return fail(TT_ERR_ARG, "null argument");
   DeviceState* ds;
   if (int rc = current_device_state(&ds)) return rc;
@@ -1152,8 +1219,7 @@ int tt_model_forward(tt_model* m, const float* x, const uint8_t* mask, float* ou
     return fail(TT_ERR_ALIGN, "workspace must be 1024-byte aligned");
   if (reinterpret_cast<uintptr_t>(x) % 16 != 0 || reinterpret_cast<uintptr_t>(out) % 16 != 0)
     return fail(TT_ERR_ALIGN, "x and out must be 16-byte aligned");
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
-  if (int rc = bind_workspace(m, batch, seq, workspace, s)) return rc;
+  if (int rc = bind_workspace(m, batch, seq, workspace)) return rc;
   const Route& r = m->route;
   uint8_t* base = static_cast<uint8_t*>(workspace);
   __half* norm = reinterpret_cast<__half*>(base + w.norm);
@@ -1169,6 +1235,17 @@ int tt_model_forward(tt_model* m, const float* x, const uint8_t* mask, float* ou
   CUtensorMap tm_x, tm_out;
   if (int rc = encode_epi_tile(&tm_x, x, Nll, D, true)) return rc;
   if (int rc = encode_epi_tile(&tm_out, out, Nll, D, true)) return rc;
+  // V^T columns [seq, seq_pad) are never written by the projection, yet P.V
+  // multiplies them by the zero probabilities of keys past the sequence, so
+  // they must hold finite values: they are cleared on every forward (the
+  // workspace may have held anything since the last one).
+  if (w.seq_pad != seq)
+    if (int rc = check_cuda(cudaMemset2DAsync(base + w.vt + static_cast<size_t>(seq) * 2,
+                                              static_cast<size_t>(w.seq_pad) * 2, 0,
+                                              static_cast<size_t>(w.seq_pad - seq) * 2,
+                                              static_cast<size_t>(batch) * H * stored_head_dim(hd), s),
+                            "cudaMemset2DAsync(V^T padding)"))
+      return rc;
 
   if (mask) {
     if (int rc = record_begin(m, s, &ev)) return rc;
@@ -1225,7 +1302,7 @@ int tt_model_forward(tt_model* m, const float* x, const uint8_t* mask, float* ou
     }
     // Attention
     if (int rc = record_begin(m, s, &ev)) return rc;
-    if (int rc = launch_attention(m->tm_q, m->tm_k, m->tm_vt, ap, hd, r.attn_exp16 != 0, ds->sm_count, s))
+    if (int rc = launch_attention(m->tm_q, m->tm_k, m->tm_vt, ap, hd, ds->sm_count, s))
       return rc;
     if (int rc = record_end(m, s, TT_KERNEL_ATTN, ev)) return rc;
     // Output projection + residual + norm2
@@ -1252,6 +1329,8 @@ int tt_model_forward(tt_model* m, const float* x, const uint8_t* mask, float* ou
       if (int rc = launch_gemm(m->ksw_out, EPI_RESID_LN, maps, p, ds->sm_count, s)) return rc;
       if (int rc = record_end(m, s, TT_KERNEL_OUT_LN, ev)) return rc;
     }
+    if (last && out_guard)
+      if (int rc = check_cuda(cudaStreamWaitEvent(s, out_guard, 0), "cudaStreamWaitEvent(out guard)")) return rc;
     if (r.ffn_fused && ffn2_route(D, F)) {
       // Whole FFN + residual + next norm, hidden activations in TMEM (final_norm ->
       // FP32 output on the last layer); the residual is updated in place.
@@ -1354,6 +1433,18 @@ int tt_model_forward(tt_model* m, const float* x, const uint8_t* mask, float* ou
   return TT_OK;
 }
 
+}  // namespace
+
+extern "C" {
+
+int tt_model_forward(tt_model* m, const float* x, const uint8_t* mask, float* out, int batch,
+                     int seq, void* workspace, size_t workspace_bytes, void* stream) {
+  if (!m) return fail(TT_ERR_ARG, "null model");
+  // A gather push of an earlier tt_model_forward_gather may still read its `out`.
+  return model_forward(m, x, mask, out, batch, seq, workspace, workspace_bytes, static_cast<cudaStream_t>(stream),
+                       m->gather_pending ? m->ev_gathered : nullptr);
+}
+
 int tt_model_host_workspace_bytes(const tt_model* m, int chunk, int seq, size_t* bytes) {
   if (!m || !bytes) return fail(TT_ERR_ARG, "null argument");
   if (chunk <= 0 || seq <= 0) return fail(TT_ERR_SHAPE, "invalid chunk/seq");
@@ -1362,6 +1453,9 @@ int tt_model_host_workspace_bytes(const tt_model* m, int chunk, int seq, size_t*
 }
 
 namespace {
+
+int host_pipeline(tt_model* m, const float* x, const uint8_t* mask, float* out, int seq, const int* sizes, int n,
+                  int cap, uint8_t* base, const HostWsLayout& h, cudaStream_t s);
 
 // The pipeline over an explicit schedule: chunk i holds sizes[i] sequences
 // (all at most `cap`, the chunk the workspace was sized for).
@@ -1379,12 +1473,26 @@ int forward_host_sched(tt_model* m, const float* x, const uint8_t* mask, float* 
   if (int rc = ensure_copy_streams(m)) return rc;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   uint8_t* base = static_cast<uint8_t*>(workspace);
-  const size_t row_bytes = static_cast<size_t>(m->D) * 4;
-  const size_t model_bytes = ws_layout(m, cap, seq).total;
   // Copies start after the caller's earlier work on the stream (it may still use the workspace).
   if (int rc = check_cuda(cudaEventRecord(m->ev_entry, s), "cudaEventRecord")) return rc;
   cudaStreamWaitEvent(m->h2d, m->ev_entry, 0);
   cudaStreamWaitEvent(m->d2h, m->ev_entry, 0);
+  const int rc = host_pipeline(m, x, mask, out, seq, sizes, n, cap, base, h, s);
+  if (rc != TT_OK) {
+    // Copies already queued may still read x or write out: the caller's stream
+    // completes only after them, so synchronizing it makes the buffers safe to reuse.
+    if (cudaEventRecord(m->ev_join[0], m->h2d) == cudaSuccess) cudaStreamWaitEvent(s, m->ev_join[0], 0);
+    if (cudaEventRecord(m->ev_join[1], m->d2h) == cudaSuccess) cudaStreamWaitEvent(s, m->ev_join[1], 0);
+  }
+  return rc;
+}
+
+// The chunk loop of forward_host_sched (streams and events already set up).
+int host_pipeline(tt_model* m, const float* x, const uint8_t* mask, float* out, int seq, const int* sizes, int n,
+                  int cap, uint8_t* base, const HostWsLayout& h, cudaStream_t s) {
+  const size_t row_bytes = static_cast<size_t>(m->D) * 4;
+  const size_t model_bytes = ws_layout(m, cap, seq).total;
+  void* stream = s;
   int c0 = 0;
   for (int i = 0; i < n; c0 += sizes[i], ++i) {
     const int b = i & 1;
@@ -1463,6 +1571,93 @@ int tt_model_forward_host_chunks(tt_model* m, const float* x, const uint8_t* mas
                             workspace_bytes, stream);
 }
 
+// ---------------------------------------------------------------- batch sharding across GPUs
+
+namespace {
+
+PFN_cuMemGetAddressRange_v3020 g_addr_range = nullptr;
+std::once_flag g_addr_range_once;
+
+int get_addr_range() {
+  std::call_once(g_addr_range_once, [] {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuMemGetAddressRange", &fn, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      g_addr_range = reinterpret_cast<PFN_cuMemGetAddressRange_v3020>(fn);
+  });
+  if (!g_addr_range) return fail(TT_ERR_LAUNCH, "cuMemGetAddressRange entry point not available");
+  return TT_OK;
+}
+
+}  // namespace
+
+int tt_peer_export(const void* dev_ptr, void* handle, size_t* offset) {
+  if (!dev_ptr || !handle || !offset) return fail(TT_ERR_ARG, "null argument");
+  DeviceState* ds;
+  if (int rc = current_device_state(&ds)) return rc;
+  if (int rc = get_addr_range()) return rc;
+  CUdeviceptr base = 0;
+  size_t size = 0;
+  if (g_addr_range(&base, &size, reinterpret_cast<CUdeviceptr>(dev_ptr)) != CUDA_SUCCESS)
+    return fail(TT_ERR_ARG, "pointer %p is not device memory of the current device", dev_ptr);
+  cudaIpcMemHandle_t h;
+  if (int rc = check_cuda(cudaIpcGetMemHandle(&h, reinterpret_cast<void*>(base)), "cudaIpcGetMemHandle")) return rc;
+  memcpy(handle, &h, sizeof(h));
+  *offset = static_cast<size_t>(reinterpret_cast<uintptr_t>(dev_ptr) - static_cast<uintptr_t>(base));
+  return TT_OK;
+}
+
+int tt_peer_open(const void* handle, size_t offset, void** dev_ptr) {
+  if (!handle || !dev_ptr) return fail(TT_ERR_ARG, "null argument");
+  *dev_ptr = nullptr;
+  DeviceState* ds;
+  if (int rc = current_device_state(&ds)) return rc;
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle, sizeof(h));
+  void* base = nullptr;
+  if (int rc = check_cuda(cudaIpcOpenMemHandle(&base, h, cudaIpcMemLazyEnablePeerAccess), "cudaIpcOpenMemHandle"))
+    return rc;
+  *dev_ptr = static_cast<uint8_t*>(base) + offset;
+  return TT_OK;
+}
+
+int tt_peer_close(void* dev_ptr, size_t offset) {
+  if (!dev_ptr) return fail(TT_ERR_ARG, "null argument");
+  return check_cuda(cudaIpcCloseMemHandle(static_cast<uint8_t*>(dev_ptr) - offset), "cudaIpcCloseMemHandle");
+}
+
+int tt_model_forward_gather(tt_model* m, const float* x, const uint8_t* mask, float* out, float* gather_dst,
+                            int batch, int seq, void* workspace, size_t workspace_bytes, void* stream) {
+  if (!m) return fail(TT_ERR_ARG, "null model");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (gather_dst == nullptr || gather_dst == out)
+    return model_forward(m, x, mask, out, batch, seq, workspace, workspace_bytes, s,
+                         m->gather_pending ? m->ev_gathered : nullptr);
+  if (reinterpret_cast<uintptr_t>(gather_dst) % 16 != 0) return fail(TT_ERR_ALIGN, "gather_dst must be 16-byte aligned");
+  if (int rc = ensure_gather_stream(m)) return rc;
+  // The previous push may still be reading `out`: the last layer's FFN waits for it.
+  if (int rc = model_forward(m, x, mask, out, batch, seq, workspace, workspace_bytes, s,
+                             m->gather_pending ? m->ev_gathered : nullptr))
+    return rc;
+  if (int rc = check_cuda(cudaEventRecord(m->ev_fwd_done, s), "cudaEventRecord")) return rc;
+  if (int rc = check_cuda(cudaStreamWaitEvent(m->gather, m->ev_fwd_done, 0), "cudaStreamWaitEvent")) return rc;
+  const size_t bytes = static_cast<size_t>(batch) * seq * m->D * sizeof(float);
+  if (int rc = check_cuda(cudaMemcpyAsync(gather_dst, out, bytes, cudaMemcpyDefault, m->gather),
+                          "cudaMemcpyAsync(gather push)"))
+    return rc;
+  if (int rc = check_cuda(cudaEventRecord(m->ev_gathered, m->gather), "cudaEventRecord")) return rc;
+  m->gather_pending = true;
+  return TT_OK;
+}
+
+int tt_model_gather_wait(tt_model* m, void* stream) {
+  if (!m) return fail(TT_ERR_ARG, "null model");
+  if (!m->gather_pending) return TT_OK;
+  return check_cuda(cudaStreamWaitEvent(static_cast<cudaStream_t>(stream), m->ev_gathered, 0),
+                    "cudaStreamWaitEvent(gather)");
+}
+
 struct tt_graph {
   cudaGraph_t graph = nullptr;
   cudaGraphExec_t exec = nullptr;
@@ -1486,7 +1681,7 @@ int tt_model_graph_create(tt_model* m, const float* x, const uint8_t* mask, floa
   g->device = dev;
   int rc = check_cuda(cudaStreamBeginCapture(cs, cudaStreamCaptureModeRelaxed), "cudaStreamBeginCapture");
   if (rc == TT_OK) {
-    const int frc = tt_model_forward(m, x, mask, out, batch, seq, workspace, workspace_bytes, cs);
+    const int frc = model_forward(m, x, mask, out, batch, seq, workspace, workspace_bytes, cs, nullptr);
     const int erc = check_cuda(cudaStreamEndCapture(cs, &g->graph), "cudaStreamEndCapture");
     rc = frc != TT_OK ? frc : erc;
   }

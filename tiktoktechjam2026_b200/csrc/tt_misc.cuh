@@ -120,4 +120,16 @@ __global__ void watchdog_selftest_kernel(unsigned int* err, unsigned long long t
   __syncthreads();
 }
 
+// The FMA-pipe exponential of the attention softmax on pairs of inputs:
+// y32 = exp2_pair_fma (FP32), y16 = exp2_pair_fma_f16 (FP16 bits).  Test probe.
+__global__ void exp2_fma_probe_kernel(const float* x, float* y32, uint32_t* y16, int n_pairs) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n_pairs) return;
+  const uint64_t xx = f2_pack(x[2 * i], x[2 * i + 1]);
+  const uint64_t y = exp2_pair_fma(xx);
+  y32[2 * i] = f2_lo(y);
+  y32[2 * i + 1] = f2_hi(y);
+  y16[i] = exp2_pair_fma_f16(xx);
+}
+
 }  // namespace tt

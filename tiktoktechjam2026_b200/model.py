@@ -13,6 +13,8 @@ from __future__ import annotations
 
 import copy
 import ctypes
+import itertools
+import weakref
 from dataclasses import dataclass
 from typing import Dict, Optional, Sequence
 
@@ -117,7 +119,6 @@ class _DevicePlan:
         with torch.cuda.device(device):
             _lib.check(_lib.lib().tt_model_create(ctypes.byref(desc), ctypes.byref(handle)))
         self.handle = handle
-        self._ws: Optional[torch.Tensor] = None
         self._ws_ptr = 0
         self._ws_bytes = 0
 
@@ -157,18 +158,35 @@ class _DevicePlan:
         return self._reserve(int(nbytes.value))
 
     def _reserve(self, need: int):
-        if self._ws is None or self._ws_bytes < need:
-            self._ws = None
-            raw = torch.empty(need + 1024, dtype=torch.uint8, device=self.device)
-            base = raw.data_ptr()
-            self._ws = raw
-            self._ws_ptr = (base + 1023) // 1024 * 1024
-            self._ws_bytes = need + 1024 - (self._ws_ptr - base)
+        """The workspace, grown to ``need`` bytes.  It is the library's own cudaMalloc
+        (tt_workspace_alloc), not a PyTorch tensor: a forward first run inside a CUDA-graph
+        warm-up (torch.compile(mode="reduce-overhead")) must not leave a live allocation in
+        the graph's memory pool."""
+        if self._ws_bytes < need:
+            with torch.cuda.device(self.device):
+                torch.cuda.current_stream(self.device).synchronize()  # the old one may be in use
+                self._free_ws()
+                ptr = ctypes.c_void_p()
+                _lib.check(_lib.lib().tt_workspace_alloc(need + 1024, ctypes.byref(ptr)))
+            self._ws_raw = ptr.value
+            self._ws_ptr = (ptr.value + 1023) // 1024 * 1024
+            self._ws_bytes = need + 1024 - (self._ws_ptr - ptr.value)
         return self._ws_ptr, self._ws_bytes
+
+    def _free_ws(self) -> None:
+        raw = getattr(self, "_ws_raw", 0)
+        if raw:
+            _lib.lib().tt_workspace_free(raw)
+        self._ws_raw = 0
+        self._ws_ptr = 0
+        self._ws_bytes = 0
 
     def close(self) -> None:
         if getattr(self, "handle", None) is not None and self.handle.value:
             try:
+                with torch.cuda.device(self.device):
+                    torch.cuda.current_stream(self.device).synchronize()
+                    self._free_ws()
                 _lib.lib().tt_model_destroy(self.handle)
             except Exception:  # pragma: no cover - interpreter teardown
                 pass
@@ -219,6 +237,17 @@ class B200Transformer(nn.Module):
         self.assume_all_tokens_valid = False
         self._bias_fp32: Dict[str, torch.Tensor] = {}
         self._plans: Dict[str, _DevicePlan] = {}
+        self._op_key = _register(self)
+
+    def __deepcopy__(self, memo):
+        # Device plans hold C handles and are rebuilt on first use; the copy gets its own op key.
+        cls = self.__class__
+        new = cls.__new__(cls)
+        memo[id(self)] = new
+        for k, v in self.__dict__.items():
+            new.__dict__[k] = {} if k == "_plans" else copy.deepcopy(v, memo)
+        new._op_key = _register(new)
+        return new
 
     # -- reference surface ---------------------------------------------------
     def convert_projections_to_fp16(self) -> None:
@@ -293,8 +322,17 @@ class B200Transformer(nn.Module):
             return self.forward_host(x, valid_token_mask)
         if x.dim() != 3 or x.shape[-1] != self.config.d_model:
             raise ValueError(f"expected x of shape [B, S, {self.config.d_model}], got {tuple(x.shape)}")
-        B, S, _ = x.shape
         mask = None if self.assume_all_tokens_valid else valid_token_mask
+        if mask is not None and tuple(mask.shape) != tuple(x.shape[:2]):
+            raise ValueError(f"valid_token_mask must have shape {tuple(x.shape[:2])}, got {tuple(mask.shape)}")
+        # One custom op (tt_b200::model_forward): opaque to torch.compile, its fake
+        # implementation gives the output's shape, and a CUDA-graph capture of it
+        # records only this library's kernel launches.
+        return torch.ops.tt_b200.model_forward(x, mask, self._op_key)
+
+    def _forward_device(self, x: torch.Tensor, mask: Optional[torch.Tensor]) -> torch.Tensor:
+        """The body of tt_b200::model_forward: one tt_model_forward call on x's device."""
+        B, S, _ = x.shape
         x = x.contiguous()
         out = torch.empty_like(x)
         if B == 0 or S == 0:
@@ -302,8 +340,6 @@ class B200Transformer(nn.Module):
         plan = self._plan(x.device)
         mask_ptr = 0
         if mask is not None:
-            if mask.shape != (B, S):
-                raise ValueError(f"valid_token_mask must have shape {(B, S)}, got {tuple(mask.shape)}")
             mask8 = mask.to(device=x.device, dtype=torch.bool).contiguous().view(torch.uint8)
             mask_ptr = mask8.data_ptr()
         ws_ptr, ws_bytes = plan.workspace(B, S)
@@ -316,6 +352,59 @@ class B200Transformer(nn.Module):
             )
         return out
 
+    def reserve_workspace(self, batch: int, seq: int, device: Optional[torch.device] = None) -> None:
+        """Allocates the device workspace for ``batch`` x ``seq`` now and runs one forward of zeros,
+        so that later calls of that size or smaller allocate nothing and set nothing up (what a
+        CUDA-graph capture of the forward, e.g. torch.compile(mode="reduce-overhead"), needs)."""
+        dev = torch.device(device) if device is not None else next(self.parameters()).device
+        plan = self._plan(dev)
+        plan.workspace(batch, seq)
+        with torch.inference_mode():
+            self._forward_device(torch.zeros(batch, seq, self.config.d_model, device=dev), None)
+
+
+    def forward_gather(
+        self,
+        x: torch.Tensor,
+        valid_token_mask: Optional[torch.Tensor],
+        out: torch.Tensor,
+        gather_dst: int = 0,
+    ) -> torch.Tensor:
+        """``forward`` of this GPU's batch slice into ``out``, then pushed to ``gather_dst``.
+
+        ``gather_dst`` is a device address on another GPU (a ``PeerGatherBuffer``
+        slice) or 0.  One ``tt_model_forward_gather`` call: the push runs on the
+        copy engines while later work on the current stream computes; the next
+        call's last layer waits for it before rewriting ``out``.  Call
+        ``gather_wait`` before relying on the destination.
+        """
+        if x.dtype != torch.float32 or not x.is_cuda or x.dim() != 3 or x.shape[-1] != self.config.d_model:
+            raise ValueError("forward_gather takes an FP32 CUDA tensor [B, S, d_model]")
+        if out.shape != x.shape or out.dtype != torch.float32 or out.device != x.device or not out.is_contiguous():
+            raise ValueError("out must be a contiguous FP32 tensor shaped like x on x's device")
+        B, S, _ = x.shape
+        mask = None if self.assume_all_tokens_valid else valid_token_mask
+        x = x.contiguous()
+        plan = self._plan(x.device)
+        mask_ptr = 0
+        if mask is not None:
+            if mask.shape != (B, S):
+                raise ValueError(f"valid_token_mask must have shape {(B, S)}, got {tuple(mask.shape)}")
+            mask8 = mask.to(device=x.device, dtype=torch.bool).contiguous().view(torch.uint8)
+            mask_ptr = mask8.data_ptr()
+        ws_ptr, ws_bytes = plan.workspace(B, S)
+        with torch.cuda.device(x.device):
+            stream = torch.cuda.current_stream(x.device).cuda_stream
+            _lib.check(_lib.lib().tt_model_forward_gather(plan.handle, x.data_ptr(), mask_ptr, out.data_ptr(),
+                                                          gather_dst or None, B, S, ws_ptr, ws_bytes, stream))
+        return out
+
+    def gather_wait(self, device: Optional[torch.device] = None) -> None:
+        """Makes the current stream wait for every push ``forward_gather`` issued on ``device``."""
+        dev = torch.device(device) if device is not None else next(self.parameters()).device
+        with torch.cuda.device(dev):
+            stream = torch.cuda.current_stream(dev).cuda_stream
+            _lib.check(_lib.lib().tt_model_gather_wait(self._plan(dev).handle, stream))
 
     def forward_host(
         self,
@@ -352,9 +441,10 @@ class B200Transformer(nn.Module):
             x = x.pin_memory()
         if out is None:
             out = torch.empty(x.shape, dtype=torch.float32, pin_memory=True)
-        elif out.shape != x.shape or out.dtype != torch.float32 or out.is_cuda or not out.is_contiguous() \
-                or not out.is_pinned():
-            raise ValueError("out must be a contiguous pinned FP32 host tensor shaped like x")
+        elif out.shape != x.shape or out.dtype != torch.float32 or out.is_cuda or not out.is_contiguous():
+            # (the library itself rejects pageable memory: out may also be host memory that was
+            # page-locked with cudaHostRegister, which torch does not always report as pinned)
+            raise ValueError("out must be a contiguous page-locked FP32 host tensor shaped like x")
         if B == 0 or S == 0:
             return out
         mask = None if self.assume_all_tokens_valid else valid_token_mask
@@ -453,6 +543,34 @@ class GraphedForward:
 
     def __del__(self) -> None:  # pragma: no cover
         self.close()
+
+
+# ---------------------------------------------------------------- the custom op
+# Models are reached from the op by an integer key (the op's arguments can only be
+# tensors and scalars); the registry holds weak references.
+_REGISTRY: Dict[int, "weakref.ReferenceType[B200Transformer]"] = {}
+_KEYS = itertools.count(1)
+
+
+def _register(model: "B200Transformer") -> int:
+    key = next(_KEYS)
+    _REGISTRY[key] = weakref.ref(model)
+    return key
+
+
+@torch.library.custom_op("tt_b200::model_forward", mutates_args=())
+def _model_forward_op(x: torch.Tensor, mask: Optional[torch.Tensor], key: int) -> torch.Tensor:
+    """FP32 [B, S, D] -> FP32 [B, S, D]: the whole forward (tt_model_forward) of the model registered as key."""
+    ref = _REGISTRY.get(key)
+    model = ref() if ref is not None else None
+    if model is None:
+        raise RuntimeError(f"tt_b200::model_forward: no live model under key {key}")
+    return model._forward_device(x, mask)
+
+
+@_model_forward_op.register_fake
+def _(x: torch.Tensor, mask: Optional[torch.Tensor], key: int) -> torch.Tensor:
+    return torch.empty_like(x, memory_format=torch.contiguous_format)
 
 
 def default_host_chunk(batch: int, seq: int, d_model: int) -> int:

@@ -9,10 +9,13 @@ gather of the outputs to rank 0.  One process per GPU; ranks come from
 
 from __future__ import annotations
 
-from typing import Callable, Optional, Tuple
+import ctypes
+from typing import Callable, List, Optional, Sequence, Tuple
 
 import torch
 import torch.distributed as dist
+
+from . import _lib
 
 
 def shard_bounds(batch: int, world: int, rank: int) -> Tuple[int, int]:
@@ -59,3 +62,73 @@ def gather_to_rank0(local: torch.Tensor, batch: int, rank: int, world: int, grou
         s, e = shard_bounds(batch, world, r)
         parts.append(bufs[r][: e - s])
     return torch.cat(parts, dim=0)
+
+
+class PeerGatherBuffer:
+    """One FP32 output buffer on rank 0's GPU that every rank's batch slice is pushed into.
+
+    Rank 0 allocates ``slots`` buffers shaped ``[batch, *row_shape]`` and exports
+    them (``tt_peer_export``); the other ranks map them into their own address
+    space (``tt_peer_open``), so ``dst(slot)`` is where this rank's slice goes:
+    on rank 0 its own memory (the forward writes there directly), on the
+    others rank 0's memory across NVLink, written by the copy engines
+    (``tt_model_forward_gather``).  The handles travel through the process
+    group's object collectives; nothing is exchanged during compute.
+    """
+
+    def __init__(self, batch: int, row_shape: Sequence[int], rank: int, world: int, device: torch.device,
+                 slots: int = 1, group=None) -> None:
+        self.batch = batch
+        self.row_shape = tuple(int(d) for d in row_shape)
+        self.rank, self.world = rank, world
+        self.start, self.stop = shard_bounds(batch, world, rank)
+        row_elems = 1
+        for d in self.row_shape:
+            row_elems *= d
+        self._row_bytes = row_elems * 4
+        self.buffers: List[torch.Tensor] = []
+        self._opened: List[Tuple[int, int]] = []
+        handles = None
+        if rank == 0:
+            handles = []
+            for _ in range(slots):
+                buf = torch.empty((batch,) + self.row_shape, dtype=torch.float32, device=device)
+                self.buffers.append(buf)
+                h = (ctypes.c_char * _lib.TT_PEER_HANDLE_BYTES)()
+                off = ctypes.c_size_t()
+                with torch.cuda.device(device):
+                    _lib.check(_lib.lib().tt_peer_export(buf.data_ptr(), h, ctypes.byref(off)))
+                handles.append((bytes(h), int(off.value)))
+        if world > 1:
+            box = [handles]
+            dist.broadcast_object_list(box, src=0, group=group)
+            handles = box[0]
+        self._bases: List[int] = []
+        if rank == 0:
+            self._bases = [b.data_ptr() for b in self.buffers]
+        else:
+            with torch.cuda.device(device):
+                for raw, off in handles:
+                    ptr = ctypes.c_void_p()
+                    h = (ctypes.c_char * _lib.TT_PEER_HANDLE_BYTES).from_buffer_copy(raw)
+                    _lib.check(_lib.lib().tt_peer_open(h, off, ctypes.byref(ptr)))
+                    self._opened.append((ptr.value, off))
+                    self._bases.append(ptr.value)
+
+    def dst(self, slot: int = 0) -> int:
+        """Device address of this rank's slice of buffer ``slot`` (rank 0's memory)."""
+        return self._bases[slot] + self.start * self._row_bytes
+
+    def local_view(self, slot: int = 0) -> torch.Tensor:
+        """Rank 0: buffer ``slot`` as a tensor (the gathered batch once every push has landed)."""
+        if self.rank != 0:
+            raise RuntimeError("only rank 0 holds the gather buffer")
+        return self.buffers[slot]
+
+    def close(self) -> None:
+        for ptr, off in self._opened:
+            try:
+                _lib.lib().tt_peer_close(ptr, off)
+            except Exception:  # pragma: no cover - interpreter teardown
+                pass
+        self._opened = []
