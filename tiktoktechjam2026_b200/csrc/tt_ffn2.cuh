@@ -28,9 +28,14 @@
 // r' = acc2 + b2 + r (the residual rows bulk-prefetched into L2 a tile ahead,
 // then staged by cp.async AHEAD = 6 16-column jobs ahead), accumulates
 // shifted FP32 sums for the LayerNorm statistics and writes r' with coalesced
-// stores; acc2 is released right after that pass, so the next tile's G2
-// starts while the second pass re-reads the warp's own r' rows (L2 hits) and
-// writes the normalized rows.  d_model 128 double-buffers acc2 in TMEM.
+// stores; the second pass re-reads the warp's own r' rows (L2 hits) and
+// writes the normalized rows.  acc2 is read 64 columns at a time into
+// registers and each 64-column block is released as soon as it is loaded:
+// the next tile's first G2 chunk is issued as D / 64 MMAs of N = 64, each
+// waiting only for its own block, so the tensor core resumes while the
+// epilogue is still at the start of its first pass (with a single
+// accumulator it used to idle until the whole pass was done).  d_model 128
+// double-buffers acc2 in TMEM as well.
 // Warp 12 loads A and the even ring slots, warp 14 the odd ones (more
 // producers: warps 14, 15, ... own slots st % producers); warp 13 allocates
 // TMEM and issues the MMAs.
@@ -58,16 +63,10 @@ struct Ffn2Layout {
 #ifndef TT_FFN2_AHEAD
 #define TT_FFN2_AHEAD 6
 #endif
-#ifndef TT_FFN2_FC256
-#define TT_FFN2_FC256 128
-#endif
-#ifndef TT_FFN2_LAG256
-#define TT_FFN2_LAG256 1
-#endif
-  // Hidden units per chunk (d_model 256 may take 64), TMEM buffers of the
-  // chunk accumulator (columns 256..511), and how many chunks G2 trails G1.
-  static constexpr int FC = D == 256 ? TT_FFN2_FC256 : 128, KB = 64, NST = TT_FFN2_NST, SLOT = 32768;
-  static constexpr int NACC1 = 256 / FC, LAG = D == 256 ? TT_FFN2_LAG256 : 1;
+  // Hidden units per chunk, TMEM buffers of the chunk accumulator (columns
+  // 256..511), and how many chunks G2 trails G1.
+  static constexpr int FC = 128, KB = 64, NST = TT_FFN2_NST, SLOT = 32768;
+  static constexpr int NACC1 = 256 / FC, LAG = 1;
   static constexpr int NKA = D / KB;                 // K-blocks of G1
   static constexpr int A_KBLK = 128 * KB * 2;        // 16 KB
   static constexpr int A_BYTES = NKA * A_KBLK;
@@ -87,13 +86,16 @@ struct Ffn2Layout {
   static constexpr int OFF_LN = OFF_W + NST * SLOT;
   static constexpr int OFF_F32 = OFF_LN + 4 * RING * TILE;  // b2, gamma, beta
   static constexpr int OFF_BAR = OFF_F32 + 3 * D * 4;
-  // a_full a_empty w_full[NST] w_empty[NST] acc1_full[NACC1] h_full[NACC1] acc2_full[2] acc2_empty[2] done
-  static constexpr int NBAR = 2 + 2 * NST + 2 * NACC1 + 4 + 1;
+  static constexpr int NBLK = D / 64;  // 64-column blocks of acc2, released one by one
+  // a_full a_empty w_full[NST] w_empty[NST] acc1_full[NACC1] h_full[NACC1] acc2_full[2]
+  // acc2_empty[2][NBLK] done
+  static constexpr int NBAR = 2 + 2 * NST + 2 * NACC1 + 2 + 2 * NBLK + 1;
   static constexpr int OFF_MISC = OFF_BAR + NBAR * 8;
   static constexpr int SMEM_ALLOC = OFF_MISC + 16 + 1024;
   static constexpr int NACC2 = D <= 128 ? 2 : 1;  // acc2 buffers (TMEM columns [j * D, (j + 1) * D))
   static constexpr int TMEM_ACC1 = 256;           // acc1 buffer b at columns 256 + FC b
   static_assert(D == 128 || D == 256, "this kernel covers d_model 128 and 256");
+  static_assert(D % 64 == 0 && 64 % JW == 0, "acc2 released in 64-column blocks of whole jobs");
   static_assert(W1_SLOTS >= 1 && W2_SLOTS >= 1 && W1_PER_SLOT * W1_KBLK == SLOT && W2_PER_SLOT * W2_KBLK == SLOT,
                 "slot shapes");
   static_assert(NACC2 * D <= TMEM_ACC1, "TMEM budget");
@@ -133,8 +135,8 @@ __global__ void __launch_bounds__(kFfn2Threads, 1)
   uint64_t* acc1_full = w_empty + NST;
   uint64_t* h_full = acc1_full + L::NACC1;
   uint64_t* acc2_full = h_full + L::NACC1;
-  uint64_t* acc2_empty = acc2_full + 2;
-  uint64_t* done = acc2_empty + 2;
+  uint64_t* acc2_empty = acc2_full + 2;  // [buffer][64-column block]
+  uint64_t* done = acc2_empty + 2 * L::NBLK;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::OFF_MISC);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::OFF_MISC + 4);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -151,10 +153,8 @@ __global__ void __launch_bounds__(kFfn2Threads, 1)
       mbar_init(&acc1_full[i], 1);
       mbar_init(&h_full[i], 8);
     }
-    for (int i = 0; i < 2; ++i) {
-      mbar_init(&acc2_full[i], 1);
-      mbar_init(&acc2_empty[i], 4);
-    }
+    for (int i = 0; i < 2; ++i) mbar_init(&acc2_full[i], 1);
+    for (int i = 0; i < 2 * L::NBLK; ++i) mbar_init(&acc2_empty[i], 4);
     mbar_init(done, 1);
     *abort_flag = 0;
     fence_mbar_init();
@@ -234,6 +234,7 @@ __global__ void __launch_bounds__(kFfn2Threads, 1)
     if (lane == 0) {
       const uint32_t idesc1 = umma_idesc_f16_f32(128, FC);
       const uint32_t idesc2 = umma_idesc_f16_f32(128, D);
+      const uint32_t idesc2b = umma_idesc_f16_f32(128, 64);  // one 64-column block of acc2
       const uint32_t sA = smem_u32(smem + L::OFF_A);
       const uint32_t sW = smem_u32(smem + L::OFF_W);
       int g = 0, i = 0, cg = 0;
@@ -272,10 +273,39 @@ __global__ void __launch_bounds__(kFfn2Threads, 1)
             // G2(step - LAG): acc2 += H(c) . W2[:, chunk c]^T with H(c) in TMEM.
             const int c = cg + step - L::LAG, hb = c % L::NACC1;
             const uint32_t th = tmem_base + L::TMEM_ACC1 + hb * FC;
-            if (step == L::LAG && !(ok = wait_phase(&acc2_empty[ib], ((i / L::NACC2) & 1) ^ 1, wd, 0x613))) break;
             if (!(ok = wait_phase(&h_full[hb], (c / L::NACC1) & 1, wd, 0x614))) break;
             tc_fence_after();
-            for (int s = 0; ok && s < L::W2_SLOTS; ++s, ++g) {
+            if (step == L::LAG) {
+              // The tile's first G2 chunk: acc2 block by block, each as soon as the
+              // previous tile's epilogue has loaded it (N = 64 MMAs on rows 64 blk.. of W2).
+              for (int s = 0; ok && s < L::W2_SLOTS; ++s)
+                ok = wait_phase(&w_full[(g + s) % NST], ((g + s) / NST) & 1, wd, 0x615);
+              if (!ok) break;
+              for (int blk = 0; ok && blk < L::NBLK; ++blk) {
+                if (!(ok = wait_phase(&acc2_empty[ib * L::NBLK + blk], ((i / L::NACC2) & 1) ^ 1, wd, 0x613)))
+                  break;
+                tc_fence_after();
+                for (int s = 0; s < L::W2_SLOTS; ++s) {
+                  const int st = (g + s) % NST;
+#pragma unroll
+                  for (int q = 0; q < L::W2_PER_SLOT; ++q) {
+                    const int hk = s * L::W2_PER_SLOT + q;
+#pragma unroll
+                    for (int kk = 0; kk < L::KB / 16; ++kk) {
+                      const int u = hk * 4 + kk;
+                      const uint32_t ta = th + (u / (FC / 32)) * (FC / 2) + (u % (FC / 32)) * 8;
+                      const uint64_t db = umma_sdesc(sW + st * L::SLOT + q * L::W2_KBLK + blk * 64 * 128 + kk * 32,
+                                                     1024, kSw128);
+                      umma_f16_ts(tacc2 + blk * 64, ta, db, idesc2b, (hk > 0 || kk > 0) ? 1u : 0u);
+                    }
+                  }
+                }
+              }
+              if (!ok) break;
+              for (int s = 0; s < L::W2_SLOTS; ++s) umma_commit(&w_empty[(g + s) % NST]);
+              g += L::W2_SLOTS;
+            }
+            for (int s = 0; ok && step > L::LAG && s < L::W2_SLOTS; ++s, ++g) {
               const int st = g % NST;
               if (!(ok = wait_phase(&w_full[st], (g / NST) & 1, wd, 0x615))) break;
               tc_fence_after();
@@ -438,42 +468,49 @@ __global__ void __launch_bounds__(kFfn2Threads, 1)
       };
       if (!(ok = warp_wait_phase(&acc2_full[ib], (i / L::NACC2) & 1, wd, 0x631))) break;
       tc_fence_after();
-      // Pass 1: r' = acc2 + b2 + r; statistics; r' out.
+      // Pass 1: r' = acc2 + b2 + r; statistics; r' out.  acc2 comes into registers 64
+      // columns at a time, and each block is released once loaded.
       float shift = 0.f, s1 = 0.f, s2 = 0.f;
+      constexpr int JPB = 64 / JW;  // jobs per 64-column block
 #pragma unroll 1
-      for (int c = 0; c < nch; ++c) {
-        uint32_t v[JW];
-        tmem_ld_x16(tacc2 + c * JW, v);
-        const uint32_t slot = advance(c);
-        float x[JW];
-        read_row(slot, x);
-        tmem_ld_wait_tied(v);
-        if (c == nch - 1) {
-          tc_fence_before();
+      for (int blk = 0; blk < L::NBLK; ++blk) {
+        uint32_t v[2][32];
+        tmem_ld_x32(tacc2 + blk * 64, v[0]);
+        tmem_ld_x32(tacc2 + blk * 64 + 32, v[1]);
+        tmem_ld_wait_tied(v[0]);
+        tmem_ld_wait_tied(v[1]);
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&acc2_empty[ib * L::NBLK + blk]);  // the next tile's G2 may take it
+#pragma unroll
+        for (int jj = 0; jj < JPB; ++jj) {
+          const int c = blk * JPB + jj;
+          const uint32_t slot = advance(c);
+          float x[JW];
+          read_row(slot, x);
+          const float4* b2 = reinterpret_cast<const float4*>(s_b2 + c * JW);
+#pragma unroll
+          for (int k = 0; k < PR; ++k) {
+            const float4 bb = b2[k];
+            const uint32_t* vv = &v[(jj * JW) / 32][(jj * JW) % 32 + 4 * k];
+            x[4 * k] += __uint_as_float(vv[0]) + bb.x;
+            x[4 * k + 1] += __uint_as_float(vv[1]) + bb.y;
+            x[4 * k + 2] += __uint_as_float(vv[2]) + bb.z;
+            x[4 * k + 3] += __uint_as_float(vv[3]) + bb.w;
+          }
+          if (c == 0) shift = x[0];
+#pragma unroll
+          for (int e = 0; e < JW; ++e) {
+            const float d = x[e] - shift;
+            s1 += d;
+            s2 = fmaf(d, d, s2);
+          }
           __syncwarp();
-          if (lane == 0) mbar_arrive(&acc2_empty[ib]);  // acc2 may take the next tile's G2
+          write_row(slot, x);
+          __syncwarp();
+          store_f32(slot, p.resid_out, r0, c);
+          __syncwarp();
         }
-        const float4* b2 = reinterpret_cast<const float4*>(s_b2 + c * JW);
-#pragma unroll
-        for (int k = 0; k < PR; ++k) {
-          const float4 bb = b2[k];
-          x[4 * k] += __uint_as_float(v[4 * k]) + bb.x;
-          x[4 * k + 1] += __uint_as_float(v[4 * k + 1]) + bb.y;
-          x[4 * k + 2] += __uint_as_float(v[4 * k + 2]) + bb.z;
-          x[4 * k + 3] += __uint_as_float(v[4 * k + 3]) + bb.w;
-        }
-        if (c == 0) shift = x[0];
-#pragma unroll
-        for (int e = 0; e < JW; ++e) {
-          const float d = x[e] - shift;
-          s1 += d;
-          s2 = fmaf(d, d, s2);
-        }
-        __syncwarp();
-        write_row(slot, x);
-        __syncwarp();
-        store_f32(slot, p.resid_out, r0, c);
-        __syncwarp();
       }
       const float inv_d = 1.f / static_cast<float>(D);
       const float m1 = s1 * inv_d;
