@@ -41,6 +41,13 @@
 
 namespace tt {
 
+#ifndef TT_DB_REGS_SOFTMAX
+#define TT_DB_REGS_SOFTMAX 216
+#endif
+#ifndef TT_DB_REGS_OTHER
+#define TT_DB_REGS_OTHER 56
+#endif
+
 template <int HD>
 struct AttnDbLayout {
   static constexpr int NS = 2;   // independent pipelines per CTA
@@ -82,7 +89,7 @@ struct AttnDbLayout {
   // REGS_LAUNCH registers per thread (a split above the launch total would make
   // setmaxnreg.inc wait forever).
   static constexpr int REGS_LAUNCH = 168;
-  static constexpr int REGS_SOFTMAX = 216, REGS_OTHER = 56;
+  static constexpr int REGS_SOFTMAX = TT_DB_REGS_SOFTMAX, REGS_OTHER = TT_DB_REGS_OTHER;
   static_assert(NWARPS % 4 == 0, "whole warpgroups");
   static_assert(128 * NS * REGS_SOFTMAX + 32 * (NWARPS - 4 * NS) * REGS_OTHER <= THREADS * REGS_LAUNCH,
                 "register split");
@@ -164,6 +171,8 @@ __global__ void __launch_bounds__(AttnDbLayout<HD>::THREADS, 1)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
+  pdl_wait();  // activations of the previous kernel are final from here on
+  pdl_trigger();
   const uint32_t tmem_base = *tmem_slot;
   const Watchdog wd{p.err, abort_flag, p.timeout_ns};
 

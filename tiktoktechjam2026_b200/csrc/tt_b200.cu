@@ -13,6 +13,7 @@
 #include <cstdio>
 #include <cstring>
 #include <mutex>
+#include <utility>
 #include <vector>
 
 #include "tt_attention.cuh"
@@ -209,6 +210,34 @@ int prepare_kernel(K kernel, int smem_bytes) {
   return kernel_info(reinterpret_cast<const void*>(kernel), smem_bytes, &ki);
 }
 
+// Kernels of a whole-model forward are launched with programmatic stream
+// serialization (each starts its set-up while its predecessor drains; see
+// pdl_wait in tt_ptx.cuh).  Single-op entry points launch plainly: their
+// callers may have written the weights they stage with the kernel just before.
+thread_local bool t_pdl = false;
+
+struct PdlScope {
+  bool prev;
+  PdlScope() : prev(t_pdl) { t_pdl = true; }
+  ~PdlScope() { t_pdl = prev; }
+};
+
+template <typename... KArgs, typename... Args>
+void launch_kernel(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                   Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = t_pdl ? 1 : 0;
+  cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);  // errors surface in after_launch
+}
+
 int after_launch(const char* what) {
   const cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return fail(TT_ERR_LAUNCH, "%s launch: %s", what, cudaGetErrorString(e));
@@ -317,7 +346,7 @@ int launch_gemm_t(const GemmMaps& maps, GemmParams p, int sm_count, cudaStream_t
   if (items > 0x7fffffffLL) return fail(TT_ERR_SHAPE, "too many tiles");
   p.n_items = static_cast<int>(items);
   const unsigned grid = static_cast<unsigned>(items < sm_count ? items : sm_count);
-  kern<<<grid, gemm_threads(EPI), smem, stream>>>(maps, p);
+  launch_kernel(kern, grid, gemm_threads(EPI), smem, stream, maps, p);
   return after_launch("gemm");
 }
 
@@ -352,7 +381,7 @@ int launch_ffn(const FfnMaps& maps, FfnParams p, int sm_count, cudaStream_t stre
     const int smem = FfnLayout<DD>::smem_bytes(p.F);                        \
     if (smem > 232448) return fail(TT_ERR_UNSUPPORTED, "ffn %d too wide", p.F); \
     if (int rc = prepare_kernel(kern, smem)) return rc;                     \
-    kern<<<grid, kFfnThreads, smem, stream>>>(maps, p);                     \
+    launch_kernel(kern, grid, kFfnThreads, smem, stream, maps, p);          \
     break;                                                                  \
   }
     TT_FFN_CASE(32)
@@ -375,10 +404,10 @@ int launch_ffn2(const Ffn2Maps& maps, FfnParams p, int sm_count, cudaStream_t st
   const unsigned grid = static_cast<unsigned>(items < sm_count ? items : sm_count);
   if (p.D == 128) {
     if (int rc = prepare_kernel(ffn2_kernel<128>, Ffn2Layout<128>::SMEM_ALLOC)) return rc;
-    ffn2_kernel<128><<<grid, kFfn2Threads, Ffn2Layout<128>::SMEM_ALLOC, stream>>>(maps, p);
+    launch_kernel(ffn2_kernel<128>, grid, kFfn2Threads, Ffn2Layout<128>::SMEM_ALLOC, stream, maps, p);
   } else if (p.D == 256) {
     if (int rc = prepare_kernel(ffn2_kernel<256>, Ffn2Layout<256>::SMEM_ALLOC)) return rc;
-    ffn2_kernel<256><<<grid, kFfn2Threads, Ffn2Layout<256>::SMEM_ALLOC, stream>>>(maps, p);
+    launch_kernel(ffn2_kernel<256>, grid, kFfn2Threads, Ffn2Layout<256>::SMEM_ALLOC, stream, maps, p);
   } else {
     return fail(TT_ERR_UNSUPPORTED, "ffn2: d_model %d not in {128, 256}", p.D);
   }
@@ -431,8 +460,8 @@ int run_layernorm(const float* x, const float* gamma, const float* beta, void* o
   switch (d / 32) {
 #define TT_LN_CASE(V)                                                                  \
   case V:                                                                              \
-    layernorm_rows_kernel<V><<<grid, 256, 0, stream>>>(x, gamma, beta, out, n_rows, eps, \
-                                                       out_f16);                       \
+    launch_kernel(layernorm_rows_kernel<V>, grid, 256, 0, stream, x, gamma, beta, out, n_rows, eps, \
+                  out_f16);                                                                        \
     break;
     TT_LN_CASE(1)
     TT_LN_CASE(2)
@@ -506,12 +535,12 @@ int launch_attention(const CUtensorMap& tq, const CUtensorMap& tk, const CUtenso
                   ki.regs, AttnDbLayout<32>::REGS_LAUNCH);
     const int ctas = (n_items + AttnDbLayout<32>::NS - 1) / AttnDbLayout<32>::NS;
     const unsigned grid2 = static_cast<unsigned>(ctas < sm_count ? ctas : sm_count);
-    kern<<<grid2, AttnDbLayout<32>::THREADS, smem, stream>>>(tq, tk, tv, ap, n_items);
+    launch_kernel(kern, grid2, AttnDbLayout<32>::THREADS, smem, stream, tq, tk, tv, ap, n_items);
     (void)grid;
   } else if (hd == 64) {
     auto kern = attn_fwd_kernel<64>;
     if (int rc = prepare_kernel(kern, AttnLayout<64>::SMEM_ALLOC)) return rc;
-    kern<<<grid, 192, AttnLayout<64>::SMEM_ALLOC, stream>>>(tq, tk, tv, ap, n_items);
+    launch_kernel(kern, grid, 192, AttnLayout<64>::SMEM_ALLOC, stream, tq, tk, tv, ap, n_items);
   } else {
     return fail(TT_ERR_UNSUPPORTED, "head_dim %d not in {8, 16, 32, 64}", hd);
   }
@@ -1220,6 +1249,7 @@ int model_forward(tt_model* m, const float* x, const uint8_t* mask, float* out, 
   if (reinterpret_cast<uintptr_t>(x) % 16 != 0 || reinterpret_cast<uintptr_t>(out) % 16 != 0)
     return fail(TT_ERR_ALIGN, "x and out must be 16-byte aligned");
   if (int rc = bind_workspace(m, batch, seq, workspace)) return rc;
+  const PdlScope pdl;
   const Route& r = m->route;
   uint8_t* base = static_cast<uint8_t*>(workspace);
   __half* norm = reinterpret_cast<__half*>(base + w.norm);
@@ -1249,7 +1279,7 @@ int model_forward(tt_model* m, const float* x, const uint8_t* mask, float* out, 
 
   if (mask) {
     if (int rc = record_begin(m, s, &ev)) return rc;
-    mask_kv_end_kernel<<<batch, 256, 0, s>>>(mask, seq, kv_end);
+    launch_kernel(mask_kv_end_kernel, batch, 256, 0, s, mask, seq, kv_end);
     if (int rc = after_launch("mask_kv_end")) return rc;
     if (int rc = record_end(m, s, TT_KERNEL_MASK, ev)) return rc;
   }

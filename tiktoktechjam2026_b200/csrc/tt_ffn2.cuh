@@ -171,6 +171,8 @@ __global__ void __launch_bounds__(kFfn2Threads, 1)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
+  pdl_wait();  // activations of the previous kernel are final from here on
+  pdl_trigger();
   const uint32_t tmem_base = *tmem_slot;
   const Watchdog wd{p.err, abort_flag, p.timeout_ns};
 

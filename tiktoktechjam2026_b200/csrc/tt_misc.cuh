@@ -15,6 +15,8 @@ __global__ void __launch_bounds__(256)
     layernorm_rows_kernel(const float* __restrict__ x, const float* __restrict__ gamma,
                           const float* __restrict__ beta, void* __restrict__ out, long long n_rows,
                           float eps, int out_f16) {
+  pdl_wait();
+  pdl_trigger();
   constexpr int D = VPL * 32;
   const long long row = static_cast<long long>(blockIdx.x) * 8 + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
@@ -85,6 +87,8 @@ __global__ void __launch_bounds__(256)
 // kv_end[b] = 1 + index of the last nonzero mask byte of sequence b (0 if none).
 __global__ void __launch_bounds__(256)
     mask_kv_end_kernel(const uint8_t* __restrict__ mask, int seq, int* __restrict__ kv_end) {
+  pdl_wait();
+  pdl_trigger();
   const int b = blockIdx.x;
   int last = -1;
   for (int s = threadIdx.x; s < seq; s += blockDim.x)

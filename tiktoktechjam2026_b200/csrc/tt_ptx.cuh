@@ -21,6 +21,17 @@ __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }
 
+// Programmatic dependent launch.  A kernel launched with programmatic stream
+// serialization may start while the previous kernel of the stream is still
+// running; pdl_wait() blocks until that kernel has completed and its memory
+// is visible (a no-op for an ordinary launch), so everything before it may
+// only touch shared memory, TMEM and data that was final before the previous
+// kernel started (weights).  pdl_trigger() lets the next kernel's CTAs start
+// their own set-up; it is issued after pdl_wait(), so a kernel's successor
+// can only start once the kernel's own predecessor is done.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 __device__ __forceinline__ unsigned long long globaltimer_ns() {
   unsigned long long t;
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
