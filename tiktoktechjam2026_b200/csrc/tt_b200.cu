@@ -273,7 +273,7 @@ const RouteEntry kRouteTable[] = {
     // C4  B16 S2048 D512 H8 F2048 (+ key padding)
     {512, 8, 2048, 2048, {"d512-h8-s2048", 256, 4, 2, 256, 4, 2, 0}},
     // C5  B512 S1024 D256 H8 F1024
-    {256, 8, 1024, 1024, {"d256-h8-s1024", 256, 2, 2, 256, 2, 3, 1}},
+    {256, 8, 1024, 1024, {"d256-h8-s1024", 256, 3, 2, 256, 2, 3, 1}},
 };
 
 int largest_bn_dividing(int n, int cap) {
