@@ -88,7 +88,7 @@ def kernel_label(kind, cfg):
     if kind == "attn":
         if hd == 8:
             return "attn_db_fwd_kernel<16> (head_dim 8 stored 16 wide)"
-        return f"attn_db_fwd_kernel<{hd}>" if hd in (16, 32) else f"attn_fwd_kernel<{hd}>"
+        return f"attn_db_fwd_kernel<{hd}>"
     if kind == "ffn_fused":
         return f"ffn2_kernel<{cfg['d_model']}>" if cfg["d_model"] in (128, 256) else f"ffn_fused_kernel<{cfg['d_model']}>"
     return KERNEL_KIND_LABEL.get(kind, kind)

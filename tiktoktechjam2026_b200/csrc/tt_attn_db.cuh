@@ -1,10 +1,11 @@
-// Causal attention forward for head_dim 16 and 32 (sm_100a).
+// Causal (or full) attention forward for head_dim 16, 32 and 64 (sm_100a);
+// head_dim 8 runs the head_dim-16 instance on Q/K/V stored 16 wide.
 //
-// Same contract as attn_fwd_kernel (tt_attention.cuh; replaces
-// custom_kernel/triton_attention.py:126-232 of the reference).  At these head
-// sizes the tensor-core work is small and the softmax (one exponential per
-// score) bounds the kernel, so the layout keeps the softmax warps from ever
-// waiting on the tensor core:
+// Replaces custom_kernel/triton_attention.py:126-232 of the reference (the
+// parameters and the heavy-first work schedule are in tt_attention.cuh).  At
+// these head sizes the tensor-core work per score is small and the softmax
+// (one exponential per score) bounds the kernel, so the layout keeps the
+// softmax warps from ever waiting on the tensor core:
 //
 //  * one CTA per SM runs two independent pipelines ("streams"), each on a
 //    128-query tile of its own work item, with 4 softmax warps (one per TMEM
@@ -53,7 +54,11 @@ struct AttnDbLayout {
   static constexpr int NS = 2;   // independent pipelines per CTA
   static constexpr int NSB = 2;  // S (and P) buffers per stream
   static constexpr int BM = 128, BN = 64;
-  static constexpr int NST = HD == 16 ? 8 : 6;
+  static constexpr int NST = HD == 16 ? 8 : HD == 32 ? 6 : 4;
+  // [O | l] accumulator buffers per stream: two (an item's epilogue runs after
+  // the next item's first tile) where TMEM allows; one at head_dim 64, where the
+  // next item's first P.V waits for the epilogue to have read O.
+  static constexpr int NOB = HD <= 32 ? 2 : 1;
   static constexpr int Q_BYTES = BM * HD * 2;
   static constexpr int K_BYTES = BN * HD * 2;
   static constexpr int V_BYTES = HD * 128;  // V^T block: HD rows of 64 keys (128 bytes)
@@ -76,7 +81,7 @@ struct AttnDbLayout {
   static constexpr int OFF_MISC = OFF_DONE + 32;
   static constexpr int SMEM_ALLOC = OFF_MISC + 16 + 1024;
   // TMEM per stream: S buffers at 0, 64, ..., [O | l] of item buffer ob at NSB * 64 + ob * ON.
-  static constexpr int TMEM_COLS = 512, TMEM_O = NSB * BN, TMEM_STREAM = TMEM_O + 2 * ON;
+  static constexpr int TMEM_COLS = 512, TMEM_O = NSB * BN, TMEM_STREAM = TMEM_O + NOB * ON;
   // Warps: 4 NS softmax (stream w / 4, lane quadrant w % 4), NS producers, NS
   // MMA issuers, then idle warps up to a whole number of warpgroups:
   // setmaxnreg is a warpgroup operation, so every warpgroup must be complete.
@@ -94,7 +99,7 @@ struct AttnDbLayout {
   static_assert(128 * NS * REGS_SOFTMAX + 32 * (NWARPS - 4 * NS) * REGS_OTHER <= THREADS * REGS_LAUNCH,
                 "register split");
   static_assert(NS * TMEM_STREAM <= TMEM_COLS, "TMEM budget");
-  static_assert(HD == 16 || HD == 32, "this kernel covers head_dim 16 and 32");
+  static_assert(HD == 16 || HD == 32 || HD == 64, "this kernel covers head_dim 16, 32 and 64");
   static_assert(STREAM_BYTES % 1024 == 0 && S_V % 1024 == 0 && V_STAGE % 1024 == 0, "alignment");
   static_assert(SMEM_ALLOC <= 232448, "shared memory budget");
 };
@@ -265,16 +270,16 @@ __global__ void __launch_bounds__(AttnDbLayout<HD>::THREADS, 1)
         }
         return true;
       };
-      // P.V cursor: items it_o (O buffer it_o & 1), tile j_o of n_o.
+      // P.V cursor: items it_o (O buffer it_o % NOB), tile j_o of n_o.
       int w_o = first_item(NS * static_cast<int>(blockIdx.x) + s), j_o = 0, it_o = 0;
       int n_o = w_o < n_items ? n_tiles(attn_item(p, w_o, n_qt)) : 0;
       bool ok = true;
       // Scores of the first NSB tiles, then per tile t: P.V_t, then S_{t+NSB}.
       for (int k = 0; ok && k < NSB && w_s < n_items; ++k) ok = issue_s();
       for (int t = 0; ok && t < u; ++t) {
-        const int bb = t % NSB, st = t % NST, ob = it_o & 1;
+        const int bb = t % NSB, st = t % NST, ob = it_o % L::NOB;
         if (!(ok = wait_phase(&b[L::B_PF + bb], (t / NSB) & 1, wd, 0x234))) break;
-        if (j_o == 0 && !(ok = wait_phase(&b[L::B_OR + ob], ((it_o >> 1) & 1) ^ 1, wd, 0x235))) break;
+        if (j_o == 0 && !(ok = wait_phase(&b[L::B_OR + ob], ((it_o / L::NOB) & 1) ^ 1, wd, 0x235))) break;
         tc_fence_after();
         const uint32_t tO = tS + L::TMEM_O + ob * L::ON;
 #pragma unroll
@@ -318,18 +323,28 @@ __global__ void __launch_bounds__(AttnDbLayout<HD>::THREADS, 1)
     bool pend_store = false;
     bool pend_valid = false;
     auto finish_item = [&]() -> bool {
-      const int ob = pend_it & 1;
-      if (!warp_wait_phase(&b[L::B_OF + ob], (pend_it >> 1) & 1, wd, 0x333)) return false;
+      const int ob = pend_it % L::NOB;
+      if (!warp_wait_phase(&b[L::B_OF + ob], (pend_it / L::NOB) & 1, wd, 0x333)) return false;
       tc_fence_after();
       uint32_t o[HD];
       uint32_t lv[8];  // row sum of the FP16 probabilities (column HD of the accumulator)
-      if constexpr (HD == 32) {
-        tmem_ld_x32(tS + L::TMEM_O + ob * L::ON, o);
+      if constexpr (HD == 64) {
+        uint32_t(&o0)[32] = *reinterpret_cast<uint32_t(*)[32]>(o);
+        uint32_t(&o1)[32] = *reinterpret_cast<uint32_t(*)[32]>(o + 32);
+        tmem_ld_x32(tS + L::TMEM_O + ob * L::ON, o0);
+        tmem_ld_x32(tS + L::TMEM_O + ob * L::ON + 32, o1);
+        tmem_ld_x8(tS + L::TMEM_O + ob * L::ON + HD, lv);
+        tmem_ld_wait_tied(o0);
+        tmem_ld_wait_tied(o1);
       } else {
-        tmem_ld_x16(tS + L::TMEM_O + ob * L::ON, o);
+        if constexpr (HD == 32) {
+          tmem_ld_x32(tS + L::TMEM_O + ob * L::ON, o);
+        } else {
+          tmem_ld_x16(tS + L::TMEM_O + ob * L::ON, o);
+        }
+        tmem_ld_x8(tS + L::TMEM_O + ob * L::ON + HD, lv);
+        tmem_ld_wait_tied(o);
       }
-      tmem_ld_x8(tS + L::TMEM_O + ob * L::ON + HD, lv);
-      tmem_ld_wait_tied(o);
       tmem_ld_wait_tied(lv);
       tc_fence_before();
       __syncwarp();
@@ -365,7 +380,7 @@ __global__ void __launch_bounds__(AttnDbLayout<HD>::THREADS, 1)
         continue;
       }
       const int row_lim = p.causal ? min(qi + 1, item.kv_end) : item.kv_end;
-      const int ob = it & 1;
+      const int ob = it % L::NOB;
       const uint32_t tO = tS + L::TMEM_O + ob * L::ON;
       float m_run = -INFINITY;  // reference maximum of this row (log2 units)
 

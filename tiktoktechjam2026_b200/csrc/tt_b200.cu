@@ -499,7 +499,7 @@ int encode_attention_maps(CUtensorMap* tq, CUtensorMap* tk, CUtensorMap* tv, con
     const uint32_t box[3] = {static_cast<uint32_t>(hd), 128, 1};
     if (int rc = encode_f16(tq, q, 3, dims, strides, box)) return rc;
     // Key tiles: 64 keys for head_dim <= 32 (attn_db_fwd_kernel), else 128.
-    const uint32_t kbox[3] = {static_cast<uint32_t>(hd), hd <= 32 ? 64u : 128u, 1};
+    const uint32_t kbox[3] = {static_cast<uint32_t>(hd), 64u, 1};  // 64-key tiles (attn_db_fwd_kernel)
     if (int rc = encode_f16(tk, k, 3, dims, strides, kbox)) return rc;
   }
   {
@@ -521,11 +521,13 @@ int launch_attention(const CUtensorMap& tq, const CUtensorMap& tk, const CUtenso
   const int n_items = static_cast<int>(items);
   const unsigned grid = static_cast<unsigned>(n_items < sm_count ? n_items : sm_count);
   if (ap.ctx_hd != hd) return fail(TT_ERR_ARG, "ctx head width %d != head_dim %d", ap.ctx_hd, hd);
-  if (hd == 8 || hd == 16 || hd == 32) {
-    // Two streams per CTA, 64-key tiles, double-buffered scores and probabilities.
+  if (hd == 8 || hd == 16 || hd == 32 || hd == 64) {
+    // Two streams per CTA, 64-key tiles, double-buffered scores with the probabilities over them in TMEM.
     // head_dim 8 runs the head_dim-16 kernel on its zero-padded Q/K/V.
-    auto kern = hd <= 16 ? attn_db_fwd_kernel<16> : attn_db_fwd_kernel<32>;
-    const int smem = hd <= 16 ? AttnDbLayout<16>::SMEM_ALLOC : AttnDbLayout<32>::SMEM_ALLOC;
+    auto kern = hd <= 16 ? attn_db_fwd_kernel<16> : hd == 32 ? attn_db_fwd_kernel<32> : attn_db_fwd_kernel<64>;
+    const int smem = hd <= 16   ? AttnDbLayout<16>::SMEM_ALLOC
+                     : hd == 32 ? AttnDbLayout<32>::SMEM_ALLOC
+                                : AttnDbLayout<64>::SMEM_ALLOC;
     KernelInfo ki;
     if (int rc = kernel_info(reinterpret_cast<const void*>(kern), smem, &ki)) return rc;
     // The kernel splits its registers with setmaxnreg; that split is only sound
@@ -537,10 +539,6 @@ int launch_attention(const CUtensorMap& tq, const CUtensorMap& tk, const CUtenso
     const unsigned grid2 = static_cast<unsigned>(ctas < sm_count ? ctas : sm_count);
     launch_kernel(kern, grid2, AttnDbLayout<32>::THREADS, smem, stream, tq, tk, tv, ap, n_items);
     (void)grid;
-  } else if (hd == 64) {
-    auto kern = attn_fwd_kernel<64>;
-    if (int rc = prepare_kernel(kern, AttnLayout<64>::SMEM_ALLOC)) return rc;
-    launch_kernel(kern, grid, 192, AttnLayout<64>::SMEM_ALLOC, stream, tq, tk, tv, ap, n_items);
   } else {
     return fail(TT_ERR_UNSUPPORTED, "head_dim %d not in {8, 16, 32, 64}", hd);
   }
