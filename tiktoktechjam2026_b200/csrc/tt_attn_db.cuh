@@ -42,12 +42,6 @@
 
 namespace tt {
 
-#ifndef TT_DB_REGS_SOFTMAX
-#define TT_DB_REGS_SOFTMAX 216
-#endif
-#ifndef TT_DB_REGS_OTHER
-#define TT_DB_REGS_OTHER 56
-#endif
 
 template <int HD>
 struct AttnDbLayout {
@@ -94,7 +88,7 @@ struct AttnDbLayout {
   // REGS_LAUNCH registers per thread (a split above the launch total would make
   // setmaxnreg.inc wait forever).
   static constexpr int REGS_LAUNCH = 168;
-  static constexpr int REGS_SOFTMAX = TT_DB_REGS_SOFTMAX, REGS_OTHER = TT_DB_REGS_OTHER;
+  static constexpr int REGS_SOFTMAX = 216, REGS_OTHER = 56;
   static_assert(NWARPS % 4 == 0, "whole warpgroups");
   static_assert(128 * NS * REGS_SOFTMAX + 32 * (NWARPS - 4 * NS) * REGS_OTHER <= THREADS * REGS_LAUNCH,
                 "register split");
@@ -110,12 +104,7 @@ struct AttnDbLayout {
 #define TT_DB_EXP_FMA_OF8 2
 #endif
 constexpr int kDbExpFmaOf8 = TT_DB_EXP_FMA_OF8;
-#ifndef TT_ATTN_SKIP_MASKED
-#define TT_ATTN_SKIP_MASKED 0
-#endif
-#ifndef TT_ATTN_SCALAR_X
-#define TT_ATTN_SCALAR_X 0
-#endif
+
 
 template <int HD>
 __global__ void __launch_bounds__(AttnDbLayout<HD>::THREADS, 1)
@@ -404,23 +393,6 @@ __global__ void __launch_bounds__(AttnDbLayout<HD>::THREADS, 1)
 
         if (!(ok = warp_wait_phase(&b[L::B_SF + bb], (t / NSB) & 1, wd, 0x331))) break;
         tc_fence_after();
-#if TT_ATTN_SKIP_MASKED
-        // No row of this warp sees a key of this tile (above the causal diagonal,
-        // or past the sequence's last valid key): its probabilities are all zero.
-        if (__all_sync(0xffffffffu, k0 >= row_lim)) {
-          uint32_t zero[16];
-#pragma unroll
-          for (int e = 0; e < 16; ++e) zero[e] = 0u;
-          tmem_st_x16(tS + bb * BN, zero);
-          tmem_st_x16(tS + bb * BN + 16, zero);
-          tmem_st_wait();
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&b[L::B_PF + bb]);
-          if (j == 0 && pend && !(ok = finish_item())) break;
-          continue;
-        }
-#endif
         uint32_t sc[2][32];
         tmem_ld_x32(tS + bb * BN, sc[0]);
         tmem_ld_x32(tS + bb * BN + 32, sc[1]);
@@ -495,15 +467,9 @@ __global__ void __launch_bounds__(AttnDbLayout<HD>::THREADS, 1)
               const uint64_t pp = exp2_pair_fma(xx);
               pk[e] = pack_half2(f2_lo(pp), f2_hi(pp));
             } else {
-#if TT_ATTN_SCALAR_X
-              const float x0 = fmaf(__uint_as_float(sc[g][2 * e]), sl2, -m_use);
-              const float x1 = fmaf(__uint_as_float(sc[g][2 * e + 1]), sl2, -m_use);
-              pk[e] = pack_half2(ex2_approx(x0), ex2_approx(x1));
-#else
               const uint64_t xx =
                   ffma2(f2_pack(__uint_as_float(sc[g][2 * e]), __uint_as_float(sc[g][2 * e + 1])), sl2x2, negm);
               pk[e] = pack_half2(ex2_approx(f2_lo(xx)), ex2_approx(f2_hi(xx)));
-#endif
             }
           }
           tmem_st_x16(tS + bb * BN + 16 * g, pk);
