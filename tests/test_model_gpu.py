@@ -165,6 +165,9 @@ def test_tiny_golden_cases(tt_lib, golden, name):
         (2, 256, 512, 8, 1024, 1, True, "prefix"),
         (3, 130, 64, 8, 128, 2, True, "random"),
         (2, 96, 128, 16, 256, 1, False, "prefix"),
+        # wide FFNs at d_model 256 (16 and 32 hidden chunks per row tile)
+        (2, 200, 256, 8, 2048, 1, True, "prefix"),
+        (2, 130, 256, 8, 4096, 1, True, None),
     ],
 )
 def test_edge_shapes(tt_lib, strict_fp32, B, S, D, H, Fd, L, causal, mask_kind):

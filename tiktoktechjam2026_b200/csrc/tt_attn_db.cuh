@@ -372,20 +372,27 @@ __global__ void __launch_bounds__(AttnDbLayout<HD>::THREADS, 1)
       const int ob = it % L::NOB;
       const uint32_t tO = tS + L::TMEM_O + ob * L::ON;
       float m_run = -INFINITY;  // reference maximum of this row (log2 units)
+      // Key-mask bytes of the next tile, loaded one tile ahead so their global
+      // latency stays off the softmax's path (lane l holds keys k0 + l and k0 + 32 + l).
+      const uint8_t* mrow = p.key_mask ? p.key_mask + static_cast<size_t>(item.b) * p.seq : nullptr;
+      auto mask_bytes = [&](int k0, uint32_t& m0, uint32_t& m1) {
+        const int ka = k0 + lane;
+        m0 = (ka < p.seq && mrow[min(ka, p.seq - 1)] != 0) ? 1u : 0u;
+        m1 = (ka + 32 < p.seq && mrow[min(ka + 32, p.seq - 1)] != 0) ? 1u : 0u;
+      };
+      uint32_t mn0 = 1u, mn1 = 1u;
+      if (mrow) mask_bytes(0, mn0, mn1);
 
       for (int j = 0; j < nt; ++j, ++t) {
         const int bb = t % NSB;
         const int k0 = j * BN;
         uint32_t vb[2] = {~0u, ~0u};
         bool mask_partial = false;
-        if (p.key_mask != nullptr) {
-          const uint8_t* mrow = p.key_mask + static_cast<size_t>(item.b) * p.seq;
-#pragma unroll
-          for (int g = 0; g < 2; ++g) {
-            const int ka = k0 + lane + 32 * g;
-            vb[g] = __ballot_sync(~0u, ka < p.seq && mrow[min(ka, p.seq - 1)] != 0);
-          }
+        if (mrow) {
+          vb[0] = __ballot_sync(~0u, mn0 != 0);
+          vb[1] = __ballot_sync(~0u, mn1 != 0);
           mask_partial = (vb[0] & vb[1]) != ~0u;
+          if (j + 1 < nt) mask_bytes(k0 + BN, mn0, mn1);
         }
         // Warp-uniform: the masking branch sits between warp-collective TMEM operations.
         const bool need_mask = __any_sync(0xffffffffu, mask_partial || (k0 + BN > row_lim));

@@ -572,26 +572,12 @@ __device__ __forceinline__ float gelu_erf(float x) {
 
 // gelu_erf on a pair of inputs, the polynomial on packed FP32 pairs (same
 // coefficients and rounding steps, half the instructions).
-#ifndef TT_GELU_DEG8
-#define TT_GELU_DEG8 0
-#endif
 __device__ __forceinline__ uint64_t gelu_erf_pair(uint64_t xx) {
   const float x0 = f2_lo(xx), x1 = f2_hi(xx);
   const uint64_t z = f2_pack(fminf(fabsf(x0), 12.0f), fminf(fabsf(x1), 12.0f));
   const uint64_t a = fmul2(fmul2(z, z), f2_pack(-0.72134752044448170f, -0.72134752044448170f));
   const uint64_t e = f2_pack(ex2_approx(f2_lo(a)), ex2_approx(f2_hi(a)));
 #define TT_C2(c) f2_pack(c, c)
-#if TT_GELU_DEG8
-  // Degree 8 fitted on [0, 6] (same weighting); GELU error below 9.4e-7.
-  uint64_t q = ffma2(TT_C2(2.00383183e-05f), z, TT_C2(-3.74979019e-04f));
-  q = ffma2(q, z, TT_C2(3.09203891e-03f));
-  q = ffma2(q, z, TT_C2(-1.51119316e-02f));
-  q = ffma2(q, z, TT_C2(5.02214804e-02f));
-  q = ffma2(q, z, TT_C2(-1.24635234e-01f));
-  q = ffma2(q, z, TT_C2(2.46710628e-01f));
-  q = ffma2(q, z, TT_C2(-3.98298979e-01f));
-  q = ffma2(q, z, TT_C2(4.99956280e-01f));
-#else
   uint64_t q = ffma2(TT_C2(1.8272603e-07f), z, TT_C2(-6.2833151e-06f));
   q = ffma2(q, z, TT_C2(9.4161209e-05f));
   q = ffma2(q, z, TT_C2(-8.1654533e-04f));
@@ -602,7 +588,6 @@ __device__ __forceinline__ uint64_t gelu_erf_pair(uint64_t xx) {
   q = ffma2(q, z, TT_C2(2.4824467e-01f));
   q = ffma2(q, z, TT_C2(-3.9865106e-01f));
   q = ffma2(q, z, TT_C2(4.9998581e-01f));
-#endif
   const uint64_t g = fmul2(fmul2(z, e), q);
   return ffma2(g, TT_C2(-1.0f), f2_pack(fmaxf(x0, 0.0f), fmaxf(x1, 0.0f)));
 #undef TT_C2
