@@ -105,10 +105,7 @@ struct AttnDbLayout {
 
 // Pairs of exponentials per 8 computed by polynomial on the FP32 pipe instead
 // of MUFU.
-#ifndef TT_DB_EXP_FMA_OF8
-#define TT_DB_EXP_FMA_OF8 2
-#endif
-constexpr int kDbExpFmaOf8 = TT_DB_EXP_FMA_OF8;
+constexpr int kDbExpFmaOf8 = 2;
 
 
 template <int HD>

@@ -57,15 +57,9 @@ struct Ffn2Maps {
 
 template <int D>
 struct Ffn2Layout {
-#ifndef TT_FFN2_NST
-#define TT_FFN2_NST 3
-#endif
-#ifndef TT_FFN2_AHEAD
-#define TT_FFN2_AHEAD 6
-#endif
   // Hidden units per chunk, TMEM buffers of the chunk accumulator (columns
   // 256..511), and how many chunks G2 trails G1.
-  static constexpr int FC = 128, KB = 64, NST = TT_FFN2_NST, SLOT = 32768;
+  static constexpr int FC = 128, KB = 64, NST = 3, SLOT = 32768;
   static constexpr int NACC1 = 256 / FC, LAG = 1;
   static constexpr int NKA = D / KB;                 // K-blocks of G1
   static constexpr int A_KBLK = 128 * KB * 2;        // 16 KB
@@ -78,7 +72,7 @@ struct Ffn2Layout {
   static constexpr int W2_SLOTS = (FC / KB) / W2_PER_SLOT;
   static constexpr int W2_BOX_ROWS = D < 256 ? D : 256;
   static constexpr int JW = 16;       // columns per epilogue job
-  static constexpr int AHEAD = TT_FFN2_AHEAD;  // epilogue jobs in flight ahead of the one consumed
+  static constexpr int AHEAD = 6;  // epilogue jobs in flight ahead of the one consumed
   static constexpr int RING = AHEAD + 1;      // 32 x JW FP32 staging tiles per epilogue warp
   static constexpr int TILE = 32 * JW * 4;
   static constexpr int OFF_A = 0;
@@ -109,10 +103,7 @@ struct Ffn2Layout {
 // Warp roles: 0..7 GELU (lane quadrant w & 3, hidden half w >> 2 of each
 // chunk), 8..11 residual + LayerNorm, 12 and 14.. TMA producers, 13 TMEM
 // allocator and MMA issuer.
-#ifndef TT_FFN2_PRODUCERS
-#define TT_FFN2_PRODUCERS 2
-#endif
-constexpr int kFfn2Producers = TT_FFN2_PRODUCERS;  // warps 12, 14, 15, ...
+constexpr int kFfn2Producers = 2;  // warps 12, 14, 15, ...
 constexpr int kFfn2Threads = 32 * (13 + kFfn2Producers);
 constexpr int kFfn2Prod0 = 12, kFfn2Mma = 13;
 

@@ -44,19 +44,11 @@ namespace tt {
 enum GemmEpilogue : int { EPI_QKV = 0, EPI_RESID_LN = 1, EPI_GELU = 2 };
 
 constexpr int kGemmMaxStages = 8;
-// EPI_RESID_LN with TT_LN_SPLIT (the default): two epilogue warps per TMEM
-// lane quadrant, each on half of the row's columns, the row statistics
-// combined through shared memory (C5 out-proj 1.27 -> 1.08 ms per forward
-// against one warp per quadrant).
-#ifndef TT_LN_SPLIT
-#define TT_LN_SPLIT 1
-#endif
-#ifndef TT_LN_SPLIT_RES
-#define TT_LN_SPLIT_RES 2
-#endif
-constexpr bool kLnSplit = TT_LN_SPLIT != 0;
-// Residual tiles in flight per epilogue warp (EPI_RESID_LN).
-constexpr int kResRing = kLnSplit ? TT_LN_SPLIT_RES : 3;
+// EPI_RESID_LN runs two epilogue warps per TMEM lane quadrant, each on half
+// of the row's columns, the row statistics combined through shared memory
+// (C5 out-proj 1.27 -> 1.08 ms per forward against one warp per quadrant);
+// kResRing residual tiles are in flight per epilogue warp.
+constexpr int kResRing = 2;
 constexpr int kEpiTile = 4096;  // one [32 x 32] FP32 tile
 
 struct GemmParams {
@@ -101,22 +93,19 @@ __host__ __device__ inline int gemm_acc_stride(int bn) {
 __host__ __device__ inline int gemm_n_acc(int bn) { return bn <= 256 ? 2 : 1; }
 __host__ __device__ inline int gemm_tmem_cols(int bn) { return gemm_n_acc(bn) * gemm_acc_stride(bn); }
 // Epilogue warps: two on each TMEM lane quadrant, splitting its columns, so
-// every SM sub-partition has two epilogue warps (the LayerNorm epilogue keeps
-// a whole row per thread, 4 warps, when built without TT_LN_SPLIT).
-__host__ __device__ constexpr int gemm_epi_warps(int epi) { return epi == EPI_RESID_LN && !kLnSplit ? 4 : 8; }
+// every SM sub-partition has two epilogue warps.
+__host__ __device__ constexpr int gemm_epi_warps(int) { return 8; }
 // Warps: epilogue warps, then the first TMA producer, the MMA issuer and
 // kGemmProducers - 1 more producers.  Ring slot st is always filled by
 // producer st % kGemmProducers: one producer per slot keeps the parity-based
 // empty-slot wait exact (a producer can never be two phases ahead on a slot
 // that another producer fills).
-#ifndef TT_GEMM_PRODUCERS
-#define TT_GEMM_PRODUCERS 2
-#endif
-constexpr int kGemmProducers = TT_GEMM_PRODUCERS;
+constexpr int kGemmProducers = 2;
 __host__ __device__ constexpr int gemm_threads(int epi) { return 32 * (gemm_epi_warps(epi) + 1 + kGemmProducers); }
 // Output staging tiles per epilogue warp.  The LayerNorm epilogue spends its
-// shared memory on the residual ring instead (3 residual tiles and 1 output
-// tile measured 4 % faster than 2 and 2 at C5).
+// shared memory on the residual ring instead (with one epilogue warp per
+// quadrant, 3 residual tiles and 1 output tile measured 4 % faster than 2 and 2
+// at C5).
 __host__ __device__ constexpr int gemm_out_ring(int epi) { return epi == EPI_RESID_LN ? 1 : 2; }
 __host__ __device__ inline int gemm_epi_bytes(int epi) {
   return gemm_epi_warps(epi) * ((epi == EPI_RESID_LN ? kResRing : 0) + gemm_out_ring(epi)) * kEpiTile;

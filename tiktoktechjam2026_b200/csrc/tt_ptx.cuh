@@ -124,28 +124,21 @@ __device__ __forceinline__ bool wait_slow(uint64_t* bar, uint32_t parity, const 
   }
 }
 
-#ifndef TT_WAIT_TEST_FIRST
-#define TT_WAIT_TEST_FIRST 0
-#endif
-// With TT_WAIT_TEST_FIRST the non-blocking probe runs first: a potentially
-// suspending try_wait costs a couple of hundred cycles even when the phase
-// has long completed.
+// Single-thread wait (producer and MMA warps): straight to try_wait.
 __device__ __forceinline__ bool wait_phase(uint64_t* bar, uint32_t parity, const Watchdog& wd,
                                            uint32_t site) {
-  if (TT_WAIT_TEST_FIRST && mbar_test_wait(bar, parity)) return true;
   if (mbar_try_wait(bar, parity)) return true;
   return wait_slow(bar, parity, wd, site);
 }
 
 // Whole-warp wait: every lane observes the phase, then the warp reconverges
 // and agrees on the outcome, so the warp-collective tcgen05.ld/st that follow
-// always run converged.
-#ifndef TT_WARP_WAIT_TEST_FIRST
-#define TT_WARP_WAIT_TEST_FIRST 1
-#endif
+// always run converged.  It probes with the non-blocking test first: a
+// try_wait that may suspend costs a couple of hundred cycles even when the
+// phase completed long ago.
 __device__ __forceinline__ bool warp_wait_phase(uint64_t* bar, uint32_t parity,
                                                 const Watchdog& wd, uint32_t site) {
-  const bool ok = (TT_WARP_WAIT_TEST_FIRST && mbar_test_wait(bar, parity)) || wait_phase(bar, parity, wd, site);
+  const bool ok = mbar_test_wait(bar, parity) || wait_phase(bar, parity, wd, site);
   return __all_sync(0xffffffffu, ok);
 }
 
