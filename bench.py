@@ -70,6 +70,7 @@ WORKLOADS = {
     "C5": (512, 1024, 256, 8, 1024, 4, True, 0.0),
     # The reference suite's other cases (analysis_profile_mixed.py:20-26), every token valid.
     "S6": (10000, 128, 128, 4, 128, 4, True, 0.0),
+    "S8": (64, 128, 1024, 4, 1024, 4, True, 0.0),
     "S10": (64, 128, 128, 2, 128, 4, True, 0.0),
     "S11": (64, 128, 128, 16, 128, 4, True, 0.0),
     "S13": (64, 1024, 128, 4, 128, 4, True, 0.0),

@@ -69,7 +69,7 @@ int tt_selftest_exp2_fma(const float* x, float* y32, uint16_t* y16, int n, void*
 /* ---- single ops ----------------------------------------------------------- */
 
 /* out[r, :] = LayerNorm(x[r, :]) * gamma + beta over d features, FP32 math,
- * out FP16 (out_is_f16 = 1) or FP32.  Requires d % 32 == 0, d <= 1024.
+ * out FP16 (out_is_f16 = 1) or FP32.  d / 32 in {1, 2, 3, 4, 8, 12, 16, 24, 32}.
  * Replaces `layers[0].norm1(x)` + cast (mixed_precision/transformer.py:489-491)
  * and the row LayerNorm of fused_add_layer_norm
  * (torch_transformer_benchmark.py:37-103). */
@@ -101,7 +101,7 @@ int tt_qkv_projection(const void* normalized, const void* w_qkv, const float* b_
  * (the reference zeroes those rows on the model output).  vt's padding columns
  * [seq, seq_pad) must hold finite values (zeros, say): they are multiplied by
  * zero probabilities, and 0 * Inf or 0 * NaN would reach ctx.  head_dim in
- * {8, 16, 32, 64}; q, k and vt have tt_qkv_projection's layout (16 features
+ * {8, 16, 32, 64, 128, 256}; q, k and vt have tt_qkv_projection's layout (16 features
  * per head when head_dim is 8, the extra q/k features zero), ctx has head_dim
  * per head.
  * Replaces fp16_causal_attention / causal_attention
@@ -133,8 +133,10 @@ int tt_causal_attention_masked_noalloc(const void* q, const void* k, const void*
 
 /* resid_out = a[N, k_in] (FP16) . w[d_model, k_in]^T + bias + resid_in (FP32);
  * norm_out = LayerNorm(resid_out) * gamma + beta (FP16 or FP32); rows whose
- * row_mask byte is 0 get norm_out = 0 (row_mask may be NULL).  d_model <= 256
- * or 512; in-place (resid_out == resid_in) is allowed.
+ * row_mask byte is 0 get norm_out = 0 (row_mask may be NULL).  d_model a
+ * multiple of 32 up to 256, or 512, 768 or 1024 (above 512 the product runs in
+ * 256-column splits and the LayerNorm as a second kernel on resid_out); in-place
+ * (resid_out == resid_in) is allowed.
  * Replaces mixed_linear_add_layer_norm (mixed_precision/triton_linear.py:72-125,
  * 272-324) and, with k_in = ffn, the FFN-out + fused_add_layer_norm tail of
  * the generic route (mixed_precision/transformer.py:675-695). */
@@ -203,6 +205,8 @@ typedef struct tt_model tt_model;
 
 /* Creates a model handle bound to the current device; weights are referenced,
  * not copied, and must outlive the handle.  The handle is not thread-safe.
+ * Shapes: head_dim = d_model / heads in {8, 16, 32, 64, 128, 256}; d_model a
+ * multiple of 32 up to 256, or 512, 768 or 1024; ffn_dim a multiple of 32.
  * Replaces MixedPrecisionTransformer.__init__ + convert_projections_to_fp16
  * (mixed_precision/transformer.py:330-478). */
 int tt_model_create(const tt_model_desc* desc, tt_model** out);

@@ -46,6 +46,8 @@ def test_abi_version_and_error_string(tt_lib):
         ((256, 8, 1024, 1024), "d256-h8-s1024"),
         ((64, 4, 77, 96), "generic"),
         ((128, 16, 128, 128), "generic"),
+        ((1024, 4, 128, 1024), "generic"),
+        ((768, 6, 512, 512), "generic"),
     ],
 )
 def test_dispatch_table(tt_lib, shape, name):
@@ -53,7 +55,8 @@ def test_dispatch_table(tt_lib, shape, name):
     assert f"route={name}" in desc
 
 
-@pytest.mark.parametrize("shape", [(96, 1, 128, 128), (128, 32, 128, 128), (1024, 8, 128, 128), (130, 2, 16, 16)])
+@pytest.mark.parametrize("shape", [(96, 1, 128, 128), (128, 32, 128, 128), (2048, 8, 128, 128), (1024, 2, 128, 128),
+                                   (130, 2, 16, 16)])
 def test_dispatch_rejects_unsupported(tt_lib, shape):
     with pytest.raises(_lib.TTError) as e:
         _lib.route_describe(*shape)

@@ -23,7 +23,7 @@ def _gen(seed):
     return g
 
 
-@pytest.mark.parametrize("d", [32, 64, 96, 128, 256, 512])
+@pytest.mark.parametrize("d", [32, 64, 96, 128, 256, 512, 768, 1024])
 @pytest.mark.parametrize("n", [1, 7, 1000])
 @pytest.mark.parametrize("out_dtype", [torch.float16, torch.float32])
 def test_layernorm_rows(tt_lib, d, n, out_dtype):
@@ -38,7 +38,7 @@ def test_layernorm_rows(tt_lib, d, n, out_dtype):
 
 
 QKV_SHAPES = [(2, 16, 32, 2), (3, 130, 128, 4), (1, 256, 256, 8), (2, 64, 512, 8), (64, 128, 128, 4),
-              (2, 128, 128, 16), (1, 70, 64, 8)]
+              (2, 128, 128, 16), (1, 70, 64, 8), (2, 128, 1024, 4), (1, 64, 768, 6), (1, 100, 512, 4)]
 
 
 @pytest.mark.parametrize("B,S,D,H", QKV_SHAPES)
@@ -89,7 +89,7 @@ def _attn_ref(q, k, vt, scale, causal, mask):
 
 ATTN_SHAPES = [
     (2, 2, 16, 16), (1, 4, 130, 32), (2, 2, 256, 64), (1, 8, 1024, 32), (3, 1, 200, 16), (1, 2, 384, 64),
-    (2, 4, 200, 8), (1, 16, 128, 8),
+    (2, 4, 200, 8), (1, 16, 128, 8), (2, 2, 200, 128), (1, 2, 1024, 128), (1, 4, 128, 256), (2, 1, 300, 256),
 ]
 
 
@@ -145,7 +145,8 @@ def test_attention_fully_padded_tile_is_zero(tt_lib):
 
 # d_model 96, 160 and 224 split their rows unevenly between the two epilogue warps of a lane quadrant.
 LIN_LN_SHAPES = [(1000, 128, 128), (300, 32, 32), (513, 256, 256), (257, 512, 512), (200, 2048, 512),
-                 (129, 1024, 256), (4096, 128, 128), (300, 96, 96), (257, 160, 160), (129, 224, 224)]
+                 (129, 1024, 256), (4096, 128, 128), (300, 96, 96), (257, 160, 160), (129, 224, 224),
+                 (300, 1024, 1024), (257, 768, 768), (129, 2048, 1024)]
 
 
 @pytest.mark.parametrize("N,K,D", LIN_LN_SHAPES)

@@ -107,13 +107,14 @@ def test_config_parity_zero_failures(tt_lib, strict_fp32, golden, name, seed):
             assert r.failed == 0, (i, r)
 
 
-SUITE_CHUNK = {"S6": 500, "S10": 64, "S11": 64, "S13": 16}
+SUITE_CHUNK = {"S6": 500, "S8": 16, "S10": 64, "S11": 64, "S13": 16}
 
 
-@pytest.mark.parametrize("name", ["S6", "S10", "S11", "S13"])
+@pytest.mark.parametrize("name", ["S6", "S8", "S10", "S11", "S13"])
 def test_suite_case_parity_zero_failures(tt_lib, strict_fp32, name):
     """The reference suite's cases outside BASELINE.json (analysis_profile_mixed.py:20-26, every token
-    valid): batch 10000, head_dim 64, head_dim 8 (stored 16 wide), seq 1024 at d_model 128."""
+    valid): batch 10000, d_model 1024 with head_dim 256, head_dim 64, head_dim 8 (stored 16 wide), seq
+    1024 at d_model 128."""
     cfg, pad = oracle.SUITE_CONFIGS[name]
     sd = oracle.seeded_state_dict(cfg, oracle.DEFAULT_SEED)
     model = build_model(cfg, sd)
@@ -129,9 +130,9 @@ def test_suite_case_parity_zero_failures(tt_lib, strict_fp32, name):
     assert res.failed == 0, res
 
 
-def test_suite_case8_outside_coverage(tt_lib):
-    """Suite case 8 (d_model 1024, head_dim 256) is refused with TT_ERR_UNSUPPORTED, not run wrongly."""
-    cfg, _ = oracle.SUITE_CONFIGS["S8"]
+def test_unsupported_width_is_refused(tt_lib):
+    """d_model 2048 is outside the shape coverage: refused with TT_ERR_UNSUPPORTED, not run wrongly."""
+    cfg = oracle.Config(1, 16, 2048, 8, 2048, 1, True)
     model = build_model(cfg, oracle.seeded_state_dict(cfg, 1))
     x = torch.zeros(1, cfg.seq_len, cfg.d_model, device=DEV)
     with torch.inference_mode(), pytest.raises(_lib.TTError) as e:
@@ -168,6 +169,11 @@ def test_tiny_golden_cases(tt_lib, golden, name):
         # wide FFNs at d_model 256 (16 and 32 hidden chunks per row tile)
         (2, 200, 256, 8, 2048, 1, True, "prefix"),
         (2, 130, 256, 8, 4096, 1, True, None),
+        # head_dim 128 and 256; d_model 768 and 1024 (residual GEMMs in 256-column splits + row LayerNorm)
+        (3, 130, 512, 4, 1024, 1, False, None),
+        (2, 200, 1024, 4, 1024, 2, True, "prefix"),
+        (2, 96, 768, 6, 512, 1, True, "random"),
+        (1, 300, 1024, 8, 2048, 1, False, "prefix"),
     ],
 )
 def test_edge_shapes(tt_lib, strict_fp32, B, S, D, H, Fd, L, causal, mask_kind):

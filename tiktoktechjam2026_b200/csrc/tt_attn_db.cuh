@@ -1,5 +1,5 @@
-// Causal (or full) attention forward for head_dim 16, 32 and 64 (sm_100a);
-// head_dim 8 runs the head_dim-16 instance on Q/K/V stored 16 wide.
+// Causal (or full) attention forward for head_dim 16, 32, 64, 128 and 256
+// (sm_100a); head_dim 8 runs the head_dim-16 instance on Q/K/V stored 16 wide.
 //
 // Replaces custom_kernel/triton_attention.py:126-232 of the reference (the
 // parameters and the heavy-first work schedule are in tt_attention.cuh).  At
@@ -7,11 +7,12 @@
 // (one exponential per score) bounds the kernel, so the layout keeps the
 // softmax warps from ever waiting on the tensor core:
 //
-//  * one CTA per SM runs two independent pipelines ("streams"), each on a
+//  * one CTA per SM runs two independent pipelines ("streams"; one at head_dim
+//    128 and 256, whose [O | l] accumulator takes most of TMEM), each on a
 //    128-query tile of its own work item, with 4 softmax warps (one per TMEM
-//    lane quadrant, a whole row per thread), its own TMA producer warp (8 + s)
-//    and its own MMA-issuer warp (10 + s); idle warps complete the last
-//    warpgroup (setmaxnreg acts on whole warpgroups);
+//    lane quadrant, a whole row per thread), its own TMA producer warp
+//    (4 NS + s) and its own MMA-issuer warp (5 NS + s); idle warps complete
+//    the last warpgroup (setmaxnreg acts on whole warpgroups);
 //  * key tiles are 64 wide; each stream has NSB score buffers S in TMEM (three
 //    at head_dim 16/32, two at 64); the softmax writes the FP16 probabilities
 //    P back over the first 32 columns of the S buffer it has just read (one
@@ -35,6 +36,10 @@
 //                           followed by 16 rows of FP16 ones, so the same MMA
 //                           (N = HD + 16) also sums the FP16 probabilities
 //                           of every row: the softmax warps never add them.
+//                           At head_dim 256 (N = 272 > 256) it is issued as
+//                           two MMAs, N = 128 and N = 144.
+// Q and K tiles are stored as 128-byte swizzle atoms of 64 features (head_dim
+// >= 64; one TMA copy per atom) or as one atom of head_dim features.
 // Items (sequence*head, query tile) are dealt heavy-first: stream s of CTA c
 // takes items NS c + s, NS c + s + NS G, ... (G = gridDim.x).
 #pragma once
@@ -46,7 +51,7 @@ namespace tt {
 
 template <int HD>
 struct AttnDbLayout {
-  static constexpr int NS = 2;   // independent pipelines per CTA
+  static constexpr int NS = HD >= 128 ? 1 : 2;   // independent pipelines per CTA
   // S (and P) buffers per stream: the MMA warp issues S up to NSB - 1 tiles
   // ahead of the softmax, so the softmax rarely waits for the round trip
   // (P published -> P.V and the next S issued and done).  Three where TMEM
@@ -54,20 +59,25 @@ struct AttnDbLayout {
   // C5 attention 4.78 -> 4.61 ms per forward, C2 0.337 -> 0.321, same bits.
   static constexpr int NSB = HD <= 32 ? 3 : 2;
   static constexpr int BM = 128, BN = 64;
-  static constexpr int NST = HD == 16 ? 8 : HD == 32 ? 6 : 4;
+  static constexpr int NST = HD == 16 ? 8 : HD == 32 ? 6 : HD <= 128 ? 4 : 2;
+  static constexpr int NQ = HD == 256 ? 1 : 2;  // Q tile buffers per stream
   // [O | l] accumulator buffers per stream: two (an item's epilogue runs after
   // the next item's first tile) where TMEM allows; one at head_dim 64, where the
   // next item's first P.V waits for the epilogue to have read O.
-  static constexpr int NOB = 2 * (NSB * 64 + 2 * (HD + 16)) <= 512 ? 2 : 1;
-  static constexpr int Q_BYTES = BM * HD * 2;
-  static constexpr int K_BYTES = BN * HD * 2;
+  static constexpr int NOB = NS * (NSB * 64 + 2 * (HD + 16)) <= 512 ? 2 : 1;
+  static constexpr int KATOM = HD >= 64 ? 64 : HD;  // features per swizzle atom of Q and K
+  static constexpr int NATOM = HD / KATOM;
+  static constexpr int Q_ATOM = BM * KATOM * 2, K_ATOM = BN * KATOM * 2;
+  static constexpr int Q_BYTES = NATOM * Q_ATOM;
+  static constexpr int K_BYTES = NATOM * K_ATOM;
   static constexpr int V_BYTES = HD * 128;  // V^T block: HD rows of 64 keys (128 bytes)
   static constexpr int ONES_BYTES = 16 * 128;           // 16 rows of 64 FP16 ones after each V^T block
   static constexpr int V_STAGE = V_BYTES + ONES_BYTES;  // B operand of P.[V | 1], N = ON rows
   static constexpr int ON = HD + 16;                    // accumulator columns: O, then 16 copies of l
-  // Per-stream region: Q[2] | K[NST] | V[NST] (each with its ones block)
+  static constexpr int ON0 = ON <= 256 ? ON : 128;      // N of the first P.V MMA (the second: ON - ON0)
+  // Per-stream region: Q[NQ] | K[NST] | V[NST] (each with its ones block)
   static constexpr int S_Q = 0;
-  static constexpr int S_K = S_Q + 2 * Q_BYTES;
+  static constexpr int S_K = S_Q + NQ * Q_BYTES;
   static constexpr int S_V = S_K + NST * K_BYTES;
   static constexpr int STREAM_BYTES = S_V + NST * V_STAGE;
   // Per-stream barriers: q_full[2] q_empty[2] kv_full[NST] kv_empty[NST]
@@ -92,13 +102,18 @@ struct AttnDbLayout {
   // The launcher refuses to start the kernel unless it was built with exactly
   // REGS_LAUNCH registers per thread (a split above the launch total would make
   // setmaxnreg.inc wait forever).
+  // With one stream (8 warps) every warp fits REGS_SOFTMAX at launch and
+  // there is no split.
+  static constexpr bool SPLIT = NS == 2;
   static constexpr int REGS_LAUNCH = 168;
   static constexpr int REGS_SOFTMAX = 216, REGS_OTHER = 56;
   static_assert(NWARPS % 4 == 0, "whole warpgroups");
-  static_assert(128 * NS * REGS_SOFTMAX + 32 * (NWARPS - 4 * NS) * REGS_OTHER <= THREADS * REGS_LAUNCH,
+  static_assert(!SPLIT || 128 * NS * REGS_SOFTMAX + 32 * (NWARPS - 4 * NS) * REGS_OTHER <= THREADS * REGS_LAUNCH,
                 "register split");
   static_assert(NS * TMEM_STREAM <= TMEM_COLS, "TMEM budget");
-  static_assert(HD == 16 || HD == 32 || HD == 64, "this kernel covers head_dim 16, 32 and 64");
+  static_assert(HD == 16 || HD == 32 || HD == 64 || HD == 128 || HD == 256,
+                "this kernel covers head_dim 16, 32, 64, 128 and 256");
+  static_assert(ON - ON0 <= 256 && ON0 % 16 == 0, "P.V MMA widths");
   static_assert(STREAM_BYTES % 1024 == 0 && S_V % 1024 == 0 && V_STAGE % 1024 == 0, "alignment");
   static_assert(SMEM_ALLOC <= 232448, "shared memory budget");
 };
@@ -186,7 +201,7 @@ __global__ void __launch_bounds__(AttnDbLayout<HD>::THREADS, 1)
 
   if (warp >= L::W_PROD && warp < L::W_MMA) {
     // ------------------------------------------------------------ producer of stream warp - W_PROD
-    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(L::REGS_OTHER));
+    if constexpr (L::SPLIT) asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(L::REGS_OTHER));
     if (lane == 0) {
       const int s = warp - L::W_PROD;
       uint64_t* b = bars_all + s * L::NBAR_STREAM;
@@ -200,55 +215,64 @@ __global__ void __launch_bounds__(AttnDbLayout<HD>::THREADS, 1)
            w = first_item(w + G2)) {
         const AttnItem item = attn_item(p, w, n_qt);
         const int nt = n_tiles(item);
-        const int qb = it & 1;
-        if (!(ok = wait_phase(&b[L::B_QE + qb], ((it >> 1) & 1) ^ 1, wd, 0x131))) break;
+        const int qb = it % L::NQ;
+        if (!(ok = wait_phase(&b[L::B_QE + qb], ((it / L::NQ) & 1) ^ 1, wd, 0x131))) break;
         mbar_arrive_expect_tx(&b[L::B_QF + qb], L::Q_BYTES);
-        tma_load_3d(sb + L::S_Q + qb * L::Q_BYTES, &tmQ, &b[L::B_QF + qb], 0, item.q0, item.bh);
+#pragma unroll
+        for (int a = 0; a < L::NATOM; ++a)
+          tma_load_3d(sb + L::S_Q + qb * L::Q_BYTES + a * L::Q_ATOM, &tmQ, &b[L::B_QF + qb], a * L::KATOM,
+                      item.q0, item.bh);
         ++it;
         for (int j = 0; j < nt; ++j) {
           const int st = t % NST;
           if (!(ok = wait_phase(&b[L::B_KE + st], ((t / NST) & 1) ^ 1, wd, 0x132))) break;
           mbar_arrive_expect_tx(&b[L::B_KF + st], L::K_BYTES + L::V_BYTES);
-          tma_load_3d(sb + L::S_K + st * L::K_BYTES, &tmK, &b[L::B_KF + st], 0, j * BN, item.bh);
+#pragma unroll
+          for (int a = 0; a < L::NATOM; ++a)
+            tma_load_3d(sb + L::S_K + st * L::K_BYTES + a * L::K_ATOM, &tmK, &b[L::B_KF + st], a * L::KATOM,
+                        j * BN, item.bh);
           tma_load_3d(sb + L::S_V + st * L::V_STAGE, &tmV, &b[L::B_KF + st], j * BN, 0, item.bh);
           ++t;
         }
       }
       // Let every copy this stream started land before the CTA may exit.
-      for (int i = (it > 2 ? it - 2 : 0); i < it; ++i)
-        wait_drain(&b[L::B_QF + (i & 1)], (i >> 1) & 1, kDrainLimitNs);
+      for (int i = (it > L::NQ ? it - L::NQ : 0); i < it; ++i)
+        wait_drain(&b[L::B_QF + i % L::NQ], (i / L::NQ) & 1, kDrainLimitNs);
       for (int i = (t > NST ? t - NST : 0); i < t; ++i)
         wait_drain(&b[L::B_KF + i % NST], (i / NST) & 1, kDrainLimitNs);
     }
   } else if (warp >= 6 * NS) {
     // ------------------------------------------------------------ idle warps (whole warpgroups)
-    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(L::REGS_OTHER));
+    if constexpr (L::SPLIT) asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(L::REGS_OTHER));
   } else if (warp >= L::W_MMA) {
     // ------------------------------------------------------------ MMA issuer of stream warp - W_MMA
-    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(L::REGS_OTHER));
+    if constexpr (L::SPLIT) asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(L::REGS_OTHER));
     if (lane == 0) {
       const int s = warp - L::W_MMA;
       uint64_t* b = bars_all + s * L::NBAR_STREAM;
       const uint32_t sb = smem_u32(smem + s * L::STREAM_BYTES);
       const uint32_t tS = tmem_base + s * L::TMEM_STREAM;
-      constexpr uint32_t kSwQK = swizzle_kind_for_bytes(HD * 2);
-      constexpr uint32_t kSboQK = 8 * HD * 2;
+      constexpr uint32_t kSwQK = swizzle_kind_for_bytes(L::KATOM * 2);
+      constexpr uint32_t kSboQK = 8 * L::KATOM * 2;
       const uint32_t idesc_s = umma_idesc_f16_f32(BM, BN);
-      const uint32_t idesc_o = umma_idesc_f16_f32(BM, L::ON);
+      const uint32_t idesc_o = umma_idesc_f16_f32(BM, L::ON0);
+      const uint32_t idesc_o1 = umma_idesc_f16_f32(BM, L::ON > L::ON0 ? L::ON - L::ON0 : 16);
       // S cursor: item w_s, tile j_s of n_s, stream tile u, item count it_s.
       int w_s = first_item(NS * static_cast<int>(blockIdx.x) + s), j_s = 0, n_s = 0, u = 0, it_s = 0;
       if (w_s < n_items) n_s = n_tiles(attn_item(p, w_s, n_qt));
       auto issue_s = [&]() -> bool {
-        const int st = u % NST, qb = it_s & 1, bb = u % NSB;
-        if (j_s == 0 && !wait_phase(&b[L::B_QF + qb], (it_s >> 1) & 1, wd, 0x231)) return false;
+        const int st = u % NST, qb = it_s % L::NQ, bb = u % NSB;
+        if (j_s == 0 && !wait_phase(&b[L::B_QF + qb], (it_s / L::NQ) & 1, wd, 0x231)) return false;
         if (!wait_phase(&b[L::B_KF + st], (u / NST) & 1, wd, 0x232)) return false;
         // S buffer bb last held P_{u-NSB}, read by P.V of tile u - NSB, which
         // this thread issued before this MMA (same-thread MMAs execute in order).
         tc_fence_after();
 #pragma unroll
         for (int kk = 0; kk < HD / 16; ++kk) {
-          const uint64_t da = umma_sdesc(sb + L::S_Q + qb * L::Q_BYTES + kk * 32, kSboQK, kSwQK);
-          const uint64_t db = umma_sdesc(sb + L::S_K + st * L::K_BYTES + kk * 32, kSboQK, kSwQK);
+          // Features 16kk .. 16kk+15: atom 16kk / KATOM, 32-byte step within it.
+          const int qa = (16 * kk) / L::KATOM, qo = ((16 * kk) % L::KATOM) * 2;
+          const uint64_t da = umma_sdesc(sb + L::S_Q + qb * L::Q_BYTES + qa * L::Q_ATOM + qo, kSboQK, kSwQK);
+          const uint64_t db = umma_sdesc(sb + L::S_K + st * L::K_BYTES + qa * L::K_ATOM + qo, kSboQK, kSwQK);
           umma_f16(tS + bb * BN, da, db, idesc_s, kk > 0 ? 1u : 0u);
         }
         umma_commit(&b[L::B_SF + bb]);
@@ -277,8 +301,12 @@ __global__ void __launch_bounds__(AttnDbLayout<HD>::THREADS, 1)
 #pragma unroll
         for (int kk = 0; kk < BN / 16; ++kk) {
           // Keys 16kk .. 16kk+15 of P_t: columns 8kk .. 8kk+7 of S buffer bb (FP16 pairs).
-          const uint64_t db = umma_sdesc(sb + L::S_V + st * L::V_STAGE + kk * 32, 1024, kSw128);
-          umma_f16_ts(tO, tS + bb * BN + kk * 8, db, idesc_o, (kk > 0 || j_o > 0) ? 1u : 0u);
+          const uint32_t vrow0 = sb + L::S_V + st * L::V_STAGE + kk * 32;
+          const uint32_t acc = (kk > 0 || j_o > 0) ? 1u : 0u;
+          umma_f16_ts(tO, tS + bb * BN + kk * 8, umma_sdesc(vrow0, 1024, kSw128), idesc_o, acc);
+          if constexpr (L::ON > L::ON0)  // rows ON0 .. ON - 1 of [V | 1]^T: 128 bytes each
+            umma_f16_ts(tO + L::ON0, tS + bb * BN + kk * 8, umma_sdesc(vrow0 + L::ON0 * 128, 1024, kSw128),
+                        idesc_o1, acc);
         }
         umma_commit(&b[L::B_KE + st]);
         umma_commit(&b[L::B_PE + bb]);  // P.V of tile t done (the rescale path waits on it)
@@ -297,7 +325,7 @@ __global__ void __launch_bounds__(AttnDbLayout<HD>::THREADS, 1)
     }
   } else {
     // ------------------------------------------------------------ softmax
-    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(L::REGS_SOFTMAX));
+    if constexpr (L::SPLIT) asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(L::REGS_SOFTMAX));
     const int s = warp >> 2;  // stream
     const int q = warp & 3;   // TMEM lane quadrant (warp % 4)
     const int row = q * 32 + lane;
@@ -318,44 +346,76 @@ __global__ void __launch_bounds__(AttnDbLayout<HD>::THREADS, 1)
       const int ob = pend_it % L::NOB;
       if (!warp_wait_phase(&b[L::B_OF + ob], (pend_it / L::NOB) & 1, wd, 0x333)) return false;
       tc_fence_after();
-      uint32_t o[HD];
-      uint32_t lv[8];  // row sum of the FP16 probabilities (column HD of the accumulator)
-      if constexpr (HD == 64) {
-        uint32_t(&o0)[32] = *reinterpret_cast<uint32_t(*)[32]>(o);
-        uint32_t(&o1)[32] = *reinterpret_cast<uint32_t(*)[32]>(o + 32);
-        tmem_ld_x32(tS + L::TMEM_O + ob * L::ON, o0);
-        tmem_ld_x32(tS + L::TMEM_O + ob * L::ON + 32, o1);
-        tmem_ld_x8(tS + L::TMEM_O + ob * L::ON + HD, lv);
-        tmem_ld_wait_tied(o0);
-        tmem_ld_wait_tied(o1);
-      } else {
-        if constexpr (HD == 32) {
-          tmem_ld_x32(tS + L::TMEM_O + ob * L::ON, o);
-        } else {
-          tmem_ld_x16(tS + L::TMEM_O + ob * L::ON, o);
-        }
-        tmem_ld_x8(tS + L::TMEM_O + ob * L::ON + HD, lv);
-        tmem_ld_wait_tied(o);
-      }
-      tmem_ld_wait_tied(lv);
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&b[L::B_OR + ob]);
-      pend = false;
-      const float lsum = __uint_as_float(lv[0]);
-      const float pend_inv = (pend_valid && lsum > 0.f) ? 1.f / lsum : 0.f;
-      if (pend_store) {
+      if constexpr (HD >= 128) {
+        // O comes out 32 columns at a time (a whole row would take HD registers).
+        const uint32_t tOf = tS + L::TMEM_O + ob * L::ON;
+        uint32_t lv[8];  // row sum of the FP16 probabilities (column HD of the accumulator)
+        tmem_ld_x8(tOf + HD, lv);
+        tmem_ld_wait_tied(lv);
+        const float lsum = __uint_as_float(lv[0]);
+        const float inv = (pend_valid && lsum > 0.f) ? 1.f / lsum : 0.f;
+#pragma unroll 1
+        for (int c = 0; c < HD / 32; ++c) {
+          uint32_t o[32];
+          tmem_ld_x32(tOf + 32 * c, o);
+          tmem_ld_wait_tied(o);
+          if (pend_store) {
 #pragma unroll
-        for (int i = 0; i < HD / 8; ++i) {
-          uint4 v;
-          v.x = pack_half2(__uint_as_float(o[8 * i + 0]) * pend_inv, __uint_as_float(o[8 * i + 1]) * pend_inv);
-          v.y = pack_half2(__uint_as_float(o[8 * i + 2]) * pend_inv, __uint_as_float(o[8 * i + 3]) * pend_inv);
-          v.z = pack_half2(__uint_as_float(o[8 * i + 4]) * pend_inv, __uint_as_float(o[8 * i + 5]) * pend_inv);
-          v.w = pack_half2(__uint_as_float(o[8 * i + 6]) * pend_inv, __uint_as_float(o[8 * i + 7]) * pend_inv);
-          if (i < n_out16) reinterpret_cast<uint4*>(pend_dst)[i] = v;
+            for (int i = 0; i < 4; ++i) {
+              uint4 v;
+              v.x = pack_half2(__uint_as_float(o[8 * i + 0]) * inv, __uint_as_float(o[8 * i + 1]) * inv);
+              v.y = pack_half2(__uint_as_float(o[8 * i + 2]) * inv, __uint_as_float(o[8 * i + 3]) * inv);
+              v.z = pack_half2(__uint_as_float(o[8 * i + 4]) * inv, __uint_as_float(o[8 * i + 5]) * inv);
+              v.w = pack_half2(__uint_as_float(o[8 * i + 6]) * inv, __uint_as_float(o[8 * i + 7]) * inv);
+              if (4 * c + i < n_out16) reinterpret_cast<uint4*>(pend_dst)[4 * c + i] = v;
+            }
+          }
         }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&b[L::B_OR + ob]);
+        pend = false;
+        return true;
+      } else {
+        uint32_t o[HD];
+        uint32_t lv[8];  // row sum of the FP16 probabilities (column HD of the accumulator)
+        if constexpr (HD == 64) {
+          uint32_t(&o0)[32] = *reinterpret_cast<uint32_t(*)[32]>(o);
+          uint32_t(&o1)[32] = *reinterpret_cast<uint32_t(*)[32]>(o + 32);
+          tmem_ld_x32(tS + L::TMEM_O + ob * L::ON, o0);
+          tmem_ld_x32(tS + L::TMEM_O + ob * L::ON + 32, o1);
+          tmem_ld_x8(tS + L::TMEM_O + ob * L::ON + HD, lv);
+          tmem_ld_wait_tied(o0);
+          tmem_ld_wait_tied(o1);
+        } else {
+          if constexpr (HD == 32) {
+            tmem_ld_x32(tS + L::TMEM_O + ob * L::ON, o);
+          } else if constexpr (HD == 16) {
+            tmem_ld_x16(tS + L::TMEM_O + ob * L::ON, o);
+          }
+          tmem_ld_x8(tS + L::TMEM_O + ob * L::ON + HD, lv);
+          tmem_ld_wait_tied(o);
+        }
+        tmem_ld_wait_tied(lv);
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&b[L::B_OR + ob]);
+        pend = false;
+        const float lsum = __uint_as_float(lv[0]);
+        const float pend_inv = (pend_valid && lsum > 0.f) ? 1.f / lsum : 0.f;
+        if (pend_store) {
+#pragma unroll
+          for (int i = 0; i < HD / 8; ++i) {
+            uint4 v;
+            v.x = pack_half2(__uint_as_float(o[8 * i + 0]) * pend_inv, __uint_as_float(o[8 * i + 1]) * pend_inv);
+            v.y = pack_half2(__uint_as_float(o[8 * i + 2]) * pend_inv, __uint_as_float(o[8 * i + 3]) * pend_inv);
+            v.z = pack_half2(__uint_as_float(o[8 * i + 4]) * pend_inv, __uint_as_float(o[8 * i + 5]) * pend_inv);
+            v.w = pack_half2(__uint_as_float(o[8 * i + 6]) * pend_inv, __uint_as_float(o[8 * i + 7]) * pend_inv);
+            if (i < n_out16) reinterpret_cast<uint4*>(pend_dst)[i] = v;
+          }
+        }
+        return true;
       }
-      return true;
     };
 
     for (int w = NS * static_cast<int>(blockIdx.x) + s; ok && w < n_items; w += G2) {

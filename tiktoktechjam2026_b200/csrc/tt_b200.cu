@@ -38,6 +38,9 @@ constexpr int kSmemBudget = 225 * 1024;
 // (features 8..15 of Q and K zero) so that the head_dim-16 attention kernel,
 // whose MMAs need K = 16, runs on it unchanged.
 inline int stored_head_dim(int hd) { return hd < 16 ? 16 : hd; }
+inline bool attention_head_dim_ok(int hd) {
+  return hd == 8 || hd == 16 || hd == 32 || hd == 64 || hd == 128 || hd == 256;
+}
 
 thread_local char g_last_error[512] = "";
 std::atomic<unsigned long long> g_launches{0};
@@ -294,6 +297,11 @@ int clamp_nst(int ksw, int bn, int k, int want, int epi, int n_total) {
 // multiple of 64 or the 512-column residual tile needs the smaller stage.
 int gemm_ksw(int k, int bn) { return (k % 64 == 0 && bn <= 256) ? 64 : 32; }
 
+// Rows wider than TMEM's 512 accumulator columns: the residual GEMMs run in
+// 256-column splits without their LayerNorm, which a row kernel applies after.
+bool wide_model(int d_model) { return d_model == 768 || d_model == 1024; }
+constexpr int kWideBn = 256;
+
 bool ffn_fusable(int d_model, int ffn) {
   return (d_model == 32 || d_model == 64 || d_model == 128 || d_model == 256) && ffn % 128 == 0;
 }
@@ -302,10 +310,10 @@ int check_model_shape(int d_model, int heads, int ffn) {
   if (d_model <= 0 || heads <= 0 || ffn <= 0 || d_model % heads != 0)
     return fail(TT_ERR_SHAPE, "invalid (d_model=%d, heads=%d, ffn=%d)", d_model, heads, ffn);
   const int hd = d_model / heads;
-  if (hd != 8 && hd != 16 && hd != 32 && hd != 64)
-    return fail(TT_ERR_UNSUPPORTED, "head_dim %d not in {8, 16, 32, 64}", hd);
-  if (d_model % 32 != 0 || d_model > 512 || (d_model > 256 && d_model != 512))
-    return fail(TT_ERR_UNSUPPORTED, "d_model %d must be a multiple of 32, <= 256, or 512", d_model);
+  if (!attention_head_dim_ok(hd))
+    return fail(TT_ERR_UNSUPPORTED, "head_dim %d not in {8, 16, 32, 64, 128, 256}", hd);
+  if (d_model % 32 != 0 || (d_model > 256 && d_model != 512 && !wide_model(d_model)))
+    return fail(TT_ERR_UNSUPPORTED, "d_model %d must be a multiple of 32 up to 256, 512, 768 or 1024", d_model);
   if (ffn % 32 != 0) return fail(TT_ERR_UNSUPPORTED, "ffn %d must be a multiple of 32", ffn);
   return TT_OK;
 }
@@ -454,14 +462,15 @@ int encode_ffn_maps(FfnMaps* maps, const void* a, const void* w1, const void* w2
 }
 
 int run_layernorm(const float* x, const float* gamma, const float* beta, void* out,
-                  long long n_rows, int d, float eps, int out_f16, cudaStream_t stream) {
+                  long long n_rows, int d, float eps, int out_f16, cudaStream_t stream,
+                  const uint8_t* row_mask = nullptr) {
   if (n_rows <= 0) return TT_OK;
   const unsigned grid = static_cast<unsigned>((n_rows + 7) / 8);
   switch (d / 32) {
 #define TT_LN_CASE(V)                                                                  \
   case V:                                                                              \
     launch_kernel(layernorm_rows_kernel<V>, grid, 256, 0, stream, x, gamma, beta, out, n_rows, eps, \
-                  out_f16);                                                                        \
+                  out_f16, row_mask);                                                              \
     break;
     TT_LN_CASE(1)
     TT_LN_CASE(2)
@@ -470,6 +479,7 @@ int run_layernorm(const float* x, const float* gamma, const float* beta, void* o
     TT_LN_CASE(8)
     TT_LN_CASE(12)
     TT_LN_CASE(16)
+    TT_LN_CASE(24)
     TT_LN_CASE(32)
 #undef TT_LN_CASE
     default:
@@ -481,7 +491,7 @@ int run_layernorm(const float* x, const float* gamma, const float* beta, void* o
 int check_ln_width(int d) {
   const int v = d / 32;
   if (d % 32 != 0 || !(v == 1 || v == 2 || v == 3 || v == 4 || v == 8 || v == 12 || v == 16 ||
-                       v == 32))
+                       v == 24 || v == 32))
     return fail(TT_ERR_UNSUPPORTED, "layernorm width %d not supported", d);
   return TT_OK;
 }
@@ -496,10 +506,12 @@ int encode_attention_maps(CUtensorMap* tq, CUtensorMap* tk, CUtensorMap* tv, con
                               static_cast<uint64_t>(bh)};
     const uint64_t strides[2] = {static_cast<uint64_t>(hd) * 2,
                                  static_cast<uint64_t>(hd) * seq * 2};
-    const uint32_t box[3] = {static_cast<uint32_t>(hd), 128, 1};
+    // 128-query and 64-key tiles; above 64 features (128-byte rows) a tile is
+    // copied as several boxes of 64 features, one per swizzle atom.
+    const uint32_t inner = static_cast<uint32_t>(hd < 64 ? hd : 64);
+    const uint32_t box[3] = {inner, 128, 1};
     if (int rc = encode_f16(tq, q, 3, dims, strides, box)) return rc;
-    // Key tiles: 64 keys for head_dim <= 32 (attn_db_fwd_kernel), else 128.
-    const uint32_t kbox[3] = {static_cast<uint32_t>(hd), 64u, 1};  // 64-key tiles (attn_db_fwd_kernel)
+    const uint32_t kbox[3] = {inner, 64u, 1};
     if (int rc = encode_f16(tk, k, 3, dims, strides, kbox)) return rc;
   }
   {
@@ -513,35 +525,44 @@ int encode_attention_maps(CUtensorMap* tq, CUtensorMap* tk, CUtensorMap* tv, con
   return TT_OK;
 }
 
+template <int HD>
+int launch_attn_db(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv, const AttnParams& ap,
+                   int n_items, int sm_count, cudaStream_t stream) {
+  using L = AttnDbLayout<HD>;
+  auto kern = attn_db_fwd_kernel<HD>;
+  KernelInfo ki;
+  if (int rc = kernel_info(reinterpret_cast<const void*>(kern), L::SMEM_ALLOC, &ki)) return rc;
+  // The kernel splits its registers with setmaxnreg; that split is only sound
+  // when each thread is launched with exactly the planned register count.
+  if (L::SPLIT ? ki.regs != L::REGS_LAUNCH : ki.regs > 255)
+    return fail(TT_ERR_UNSUPPORTED, "attention kernel built with %d registers per thread, expected %d", ki.regs,
+                L::REGS_LAUNCH);
+  const int ctas = (n_items + L::NS - 1) / L::NS;
+  const unsigned grid = static_cast<unsigned>(ctas < sm_count ? ctas : sm_count);
+  launch_kernel(kern, grid, L::THREADS, L::SMEM_ALLOC, stream, tq, tk, tv, ap, n_items);
+  return TT_OK;
+}
+
 int launch_attention(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
                      const AttnParams& ap, int hd, int sm_count, cudaStream_t stream) {
   const long long n_qt = (ap.seq + 127) / 128;
   const long long items = static_cast<long long>(ap.batch) * ap.heads * n_qt;
   if (items > 0x7fffffffLL) return fail(TT_ERR_SHAPE, "batch*heads*query tiles too large");
   const int n_items = static_cast<int>(items);
-  const unsigned grid = static_cast<unsigned>(n_items < sm_count ? n_items : sm_count);
   if (ap.ctx_hd != hd) return fail(TT_ERR_ARG, "ctx head width %d != head_dim %d", ap.ctx_hd, hd);
-  if (hd == 8 || hd == 16 || hd == 32 || hd == 64) {
-    // Two streams per CTA, 64-key tiles, double-buffered scores with the probabilities over them in TMEM.
-    // head_dim 8 runs the head_dim-16 kernel on its zero-padded Q/K/V.
-    auto kern = hd <= 16 ? attn_db_fwd_kernel<16> : hd == 32 ? attn_db_fwd_kernel<32> : attn_db_fwd_kernel<64>;
-    const int smem = hd <= 16   ? AttnDbLayout<16>::SMEM_ALLOC
-                     : hd == 32 ? AttnDbLayout<32>::SMEM_ALLOC
-                                : AttnDbLayout<64>::SMEM_ALLOC;
-    KernelInfo ki;
-    if (int rc = kernel_info(reinterpret_cast<const void*>(kern), smem, &ki)) return rc;
-    // The kernel splits its registers with setmaxnreg; that split is only sound
-    // when each thread is launched with exactly the planned register count.
-    if (ki.regs != AttnDbLayout<32>::REGS_LAUNCH)
-      return fail(TT_ERR_UNSUPPORTED, "attention kernel built with %d registers per thread, expected %d",
-                  ki.regs, AttnDbLayout<32>::REGS_LAUNCH);
-    const int ctas = (n_items + AttnDbLayout<32>::NS - 1) / AttnDbLayout<32>::NS;
-    const unsigned grid2 = static_cast<unsigned>(ctas < sm_count ? ctas : sm_count);
-    launch_kernel(kern, grid2, AttnDbLayout<32>::THREADS, smem, stream, tq, tk, tv, ap, n_items);
-    (void)grid;
-  } else {
-    return fail(TT_ERR_UNSUPPORTED, "head_dim %d not in {8, 16, 32, 64}", hd);
+  // 64-key tiles, scores and the probabilities over them in TMEM; head_dim 8
+  // runs the head_dim-16 kernel on its zero-padded Q/K/V.
+  int rc;
+  switch (hd) {
+    case 8:
+    case 16: rc = launch_attn_db<16>(tq, tk, tv, ap, n_items, sm_count, stream); break;
+    case 32: rc = launch_attn_db<32>(tq, tk, tv, ap, n_items, sm_count, stream); break;
+    case 64: rc = launch_attn_db<64>(tq, tk, tv, ap, n_items, sm_count, stream); break;
+    case 128: rc = launch_attn_db<128>(tq, tk, tv, ap, n_items, sm_count, stream); break;
+    case 256: rc = launch_attn_db<256>(tq, tk, tv, ap, n_items, sm_count, stream); break;
+    default: return fail(TT_ERR_UNSUPPORTED, "head_dim %d not in {8, 16, 32, 64, 128, 256}", hd);
   }
+  if (rc) return rc;
   return after_launch("attention");
 }
 
@@ -761,9 +782,10 @@ int bind_workspace(tt_model* m, int batch, int seq, void* ws) {
     m->route_seq = seq;
     // Weight maps depend on the route's column tiles.
     m->ksw_qkv = gemm_ksw(m->D, m->route.qkv_bn);
-    m->ksw_out = gemm_ksw(m->D, m->D);
+    const int resid_bn = wide_model(m->D) ? kWideBn : m->D;  // column tile of the residual GEMMs
+    m->ksw_out = gemm_ksw(m->D, resid_bn);
     m->ksw_in = gemm_ksw(m->D, m->route.ffn_in_bn);
-    m->ksw_out2 = gemm_ksw(m->F, m->D);
+    m->ksw_out2 = gemm_ksw(m->F, resid_bn);
     m->tm_wqkv.resize(m->L);
     m->tm_wout.resize(m->L);
     m->tm_win.resize(m->L);
@@ -951,6 +973,8 @@ int tt_causal_attention(const void* q, const void* k, const void* vt, const uint
   if (!q || !k || !vt || !ctx || (key_mask && !kv_end)) return fail(TT_ERR_ARG, "null argument");
   if (batch <= 0 || seq <= 0 || heads <= 0 || seq_pad < seq || seq_pad % 8 != 0)
     return fail(TT_ERR_SHAPE, "invalid sizes");
+  if (!attention_head_dim_ok(head_dim))
+    return fail(TT_ERR_UNSUPPORTED, "head_dim %d not in {8, 16, 32, 64, 128, 256}", head_dim);
   CUtensorMap tq, tk, tv;
   if (int rc = encode_attention_maps(&tq, &tk, &tv, q, k, vt, batch * heads, seq, head_dim, seq_pad))
     return rc;
@@ -1025,13 +1049,15 @@ int tt_linear_residual_layernorm(const void* a, const void* w, const float* bias
     return fail(TT_ERR_ARG, "null argument");
   if (n_rows <= 0 || n_rows > 0x7fffffffLL || k_in <= 0 || k_in % 32 != 0)
     return fail(TT_ERR_SHAPE, "invalid n_rows/k_in (%lld, %d)", (long long)n_rows, k_in);
-  if (d_model % 32 != 0 || d_model <= 0 || (d_model > 256 && d_model != 512))
-    return fail(TT_ERR_UNSUPPORTED, "d_model %d must be a multiple of 32, <= 256, or 512", d_model);
-  const int ksw = gemm_ksw(k_in, d_model);
+  if (d_model % 32 != 0 || d_model <= 0 || (d_model > 256 && d_model != 512 && !wide_model(d_model)))
+    return fail(TT_ERR_UNSUPPORTED, "d_model %d must be a multiple of 32 up to 256, 512, 768 or 1024", d_model);
+  const bool wide = wide_model(d_model);
+  const int bn = wide ? kWideBn : d_model;
+  const int ksw = gemm_ksw(k_in, bn);
   GemmMaps maps;
   memset(&maps, 0, sizeof(maps));
   if (int rc = encode_matrix(&maps.a, a, n_rows, k_in, ksw, 128)) return rc;
-  if (int rc = encode_matrix(&maps.w, w, d_model, k_in, ksw, d_model > 256 ? 256 : d_model)) return rc;
+  if (int rc = encode_matrix(&maps.w, w, d_model, k_in, ksw, bn > 256 ? 256 : bn)) return rc;
   if (int rc = encode_epi_tile(&maps.out0, resid_out, n_rows, d_model, true)) return rc;
   if (int rc = encode_epi_tile(&maps.out1, norm_out, n_rows, d_model, norm_out_is_f16 == 0)) return rc;
   if (int rc = encode_epi_tile(&maps.res, resid_in, n_rows, d_model, true)) return rc;
@@ -1039,8 +1065,9 @@ int tt_linear_residual_layernorm(const void* a, const void* w, const float* bias
   p.M = static_cast<int>(n_rows);
   p.N_total = d_model;
   p.K = k_in;
-  p.bn = d_model;
-  p.n_splits = 1;
+  p.bn = bn;
+  p.n_splits = d_model / bn;
+  p.no_norm = wide ? 1 : 0;
   p.nst = clamp_nst(ksw, p.bn, p.K, 4, EPI_RESID_LN, p.N_total);
   p.bias = bias;
   p.gamma = gamma;
@@ -1048,7 +1075,12 @@ int tt_linear_residual_layernorm(const void* a, const void* w, const float* bias
   p.norm_f16 = norm_out_is_f16 ? 1 : 0;
   p.eps = eps;
   p.row_mask = row_mask;
-  return launch_gemm(ksw, EPI_RESID_LN, maps, p, ds->sm_count, static_cast<cudaStream_t>(stream));
+  const cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (int rc = launch_gemm(ksw, EPI_RESID_LN, maps, p, ds->sm_count, s)) return rc;
+  if (!wide) return TT_OK;
+  // Rows wider than TMEM: the LayerNorm of the residual sum runs as a row kernel.
+  return run_layernorm(resid_out, gamma, beta, norm_out, n_rows, d_model, eps, norm_out_is_f16 ? 1 : 0, s,
+                       row_mask);
 }
 
 int tt_linear_gelu(const void* a, const void* w, const float* bias, void* out, int64_t n_rows,
@@ -1258,6 +1290,7 @@ int model_forward(tt_model* m, const float* x, const uint8_t* mask, float* out, 
   int* kv_end = reinterpret_cast<int*>(base + w.kv_end);
   const int N = static_cast<int>(Nll);
   const int D = m->D, F = m->F, H = m->H, hd = D / H;
+  const bool wide = wide_model(D);
   cudaEvent_t ev = nullptr;
   // Per-call maps: the caller's input (residual of layer 0) and output.
   CUtensorMap tm_x, tm_out;
@@ -1339,9 +1372,10 @@ int model_forward(tt_model* m, const float* x, const uint8_t* mask, float* out, 
       p.M = N;
       p.N_total = D;
       p.K = D;
-      p.bn = D;
-      p.n_splits = 1;
-      p.nst = clamp_nst(m->ksw_out, D, D, r.out_nst, EPI_RESID_LN, D);
+      p.bn = wide ? kWideBn : D;
+      p.n_splits = D / p.bn;
+      p.no_norm = wide ? 1 : 0;
+      p.nst = clamp_nst(m->ksw_out, p.bn, D, r.out_nst, EPI_RESID_LN, D);
       p.bias = lw.b_out;
       p.gamma = lw.ln_attn_w;
       p.beta = lw.ln_attn_b;
@@ -1355,6 +1389,10 @@ int model_forward(tt_model* m, const float* x, const uint8_t* mask, float* out, 
       maps.res = (l == 0) ? tm_x : m->tm_resid;
       if (int rc = record_begin(m, s, &ev)) return rc;
       if (int rc = launch_gemm(m->ksw_out, EPI_RESID_LN, maps, p, ds->sm_count, s)) return rc;
+      if (wide)
+        if (int rc = run_layernorm(reinterpret_cast<const float*>(base + w.resid), lw.ln_attn_w, lw.ln_attn_b,
+                                   norm, N, D, m->eps, 1, s))
+          return rc;
       if (int rc = record_end(m, s, TT_KERNEL_OUT_LN, ev)) return rc;
     }
     if (last && out_guard)
@@ -1439,9 +1477,10 @@ int model_forward(tt_model* m, const float* x, const uint8_t* mask, float* out, 
       p.M = N;
       p.N_total = D;
       p.K = F;
-      p.bn = D;
-      p.n_splits = 1;
-      p.nst = clamp_nst(m->ksw_out2, D, F, r.ffn_out_nst, EPI_RESID_LN, D);
+      p.bn = wide ? kWideBn : D;
+      p.n_splits = D / p.bn;
+      p.no_norm = wide ? 1 : 0;
+      p.nst = clamp_nst(m->ksw_out2, p.bn, F, r.ffn_out_nst, EPI_RESID_LN, D);
       p.bias = lw.b_ffn_out;
       p.gamma = lw.ln_next_w;
       p.beta = lw.ln_next_b;
@@ -1455,6 +1494,11 @@ int model_forward(tt_model* m, const float* x, const uint8_t* mask, float* out, 
       maps.res = m->tm_resid;
       if (int rc = record_begin(m, s, &ev)) return rc;
       if (int rc = launch_gemm(m->ksw_out2, EPI_RESID_LN, maps, p, ds->sm_count, s)) return rc;
+      if (wide)
+        if (int rc = run_layernorm(reinterpret_cast<const float*>(base + w.resid), lw.ln_next_w, lw.ln_next_b,
+                                   last ? static_cast<void*>(out) : static_cast<void*>(norm), N, D, m->eps,
+                                   last ? 0 : 1, s, last ? mask : nullptr))
+          return rc;
       if (int rc = record_end(m, s, TT_KERNEL_FFN_OUT_LN, ev)) return rc;
     }
   }

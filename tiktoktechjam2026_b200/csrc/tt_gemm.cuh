@@ -68,6 +68,10 @@ struct GemmParams {
   const float* gamma;
   const float* beta;
   int norm_f16;
+  // 1: the residual sum only (out0), no LayerNorm: rows wider than 512 FP32
+  // accumulator columns run column-split (n_splits > 1) and are normalized by
+  // a row kernel afterwards.
+  int no_norm;
   float eps;
   const uint8_t* row_mask;
   unsigned int* err;
@@ -263,7 +267,7 @@ __global__ void __launch_bounds__(gemm_threads(EPI), 1)
   }
   for (int c = threadIdx.x; c < p.N_total; c += blockDim.x) s_bias[c] = p.bias[c];
   if constexpr (EPI == EPI_RESID_LN) {
-    for (int c = threadIdx.x; c < bn; c += blockDim.x) {
+    for (int c = threadIdx.x; c < (p.no_norm ? 0 : bn); c += blockDim.x) {
       s_gamma[c] = p.gamma[c];
       s_beta[c] = p.beta[c];
     }
@@ -387,7 +391,7 @@ __global__ void __launch_bounds__(gemm_threads(EPI), 1)
 
       if constexpr (EPI == EPI_QKV) {
         const int D = p.d_model, hd = p.head_dim;
-        // head_dim is 16, 32 or 64: heads and features by shift and mask; the
+        // head_dim is a power of two (8 .. 256): heads and features by shift and mask; the
         // Q/K/V part of a column by one division per item (chunks of 32 never
         // straddle a part, D % 32 == 0).
         const int lg_hd = __ffs(hd) - 1;
@@ -567,7 +571,8 @@ __global__ void __launch_bounds__(gemm_threads(EPI), 1)
         }
         }
       } else {
-        // EPI_RESID_LN: bn == N_total == d_model (the whole row lives in TMEM).
+        // EPI_RESID_LN: bn == N_total == d_model (the whole row lives in TMEM),
+        // or, with p.no_norm, any column split of the row (pass 1 only).
         // Pass 1 (two chunks per TMEM wait): r' = acc + bias + residual, written
         // back into TMEM and out to HBM, with FP32 sums of r' - shift (shift =
         // the row's first r') for the mean and variance; pass 2 normalizes.
@@ -608,7 +613,7 @@ __global__ void __launch_bounds__(gemm_threads(EPI), 1)
           uint32_t out[32];
 #pragma unroll
           for (int e = 0; e < 32; ++e) {
-            rr[e] = __uint_as_float(v[e]) + s_bias[c * 32 + e] + res[e];
+            rr[e] = __uint_as_float(v[e]) + s_bias[n0 + c * 32 + e] + res[e];
             out[e] = __float_as_uint(rr[e]);
           }
           if (c == c_lo) shift = rr[0];
@@ -653,6 +658,13 @@ __global__ void __launch_bounds__(gemm_threads(EPI), 1)
           }
         }
         tmem_st_wait();
+        if (p.no_norm) {
+          // The accumulator buffer may be overwritten by the next item's MMAs.
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&acc_empty[ab]);
+          continue;
+        }
         // Row statistics: this warp's columns give (count, mean, M2) from the
         // shifted sums; with the split epilogue the two warps of the quadrant
         // swap theirs through shared memory and both combine them in column

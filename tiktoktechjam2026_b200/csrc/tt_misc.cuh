@@ -8,13 +8,16 @@
 namespace tt {
 
 // LayerNorm of FP32 rows (one warp per row, two-pass mean/variance in FP32),
-// output FP16 or FP32.  Replaces `layers[0].norm1(x)` + the FP16 cast of the
-// reference (mixed_precision/transformer.py:489-491).  Requires d % 32 == 0.
+// output FP16 or FP32; rows whose row_mask byte is 0 (row_mask may be null)
+// are written as zeros.  Replaces `layers[0].norm1(x)` + the FP16 cast of the
+// reference (mixed_precision/transformer.py:489-491), and for d_model above
+// 512 the LayerNorm half of the residual + LayerNorm steps
+// (mixed_precision/transformer.py:223-227, 675-695).  Requires d % 32 == 0.
 template <int VPL>  // values per lane = d / 32
 __global__ void __launch_bounds__(256)
     layernorm_rows_kernel(const float* __restrict__ x, const float* __restrict__ gamma,
                           const float* __restrict__ beta, void* __restrict__ out, long long n_rows,
-                          float eps, int out_f16) {
+                          float eps, int out_f16, const uint8_t* __restrict__ row_mask) {
   pdl_wait();
   pdl_trigger();
   constexpr int D = VPL * 32;
@@ -51,16 +54,17 @@ __global__ void __launch_bounds__(256)
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) q += __shfl_xor_sync(0xffffffffu, q, o);
   const float rstd = rsqrtf(q / static_cast<float>(D) + eps);
+  const bool zero = row_mask != nullptr && row_mask[row] == 0;
   if constexpr (VPL % 4 == 0) {
 #pragma unroll
     for (int i = 0; i < VPL / 4; ++i) {
       const int c = 4 * (lane + 32 * i);
       const float4 g = reinterpret_cast<const float4*>(gamma)[lane + 32 * i];
       const float4 bb = reinterpret_cast<const float4*>(beta)[lane + 32 * i];
-      const float y0 = fmaf((v[4 * i + 0] - mean) * rstd, g.x, bb.x);
-      const float y1 = fmaf((v[4 * i + 1] - mean) * rstd, g.y, bb.y);
-      const float y2 = fmaf((v[4 * i + 2] - mean) * rstd, g.z, bb.z);
-      const float y3 = fmaf((v[4 * i + 3] - mean) * rstd, g.w, bb.w);
+      const float y0 = zero ? 0.f : fmaf((v[4 * i + 0] - mean) * rstd, g.x, bb.x);
+      const float y1 = zero ? 0.f : fmaf((v[4 * i + 1] - mean) * rstd, g.y, bb.y);
+      const float y2 = zero ? 0.f : fmaf((v[4 * i + 2] - mean) * rstd, g.z, bb.z);
+      const float y3 = zero ? 0.f : fmaf((v[4 * i + 3] - mean) * rstd, g.w, bb.w);
       if (out_f16) {
         uint2 w;
         w.x = pack_half2(y0, y1);
@@ -75,7 +79,7 @@ __global__ void __launch_bounds__(256)
 #pragma unroll
     for (int i = 0; i < VPL; ++i) {
       const int c = lane + 32 * i;
-      const float y = fmaf((v[i] - mean) * rstd, gamma[c], beta[c]);
+      const float y = zero ? 0.f : fmaf((v[i] - mean) * rstd, gamma[c], beta[c]);
       if (out_f16)
         reinterpret_cast<__half*>(out)[row * D + c] = __float2half_rn(y);
       else
