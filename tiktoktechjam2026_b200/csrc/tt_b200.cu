@@ -171,6 +171,16 @@ int encode_epi_tile(CUtensorMap* tm, const void* base, uint64_t rows, uint64_t c
                        base, 2, dims, strides, box);
 }
 
+// Store maps of the QKV epilogue's TMA path (seq % 32 == 0, head_dim >= 32):
+// Q and K as [B*H*S, hd], V^T as [B*H*hd, seq_pad], FP16, 32 x 32 boxes.
+int encode_qkv_store_maps(GemmMaps* maps, const void* q, const void* k, const void* vt, int batch, int seq,
+                          int heads, int hd, int seq_pad) {
+  const uint64_t rows = static_cast<uint64_t>(batch) * heads * seq;
+  if (int rc = encode_epi_tile(&maps->out0, q, rows, hd, false)) return rc;
+  if (int rc = encode_epi_tile(&maps->out1, k, rows, hd, false)) return rc;
+  return encode_epi_tile(&maps->res, vt, static_cast<uint64_t>(batch) * heads * hd, seq_pad, false);
+}
+
 // Per (kernel, device): the dynamic shared memory the kernel was opened up to
 // and its register count.  Each is queried or set once, so a launch is only a
 // launch (nothing else happens on the driver while a stream is captured).
@@ -642,6 +652,7 @@ struct tt_model {
   CUtensorMap tm_norm{}, tm_ctx{}, tm_hidden{}, tm_q{}, tm_k{}, tm_vt{};
   // Epilogue tiles (box 32 x 32): QKV stores, residual (FP32), normalized and hidden (FP16).
   CUtensorMap tm_resid{}, tm_norm_st{}, tm_hidden_st{};
+  CUtensorMap tm_q_st{}, tm_k_st{}, tm_vt_st{};  // QKV epilogue's TMA stores (seq % 32 == 0, head_dim >= 32)
   CUtensorMap tm_norm32{};  // normalized activations as the fused FFN's A operand (box {32, 128})
   CUtensorMap tm_norm3{};   // the same as whole 128-row K-block tiles (ffn2_kernel)
   // Profiling.
@@ -834,6 +845,14 @@ int bind_workspace(tt_model* m, int batch, int seq, void* ws) {
                                      base + w.vt, batch * m->H, seq, hd, w.seq_pad))
     return rc;
   if (int rc = encode_epi_tile(&m->tm_resid, base + w.resid, N, m->D, true)) return rc;
+  if (seq % 32 == 0 && hd >= 32) {
+    GemmMaps st;
+    if (int rc = encode_qkv_store_maps(&st, base + w.q, base + w.k, base + w.vt, batch, seq, m->H, hd, w.seq_pad))
+      return rc;
+    m->tm_q_st = st.out0;
+    m->tm_k_st = st.out1;
+    m->tm_vt_st = st.res;
+  }
   if (int rc = encode_epi_tile(&m->tm_norm_st, base + w.norm, N, m->D, false)) return rc;
   if (!m->route.ffn_fused)
     if (int rc = encode_epi_tile(&m->tm_hidden_st, base + w.hidden, N, m->F, false)) return rc;
@@ -945,6 +964,8 @@ int tt_qkv_projection(const void* normalized, const void* w_qkv, const float* b_
   if (reinterpret_cast<uintptr_t>(q) % 16 || reinterpret_cast<uintptr_t>(k) % 16 ||
       reinterpret_cast<uintptr_t>(vt) % 16)
     return fail(TT_ERR_ALIGN, "q, k and vt must be 16-byte aligned");
+  if (tma_out && hd >= 32)
+    if (int rc = encode_qkv_store_maps(&maps, q, k, vt, batch, seq, heads, hd, seq_pad)) return rc;
   GemmParams p = base_params(ds);
   p.M = static_cast<int>(N);
   p.N_total = 3 * d_model;
@@ -1357,6 +1378,9 @@ int model_forward(tt_model* m, const float* x, const uint8_t* mask, float* out, 
       p.d_model = D;
       maps.a = m->tm_norm;
       maps.w = m->tm_wqkv[l];
+      maps.out0 = m->tm_q_st;
+      maps.out1 = m->tm_k_st;
+      maps.res = m->tm_vt_st;
       if (int rc = record_begin(m, s, &ev)) return rc;
       if (int rc = launch_gemm(m->ksw_qkv, EPI_QKV, maps, p, ds->sm_count, s)) return rc;
       if (int rc = record_end(m, s, TT_KERNEL_QKV, ev)) return rc;

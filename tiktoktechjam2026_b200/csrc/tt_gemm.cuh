@@ -79,8 +79,10 @@ struct GemmParams {
 };
 
 // Tensor maps of one GEMM launch.  `a`, `w`: operands (box {KSW, 128} and
-// {KSW, min(bn, 256)}).  Outputs/inputs of the epilogue, box 32 x 32 (EPI_QKV
-// uses none: it stores through GemmParams' pointers):
+// {KSW, min(bn, 256)}).  Outputs/inputs of the epilogue, box 32 x 32:
+//   EPI_QKV       (tma_out, head_dim >= 32) out0 = Q as [B*H*S, hd], out1 = K
+//                 likewise, res = V^T as [B*H*hd, S_pad], all FP16; otherwise
+//                 none (stores through GemmParams' pointers)
 //   EPI_RESID_LN  out0 = residual out (FP32), out1 = normalized (FP16/FP32),
 //                 res  = residual in (FP32)
 //   EPI_GELU      out0 = activation (FP16)
@@ -401,7 +403,6 @@ __global__ void __launch_bounds__(gemm_threads(EPI), 1)
         const int s = valid ? row - bidx * p.seq : 0;
         const int b_w = warp_active ? r0 / p.seq : 0;
         const int s0 = warp_active ? r0 - b_w * p.seq : 0;
-        const int wbox = hd < 32 ? hd : 32;  // columns per sub-box
         // This warp takes chunks ehalf, ehalf + NSTEP, ...; two TMEM loads per wait.
         for (int cb = ehalf; cb < nch; cb += 2 * NSTEP) {
           uint32_t vv[2][32];
@@ -431,29 +432,26 @@ __global__ void __launch_bounds__(gemm_threads(EPI), 1)
             within0 -= D;
             ++which;
           }
-          if (which < 2 && p.tma_out && hd >= 32) {
-            // Q / K: the warp's 32 rows of these 32 features are 64-byte pieces of
-            // consecutive rows of [B*H, S, hd] (the slab lies within one sequence:
-            // S % 32 == 0).  Stage them row-major (16-byte piece k of row r at
-            // r * 64 + ((k ^ ((r >> 1) & 3)) << 4), conflict-free both ways), then
-            // write 8 rows per instruction, 4 lanes per 64-byte piece.
+          if (p.tma_out && hd >= 32) {
+            // Q, K, V^T by TMA bulk stores of [32 x 32] FP16 tiles (64-byte rows,
+            // SWIZZLE_64B) through maps.out0 / out1 / res, the 2-D views
+            // [B*H*S, hd] of Q and K and [B*H*hd, S_pad] of V^T.  The warp's slab
+            // lies within one sequence (S % 32 == 0), so each tile is one box.
             if (!warp_active) continue;
-            const uint32_t slot = ring.base;
-            __syncwarp();
-#pragma unroll
-            for (int k = 0; k < 4; ++k)
-              st_shared_v4(slot + lane * 64 + ((k ^ ((lane >> 1) & 3)) << 4), pack_half2(f[8 * k], f[8 * k + 1]),
-                           pack_half2(f[8 * k + 2], f[8 * k + 3]), pack_half2(f[8 * k + 4], f[8 * k + 5]),
-                           pack_half2(f[8 * k + 6], f[8 * k + 7]));
-            __syncwarp();
             const int hh = within0 >> lg_hd, d0 = within0 & (hd - 1);
-            __half* blk = (which == 0 ? p.q : p.k) +
-                          ((static_cast<size_t>(b_w) * p.heads + hh) * p.seq + s0) * hd + d0;
-#pragma unroll
-            for (int k = 0; k < 4; ++k) {
-              const int rr = 8 * k + (lane >> 2), pc = lane & 3;
-              const uint4 v4 = ld_shared_v4(slot + rr * 64 + ((pc ^ ((rr >> 1) & 3)) << 4));
-              *reinterpret_cast<uint4*>(blk + static_cast<size_t>(rr) * hd + pc * 8) = v4;
+            const int bh = b_w * p.heads + hh;
+            const uint32_t slot = ring.acquire(lane);
+            if (which < 2)
+              stage_row_f16x32(slot, lane, f);
+            else
+              stage_cols_f16<32>(slot, lane, f);
+            ring.publish();
+            if (lane == 0) {
+              if (which < 2)
+                tma_store_2d(which == 0 ? &maps.out0 : &maps.out1, slot, d0, bh * p.seq + s0);
+              else
+                tma_store_2d(&maps.res, slot, s0, bh * hd + d0);
+              bulk_commit_group();
             }
           } else if (which < 2 && hd == 8) {
             // Q / K with head_dim 8, stored 16 wide: each of the chunk's 4 heads is
@@ -498,31 +496,29 @@ __global__ void __launch_bounds__(gemm_threads(EPI), 1)
                 dst[1] = bq;
               }
             }
-          } else if (p.tma_out && hd >= 16) {
-            // V^T: transpose the 32 rows through this warp's staging tile, then write
-            // [wbox features x 32 tokens] as 64-byte rows of [B*H, hd, S_pad] with
-            // coalesced 16-byte stores (the slab lies within one sequence: S % 32 == 0).
+          } else if (p.tma_out && hd == 16) {
+            // V^T at head_dim 16: transpose the 32 rows through this warp's staging
+            // tile, then write two [16 features x 32 tokens] blocks as 64-byte rows
+            // of [B*H, 16, S_pad] with coalesced 16-byte stores (the slab lies
+            // within one sequence: S % 32 == 0).
             if (!warp_active) continue;
             const uint32_t slot = ring.base;
             __syncwarp();
-            if (wbox == 32) {
-              stage_cols_f16<32>(slot, lane, f);
-            } else {
-              stage_cols_f16<16>(slot, lane, f);
-              stage_cols_f16<16>(slot + 1024, lane, f + 16);
-            }
+            stage_cols_f16<16>(slot, lane, f);
+            stage_cols_f16<16>(slot + 1024, lane, f + 16);
             __syncwarp();
 #pragma unroll 1
-            for (int sb = 0; sb < 32 / wbox; ++sb) {
-              const int within = within0 + sb * wbox;
+            for (int sb = 0; sb < 2; ++sb) {
+              const int within = within0 + sb * 16;
               const int hh = within >> lg_hd, d0 = within & (hd - 1);
               const size_t bh = static_cast<size_t>(b_w) * p.heads + hh;
-              for (int k = 0; k < wbox / 8; ++k) {
+              for (int k = 0; k < 2; ++k) {
                 const int d = k * 8 + (lane >> 2), pc = lane & 3;
                 const uint4 q = ld_shared_v4(slot + sb * 1024 + d * 64 + ((pc ^ ((d >> 1) & 3)) << 4));
                 *reinterpret_cast<uint4*>(p.vt + (bh * hd + d0 + d) * p.seq_pad + s0 + pc * 8) = q;
               }
             }
+            __syncwarp();
           } else if (valid) {
             // V^T one element at a time ([B*H, hs, S_pad], hs = 16 for head_dim 8:
             // rows 8..15 of a head are never read into any stored output).
