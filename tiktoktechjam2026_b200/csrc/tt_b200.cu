@@ -284,7 +284,7 @@ const RouteEntry kRouteTable[] = {
     // C3  B256 S256 D32 H2 F128
     {32, 2, 256, 128, {"d32-h2-s256", 96, 1, 1, 128, 1, 4, 1}},
     // C4  B16 S2048 D512 H8 F2048 (+ key padding)
-    {512, 8, 2048, 2048, {"d512-h8-s2048", 256, 4, 2, 256, 4, 2, 0}},
+    {512, 8, 2048, 2048, {"d512-h8-s2048", 256, 4, 3, 256, 4, 3, 0}},
     // C5  B512 S1024 D256 H8 F1024
     {256, 8, 1024, 1024, {"d256-h8-s1024", 256, 3, 2, 256, 2, 3, 1}},
 };
@@ -357,7 +357,10 @@ template <int KSW, int EPI>
 int launch_gemm_t(const GemmMaps& maps, GemmParams p, int sm_count, cudaStream_t stream) {
   const int smem = gemm_smem_bytes(KSW, p.bn, p.nst, EPI, p.N_total);
   if (smem > 232448) return fail(TT_ERR_UNSUPPORTED, "GEMM tile needs %d bytes of shared memory", smem);
-  auto kern = gemm_kernel<KSW, EPI>;
+  // The kernel instance whose residual ring matches the one gemm_smem_bytes sized.
+  void (*kern)(const GemmMaps, const GemmParams) = gemm_kernel<KSW, EPI, gemm_res_ring(EPI, 0)>;
+  if constexpr (EPI == EPI_RESID_LN)
+    if (gemm_res_ring(EPI, p.bn) == 1) kern = gemm_kernel<KSW, EPI, 1>;
   if (int rc = prepare_kernel(kern, smem)) return rc;
   const long long m_tiles = (static_cast<long long>(p.M) + 127) / 128;
   const long long items = m_tiles * p.n_splits;

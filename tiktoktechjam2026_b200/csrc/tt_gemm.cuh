@@ -47,7 +47,9 @@ constexpr int kGemmMaxStages = 8;
 // EPI_RESID_LN runs two epilogue warps per TMEM lane quadrant, each on half
 // of the row's columns, the row statistics combined through shared memory
 // (C5 out-proj 1.27 -> 1.08 ms per forward against one warp per quadrant);
-// kResRing residual tiles are in flight per epilogue warp.
+// kResRing residual tiles are in flight per epilogue warp; one for the
+// 512-column tiles (d_model 512), whose single-accumulator mainloop needs the
+// 32 KB this frees for a third operand stage (C4 FFN-out 2 -> 3 stages).
 constexpr int kResRing = 2;
 constexpr int kEpiTile = 4096;  // one [32 x 32] FP32 tile
 
@@ -113,14 +115,17 @@ __host__ __device__ constexpr int gemm_threads(int epi) { return 32 * (gemm_epi_
 // quadrant, 3 residual tiles and 1 output tile measured 4 % faster than 2 and 2
 // at C5).
 __host__ __device__ constexpr int gemm_out_ring(int epi) { return epi == EPI_RESID_LN ? 1 : 2; }
-__host__ __device__ inline int gemm_epi_bytes(int epi) {
-  return gemm_epi_warps(epi) * ((epi == EPI_RESID_LN ? kResRing : 0) + gemm_out_ring(epi)) * kEpiTile;
+__host__ __device__ constexpr int gemm_res_ring(int epi, int bn) {
+  return epi == EPI_RESID_LN ? (bn > 256 ? 1 : kResRing) : 0;
+}
+__host__ __device__ inline int gemm_epi_bytes(int epi, int rr) {
+  return gemm_epi_warps(epi) * (rr + gemm_out_ring(epi)) * kEpiTile;
 }
 // Layout: stages | epilogue tiles | bias[N_total], gamma[bn], beta[bn] | barriers | misc
 // (+1024 alignment slack)
 __host__ __device__ inline int gemm_smem_bytes(int ksw, int bn, int nst, int epi, int n_total) {
   int off = nst * gemm_stage_bytes(ksw, bn);
-  off += gemm_epi_bytes(epi);
+  off += gemm_epi_bytes(epi, gemm_res_ring(epi, bn));
   off += (n_total + 2 * bn) * 4;
   off += (2 * kGemmMaxStages + 5 + 8 * kResRing + 4 + 1) * 8;
   off += 16;
@@ -213,7 +218,8 @@ struct OutRing {
   }
 };
 
-template <int KSW, int EPI>
+// RR: residual tiles in flight per epilogue warp (gemm_res_ring of the launch's bn).
+template <int KSW, int EPI, int RR>
 __global__ void __launch_bounds__(gemm_threads(EPI), 1)
     gemm_kernel(const __grid_constant__ GemmMaps maps, const GemmParams p) {
   constexpr int NEPI = gemm_epi_warps(EPI);  // epilogue warps 0..NEPI-1
@@ -231,7 +237,7 @@ __global__ void __launch_bounds__(gemm_threads(EPI), 1)
   const int w_bytes_half = (bn > 256 ? 256 : bn) * KSW * 2;
   uint8_t* stages = smem;
   uint8_t* epi = stages + nst * stage_bytes;
-  float* s_bias = reinterpret_cast<float*>(epi + gemm_epi_bytes(EPI));  // [N_total]
+  float* s_bias = reinterpret_cast<float*>(epi + gemm_epi_bytes(EPI, RR));  // [N_total]
   float* s_gamma = s_bias + p.N_total;                                    // [bn] (RESID_LN)
   float* s_beta = s_gamma + bn;
   uint64_t* full = reinterpret_cast<uint64_t*>(s_beta + bn);
@@ -353,11 +359,11 @@ __global__ void __launch_bounds__(gemm_threads(EPI), 1)
     const int eq = warp & 3;    // TMEM lane quadrant (rows eq*32 .. eq*32+31 of the tile)
     const int ehalf = warp >> 2;  // which of the NSTEP warps on this quadrant
     const uint32_t lane_base = static_cast<uint32_t>(eq * 32) << 16;
-    constexpr int kRes = (EPI == EPI_RESID_LN) ? kResRing : 0;
+    constexpr int kRes = (EPI == EPI_RESID_LN) ? RR : 0;
     constexpr int kOut = gemm_out_ring(EPI);
     const uint32_t res_base = smem_u32(epi) + warp * (kRes + kOut) * kEpiTile;
     OutRing<kOut> ring{res_base + kRes * kEpiTile, 0};
-    uint64_t* my_res_full = res_full + warp * kResRing;
+    uint64_t* my_res_full = res_full + warp * kResRing;  // the first RR of them are used
     int res_g = 0;         // residual tiles this warp has requested and consumed
     bool res_pre = false;  // this item's first residual tiles already went out
     int i = 0;
@@ -374,14 +380,14 @@ __global__ void __launch_bounds__(gemm_threads(EPI), 1)
       // with the split epilogue, where the pair of a quadrant shares a row).
       const int c_lo = NSTEP == 2 ? ehalf * nch / 2 : 0;
       const int c_hi = NSTEP == 2 ? (ehalf + 1) * nch / 2 : nch;
-      // Residual tiles of this item: the first kResRing go out now, unless the
+      // Residual tiles of this item: the first RR go out now, unless the
       // previous item sent them during its normalization pass.
       if constexpr (EPI == EPI_RESID_LN) {
         if (lane == 0 && warp_active && !res_pre) {
-          for (int k = 0; c_lo + k < c_hi && k < kResRing; ++k) {
+          for (int k = 0; c_lo + k < c_hi && k < RR; ++k) {
             const int q = res_g + k;
-            mbar_arrive_expect_tx(&my_res_full[q % kResRing], kEpiTile);
-            tma_load_2d_u32(res_base + (q % kResRing) * kEpiTile, &maps.res, &my_res_full[q % kResRing],
+            mbar_arrive_expect_tx(&my_res_full[q % RR], kEpiTile);
+            tma_load_2d_u32(res_base + (q % RR) * kEpiTile, &maps.res, &my_res_full[q % RR],
                             n0 + 32 * (c_lo + k), r0);
           }
         }
@@ -589,17 +595,17 @@ __global__ void __launch_bounds__(gemm_threads(EPI), 1)
           float res[32];
           const int q = res_g + (c - c_lo);
           if (warp_active) {
-            if (!(ok = warp_wait_phase(&my_res_full[q % kResRing], (q / kResRing) & 1, wd, 0x405)))
+            if (!(ok = warp_wait_phase(&my_res_full[q % RR], (q / RR) & 1, wd, 0x405)))
               break;
-            load_row_f32(res_base + (q % kResRing) * kEpiTile, r, res);
+            load_row_f32(res_base + (q % RR) * kEpiTile, r, res);
             __syncwarp();
-            // The slot is read; refill it with the tile kResRing chunks ahead.
-            if (lane == 0 && c + kResRing < c_hi) {
+            // The slot is read; refill it with the tile RR chunks ahead.
+            if (lane == 0 && c + RR < c_hi) {
               fence_proxy_async_smem();
-              const int q2 = q + kResRing;
-              mbar_arrive_expect_tx(&my_res_full[q2 % kResRing], kEpiTile);
-              tma_load_2d_u32(res_base + (q2 % kResRing) * kEpiTile, &maps.res,
-                              &my_res_full[q2 % kResRing], n0 + 32 * (c + kResRing), r0);
+              const int q2 = q + RR;
+              mbar_arrive_expect_tx(&my_res_full[q2 % RR], kEpiTile);
+              tma_load_2d_u32(res_base + (q2 % RR) * kEpiTile, &maps.res,
+                              &my_res_full[q2 % RR], n0 + 32 * (c + RR), r0);
             }
           } else {
 #pragma unroll
@@ -643,10 +649,10 @@ __global__ void __launch_bounds__(gemm_threads(EPI), 1)
           if (r0n < p.M) {
             if (lane == 0) {
               fence_proxy_async_smem();
-              for (int k = 0; c_lo + k < c_hi && k < kResRing; ++k) {
+              for (int k = 0; c_lo + k < c_hi && k < RR; ++k) {
                 const int q = res_g + k;
-                mbar_arrive_expect_tx(&my_res_full[q % kResRing], kEpiTile);
-                tma_load_2d_u32(res_base + (q % kResRing) * kEpiTile, &maps.res, &my_res_full[q % kResRing],
+                mbar_arrive_expect_tx(&my_res_full[q % RR], kEpiTile);
+                tma_load_2d_u32(res_base + (q % RR) * kEpiTile, &maps.res, &my_res_full[q % RR],
                                 (wn % p.n_splits) * bn + 32 * (c_lo + k), r0n);
               }
             }
@@ -744,8 +750,8 @@ __global__ void __launch_bounds__(gemm_threads(EPI), 1)
     // Residual tiles requested but never consumed (abort path) must land first.
     if constexpr (EPI == EPI_RESID_LN) {
       if (lane == 0 && !ok)
-        for (int k2 = 0; k2 < kResRing; ++k2)
-          wait_drain(&my_res_full[(res_g + k2) % kResRing], ((res_g + k2) / kResRing) & 1, kDrainLimitNs);
+        for (int k2 = 0; k2 < RR; ++k2)
+          wait_drain(&my_res_full[(res_g + k2) % RR], ((res_g + k2) / RR) & 1, kDrainLimitNs);
     }
   }
 
