@@ -509,6 +509,13 @@ def main() -> int:
         gather_tail_ms = max_over_ranks(step_ms[-1])
 
         extra = {}
+        if world > 1:
+            # Each rank's own ms per step, to see which one sets the max.
+            mine = torch.tensor([sum(step_ms) / args.steps, float(nb)], dtype=torch.float64, device=dev)
+            every = [torch.zeros_like(mine) for _ in range(world)]
+            dist.all_gather(every, mine)
+            extra["rank_ms_per_step"] = [round(float(t[0]), 4) for t in every]
+            extra["rank_sequences"] = [int(t[1]) for t in every]
         if gather is not None:
             # Compute alone (no push), and one step's latency with the push exposed.
             comp = timed_steps(lambda i: model.forward_gather(x_dev, mask_dev, outs[i % 2], 0), args.steps)
