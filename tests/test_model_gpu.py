@@ -169,6 +169,10 @@ def test_tiny_golden_cases(tt_lib, golden, name):
         # wide FFNs at d_model 256 (16 and 32 hidden chunks per row tile)
         (2, 200, 256, 8, 2048, 1, True, "prefix"),
         (2, 130, 256, 8, 4096, 1, True, None),
+        # fused FFN over more than one wave of row tiles: a ragged last tile
+        # (157 tiles), and the 8-GPU C5 slice (512 tiles, 3.46 waves)
+        (20, 1000, 256, 8, 1024, 1, True, "prefix"),
+        (64, 1024, 256, 8, 1024, 1, True, None),
         # head_dim 128 and 256; d_model 768 and 1024 (residual GEMMs in 256-column splits + row LayerNorm)
         (3, 130, 512, 4, 1024, 1, False, None),
         (2, 200, 1024, 4, 1024, 2, True, "prefix"),
