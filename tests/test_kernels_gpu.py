@@ -234,7 +234,7 @@ def test_gelu_matches_exact_erf(tt_lib):
 
 
 def test_exp2_polynomial_matches_exp2(tt_lib):
-    """The softmax's FMA-pipe exponential against exact 2^x: relative error <= 2.7e-6 (the fit's bound)
+    """The softmax's FMA-pipe exponential against exact 2^x: relative error <= 7.6e-5 (the fit's bound)
     plus FP32 rounding of the result, over [-125, 64); its FP16 form within one FP16 unit in the last
     place of the exact value (x < 15.99, below FP16's largest finite value 65504 = 2^15.9993)."""
     g = _gen(77)
@@ -248,7 +248,7 @@ def test_exp2_polynomial_matches_exp2(tt_lib):
     assert rc == _lib.TT_OK, _lib.last_error()
     exact = torch.exp2(x.double())
     rel = ((y32.double() - exact).abs() / exact).max().item()
-    assert rel <= 2.7e-6 + 2 ** -23, rel
+    assert rel <= 7.6e-5, rel
     sel = x < 15.99
     e = exact[sel]
     ulp = torch.exp2(torch.floor(torch.log2(e)) - 10).clamp_min(2.0 ** -24)

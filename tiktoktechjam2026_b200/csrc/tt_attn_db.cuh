@@ -120,7 +120,10 @@ struct AttnDbLayout {
 
 // Pairs of exponentials per 8 computed by polynomial on the FP32 pipe instead
 // of MUFU.
-constexpr int kDbExpFmaOf8 = 2;
+// (3 of 8 at head_dim 16/32, C5 attention 1.028 -> 1.000 ms per launch against
+// 2 of 8; 4 of 8 measured 1.053; at head_dim 64 2 and 3 of 8 measure the same.)
+template <int HD>
+constexpr int kDbExpFmaOf8 = HD <= 32 ? 3 : 2;
 
 
 template <int HD>
@@ -531,7 +534,7 @@ __global__ void __launch_bounds__(AttnDbLayout<HD>::THREADS, 1)
           uint32_t pk[16];
 #pragma unroll
           for (int e = 0; e < 16; ++e) {
-            if ((e & 7) < kDbExpFmaOf8) {
+            if ((e & 7) < kDbExpFmaOf8<HD>) {
               const uint64_t xx =
                   ffma2(f2_pack(__uint_as_float(sc[g][2 * e]), __uint_as_float(sc[g][2 * e + 1])), sl2x2, negm);
               const uint64_t pp = exp2_pair_fma(xx);

@@ -471,10 +471,11 @@ __device__ __forceinline__ uint32_t pack_half2(float lo, float hi) {
   return *reinterpret_cast<uint32_t*>(&h);
 }
 
-// 2^x for a pair of inputs on the FP32 pipe (no MUFU), rounded to an FP16
-// pair.  x = j + f with j = rint(x) (the 1.5*2^23 shifter) and |f| <= 1/2;
-// 2^f comes from a degree-4 polynomial fitted for relative error on
-// [-1/2, 1/2] (max 2.7e-6, far below FP16 rounding); 2^j is added into the
+// 2^x for a pair of inputs on the FP32 pipe (no MUFU).  x = j + f with
+// j = rint(x) (the 1.5*2^23 shifter) and |f| <= 1/2; 2^f comes from a degree-3
+// polynomial fitted for relative error on [-1/2, 1/2] by iteratively
+// reweighted least squares (max 7.5e-5, a sixth of FP16's half-unit rounding
+// error, which the probabilities receive next); 2^j is added into the
 // exponent field.  Inputs are clamped to >= -125 (2^-125 and smaller all round
 // to FP16 zero), and must stay below 64.
 __device__ __forceinline__ uint64_t exp2_pair_fma(uint64_t xx) {
@@ -482,28 +483,17 @@ __device__ __forceinline__ uint64_t exp2_pair_fma(uint64_t xx) {
   const uint64_t t = fadd2(x, f2_pack(12582912.f, 12582912.f));
   const uint64_t j = fadd2(t, f2_pack(-12582912.f, -12582912.f));
   const uint64_t f = ffma2(j, f2_pack(-1.f, -1.f), x);
-  uint64_t q = ffma2(f2_pack(9.570099413394928e-3f, 9.570099413394928e-3f), f,
-                     f2_pack(5.591785907745361e-2f, 5.591785907745361e-2f));
-  q = ffma2(q, f, f2_pack(2.40247443318367e-1f, 2.40247443318367e-1f));
-  q = ffma2(q, f, f2_pack(6.931217908859253e-1f, 6.931217908859253e-1f));
-  q = ffma2(q, f, f2_pack(9.999992847442627e-1f, 9.999992847442627e-1f));
+  uint64_t q = ffma2(f2_pack(5.517162383e-02f, 5.517162383e-02f), f, f2_pack(2.426111251e-01f, 2.426111251e-01f));
+  q = ffma2(q, f, f2_pack(6.932609677e-01f, 6.932609677e-01f));
+  q = ffma2(q, f, f2_pack(9.999280572e-01f, 9.999280572e-01f));
   const uint32_t r0 = static_cast<uint32_t>(q) + (static_cast<uint32_t>(t) << 23);
   const uint32_t r1 = static_cast<uint32_t>(q >> 32) + (static_cast<uint32_t>(t >> 32) << 23);
   return (static_cast<uint64_t>(r1) << 32) | r0;
 }
+// The same rounded to an FP16 pair.
 __device__ __forceinline__ uint32_t exp2_pair_fma_f16(uint64_t xx) {
-  const uint64_t x = f2_pack(fmaxf(f2_lo(xx), -125.f), fmaxf(f2_hi(xx), -125.f));
-  const uint64_t t = fadd2(x, f2_pack(12582912.f, 12582912.f));
-  const uint64_t j = fadd2(t, f2_pack(-12582912.f, -12582912.f));
-  const uint64_t f = ffma2(j, f2_pack(-1.f, -1.f), x);
-  uint64_t q = ffma2(f2_pack(9.570099413394928e-3f, 9.570099413394928e-3f), f,
-                     f2_pack(5.591785907745361e-2f, 5.591785907745361e-2f));
-  q = ffma2(q, f, f2_pack(2.40247443318367e-1f, 2.40247443318367e-1f));
-  q = ffma2(q, f, f2_pack(6.931217908859253e-1f, 6.931217908859253e-1f));
-  q = ffma2(q, f, f2_pack(9.999992847442627e-1f, 9.999992847442627e-1f));
-  const uint32_t r0 = static_cast<uint32_t>(q) + (static_cast<uint32_t>(t) << 23);
-  const uint32_t r1 = static_cast<uint32_t>(q >> 32) + (static_cast<uint32_t>(t >> 32) << 23);
-  return pack_half2(__uint_as_float(r0), __uint_as_float(r1));
+  const uint64_t y = exp2_pair_fma(xx);
+  return pack_half2(f2_lo(y), f2_hi(y));
 }
 
 // 16-byte asynchronous global -> shared copy (LDGSTS); src_bytes = 0 fills zeros
