@@ -529,15 +529,17 @@ __global__ void __launch_bounds__(AttnDbLayout<HD>::THREADS, 1)
         // comes from the P.[V | 1] MMA).  P.V of tile t-2, the last reader of
         // this buffer, finished before S_t was computed into it.
         const uint64_t negm = f2_pack(-m_use, -m_use);
+        // FMA-pipe pairs take y = saturate((s * scale - m + 26) / 128) from one fma per score.
+        const float y_scale = sl2 * kExp2YScale;
+        const float y_bias = fmaf(-m_use, kExp2YScale, kExp2YBias);
 #pragma unroll
         for (int g = 0; g < 2; ++g) {
           uint32_t pk[16];
 #pragma unroll
           for (int e = 0; e < 16; ++e) {
             if ((e & 7) < kDbExpFmaOf8<HD>) {
-              const uint64_t xx =
-                  ffma2(f2_pack(__uint_as_float(sc[g][2 * e]), __uint_as_float(sc[g][2 * e + 1])), sl2x2, negm);
-              const uint64_t pp = exp2_pair_fma(xx);
+              const uint64_t pp = exp2_pair_fma_y(f2_pack(fma_sat(__uint_as_float(sc[g][2 * e]), y_scale, y_bias),
+                                                          fma_sat(__uint_as_float(sc[g][2 * e + 1]), y_scale, y_bias)));
               pk[e] = pack_half2(f2_lo(pp), f2_hi(pp));
             } else {
               const uint64_t xx =

@@ -471,24 +471,46 @@ __device__ __forceinline__ uint32_t pack_half2(float lo, float hi) {
   return *reinterpret_cast<uint32_t*>(&h);
 }
 
-// 2^x for a pair of inputs on the FP32 pipe (no MUFU).  x = j + f with
-// j = rint(x) (the 1.5*2^23 shifter) and |f| <= 1/2; 2^f comes from a degree-3
-// polynomial fitted for relative error on [-1/2, 1/2] by iteratively
-// reweighted least squares (max 7.5e-5, a sixth of FP16's half-unit rounding
-// error, which the probabilities receive next); 2^j is added into the
-// exponent field.  Inputs are clamped to >= -125 (2^-125 and smaller all round
-// to FP16 zero), and must stay below 64.
-__device__ __forceinline__ uint64_t exp2_pair_fma(uint64_t xx) {
-  const uint64_t x = f2_pack(fmaxf(f2_lo(xx), -125.f), fmaxf(f2_hi(xx), -125.f));
-  const uint64_t t = fadd2(x, f2_pack(12582912.f, 12582912.f));
-  const uint64_t j = fadd2(t, f2_pack(-12582912.f, -12582912.f));
-  const uint64_t f = ffma2(j, f2_pack(-1.f, -1.f), x);
+// fma with the result clamped to [0, 1] (NaN -> 0).
+__device__ __forceinline__ float fma_sat(float a, float b, float c) {
+  float d;
+  asm("fma.rn.sat.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
+// Inputs of the FMA-pipe exponential: y = saturate((x + 26) / 128), which
+// clamps x to [-26, 102] in the same instruction that produces it (2^-26
+// and smaller all round to FP16 zero; -inf gives y = 0).  The attention
+// softmax folds its scale and row maximum into the same fma.
+constexpr float kExp2YScale = 1.0f / 128.0f;
+constexpr float kExp2YBias = 26.0f / 128.0f;
+
+// 2^x for a pair of inputs on the FP32 pipe (no MUFU), x given as
+// y = saturate((x + 26) / 128) (x = 128 y - 26; the rounding of y costs at
+// most 2^-19 in x for x <= 8, 2^-18 below 64).  x = j + f with j = rint(x)
+// (the 1.5*2^23 shifter, here with the -26 folded in) and |f| <= 1/2; 2^f
+// comes from a degree-3 polynomial fitted for relative error on [-1/2, 1/2]
+// by iteratively reweighted least squares (max 7.5e-5, a sixth of FP16's
+// half-unit rounding error, which the probabilities receive next); 2^j is
+// added into the exponent field.  The result is 2^max(x, -26); x must stay
+// below 64.
+__device__ __forceinline__ uint64_t exp2_pair_fma_y(uint64_t yy) {
+  constexpr float kShift = 12582912.f - 26.f;  // 1.5*2^23 - 26, exact in FP32
+  const uint64_t s128 = f2_pack(128.f, 128.f);
+  const uint64_t t = ffma2(yy, s128, f2_pack(kShift, kShift));               // 1.5*2^23 + j
+  const uint64_t u = ffma2(t, f2_pack(-1.f, -1.f), f2_pack(kShift, kShift));  // -26 - j, exact
+  const uint64_t f = ffma2(yy, s128, u);                                     // x - j
   uint64_t q = ffma2(f2_pack(5.517162383e-02f, 5.517162383e-02f), f, f2_pack(2.426111251e-01f, 2.426111251e-01f));
   q = ffma2(q, f, f2_pack(6.932609677e-01f, 6.932609677e-01f));
   q = ffma2(q, f, f2_pack(9.999280572e-01f, 9.999280572e-01f));
   const uint32_t r0 = static_cast<uint32_t>(q) + (static_cast<uint32_t>(t) << 23);
   const uint32_t r1 = static_cast<uint32_t>(q >> 32) + (static_cast<uint32_t>(t >> 32) << 23);
   return (static_cast<uint64_t>(r1) << 32) | r0;
+}
+// The same from x directly.
+__device__ __forceinline__ uint64_t exp2_pair_fma(uint64_t xx) {
+  return exp2_pair_fma_y(f2_pack(fma_sat(f2_lo(xx), kExp2YScale, kExp2YBias),
+                                 fma_sat(f2_hi(xx), kExp2YScale, kExp2YBias)));
 }
 // The same rounded to an FP16 pair.
 __device__ __forceinline__ uint32_t exp2_pair_fma_f16(uint64_t xx) {
